@@ -1,0 +1,335 @@
+#!/usr/bin/env python
+"""Benchmark of the ETHOS expert layer on B200 (one process per GPU).
+
+Metric: expert-layer tokens/s at the default size -- config 2:
+16384 tokens per GPU (batch 8 x seq 2048), d_model 1024, 262144 experts (two
+512-entry sub-key tables), d_latent 128, d_hidden 512, 8 heads, top_k 16, bf16
+forward with BatchNorm in eval mode, seeded synthetic N(0,1) inputs and
+N(0, 1/sqrt(fan_in)) parameters (no dataset is used).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ethos|reference]
+
+For N > 1 run it under torchrun (one rank per GPU): tokens shard across ranks
+with the parameters replicated and no collective in the forward (weak scaling,
+16384 tokens per GPU).  ``value`` = all ranks' tokens / max-over-ranks time.
+
+``--impl reference`` times the reference path's CPU implementation on the
+host cores (the vectorised fp32 restatement in oracle/ethos_oracle.py of
+SimplifiedHypernetMoE.forward, model.py:288-343; the reference's own code does
+not travel to the GPU box) on a bounded token sample.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG2 = dict(d_model=1024, num_experts=512 * 512, top_k=16, num_routing_heads=8, d_latent=128,
+            d_intermediate_hypernet=512, d_query=512)
+TOKENS = 16384
+METRIC = "expert-layer tokens/s (262K experts, k=16x8 heads)"
+UNIT = "tokens/s"
+L2_FLUSH_BYTES = 256 << 20
+
+# algorithmic work per token at config 2 (router + experts forward)
+#   MACs: q-proj 8*512*1024, scoring 8*2*512*256, x_proj 1024*512,
+#         expansion 128*128*512, dot + weighted sum 2*128*512, W_v 512*1024
+FLOP_PER_TOKEN = 2 * (8 * 512 * 1024 + 8 * 2 * 512 * 256 + 1024 * 512 + 128 * 128 * 512
+                      + 2 * 128 * 512 + 512 * 1024)
+# expert kernel alone (gather + expansion + GELU + dot + weighted sum)
+EXPERT_FLOP_PER_TOKEN = 2 * (128 * 128 * 512 + 2 * 128 * 512)
+EXPERT_BYTES_PER_TOKEN = 128 * 256 + 512 * 4 + 128 * 8 + 512 * 2  # rows, xp, ids+w, hacc
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm_gbs=float(p["hbm_gbs"]), bf16_tflops=float(p["bf16_tflops"]),
+                    bf16_tflops_sustained=float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                    source="measured")
+    except (OSError, KeyError, ValueError):
+        return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, source="fallback")
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the expert kernel from the committed ncu
+    summary (profiles/expert_fwd_config2.md, line 'dram_bytes_per_launch:')."""
+    path = os.path.join(ROOT, "profiles", "expert_fwd_config2.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed loop runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_layer(device, dtype=torch.bfloat16):
+    from ethos_b200 import EthosConfig, EthosExpertLayer
+    from ethos_b200.init import seeded_init_
+    layer = EthosExpertLayer(EthosConfig(**CFG2))
+    seeded_init_(layer, seed=0)
+    return layer.to(device=device, dtype=dtype).eval()
+
+
+def cpu_baseline(tokens_budget_s=12.0, sample_tokens=512):
+    """Times the oracle restatement of the reference forward (fp32, all host
+    threads) on repeated 512-token chunks of the config-2 workload for about
+    `tokens_budget_s` seconds."""
+    from ethos_b200 import EthosConfig, EthosExpertLayer
+    from ethos_b200.config import layer_dims
+    from ethos_b200.init import seeded_input, seeded_state_dict
+    from oracle import ethos_oracle as orc
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = EthosConfig(**CFG2)
+    sd = seeded_state_dict(EthosExpertLayer(cfg), seed=0)
+    p = orc.params_from_state_dict(sd, layer_dims(cfg), round_bf16=True)
+    x = seeded_input(sample_tokens, CFG2["d_model"], seed=0).to(torch.bfloat16).float()
+    done, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        orc.layer_forward(x[:64], p, CFG2["top_k"])  # warm-up
+        t0 = time.perf_counter()
+        while True:
+            orc.layer_forward(x, p, CFG2["top_k"])
+            done += sample_tokens
+            el = time.perf_counter() - t0
+            if el >= tokens_budget_s:
+                break
+    return dict(value=done / el, unit=UNIT, cores=cores, kind="port",
+                sample=f"{done} tokens in {sample_tokens}-token chunks of config 2 (oracle fp32 restatement "
+                       f"of model.py:288-343, torch CPU, {cores} threads), {el:.1f} s")
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    steps = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(tokens_budget_s=args.ref_seconds, sample_tokens=512)
+        if i >= args.warmup:
+            steps.append(r["value"])
+        cb = r
+    val = sum(steps) / len(steps)
+    line = dict(metric=METRIC, value=val, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=1000.0 * 512 / val, higher_is_better=True, scaling="weak", vs_baseline=None,
+                dtype="f32", data="synthetic", impl="reference",
+                config=dict(workload="config 2: ETHOS expert layer forward, 262144 experts, k=16 x 8 heads, "
+                                     "d_model 1024 (CPU sample)", tokens_per_sample=512),
+                cpu_baseline=dict(value=val, unit=UNIT, cores=cb["cores"], kind=cb["kind"], sample=cb["sample"]),
+                e2e=dict(value=val, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ethos", choices=["ethos", "reference"])
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=6.0)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from ethos_b200 import ops
+    from ethos_b200.init import seeded_input
+    layer = build_layer(dev)
+    T = args.tokens
+    x_host = seeded_input(T, CFG2["d_model"], seed=rank).to(torch.bfloat16).pin_memory()
+    x_dev = x_host.to(dev)
+    y_host = torch.empty((T, CFG2["d_model"]), dtype=torch.bfloat16).pin_memory()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    with torch.no_grad():
+        # ---------------- device-resident forward (value) -----------------
+        for _ in range(args.warmup):
+            layer(x_dev.view(1, T, -1))
+        torch.cuda.synchronize()
+        ops.check_device_error(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        sampler = ClockSampler(local)
+        sampler.start()
+        barrier()
+        torch.cuda.synchronize()
+        for s, e in ev:
+            flush.zero_()  # L2 flush between timed steps (outside the events)
+            s.record(stream)
+            layer(x_dev.view(1, T, -1))
+            e.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        clocks = sampler.stop()
+        ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
+        ms = max_over_ranks(ms)
+
+        # ---------------- expert kernel alone (roofline) ------------------
+        pw = layer._packed(dev)
+        out = ops.layer_forward(x_dev, pw, False, 1e-5, 0.1, save=True)
+        for _ in range(3):
+            ops.expert_forward(pw.latents, pw.w1, out["ids"], out["weights"], out["xp"], pw.dims)
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(max(5, min(args.steps, 20)))]
+        for s, e in kev:
+            flush.zero_()
+            s.record(stream)
+            ops.expert_forward(pw.latents, pw.w1, out["ids"], out["weights"], out["xp"], pw.dims)
+            e.record(stream)
+        torch.cuda.synchronize()
+        ops.check_device_error(dev)
+        kms = sum(s.elapsed_time(e) for s, e in kev) / len(kev)
+        kms = max_over_ranks(kms)
+
+        # ---------------- end to end through the public API ---------------
+        e2e_steps = max(3, min(args.steps, 20))
+        for _ in range(2):
+            xd = x_host.to(dev, non_blocking=True)
+            y_host.copy_(layer(xd.view(1, T, -1)).view(T, -1), non_blocking=True)
+        torch.cuda.synchronize()
+        eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(e2e_steps)]
+        barrier()
+        for s, e in eev:
+            flush.zero_()
+            s.record(stream)
+            xd = x_host.to(dev, non_blocking=True)
+            y = layer(xd.view(1, T, -1))
+            y_host.copy_(y.view(T, -1), non_blocking=True)
+            e.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = max_over_ranks(sum(s.elapsed_time(e) for s, e in eev) / len(eev))
+
+    peaks = load_peaks()
+    total_tokens = T * world
+    value = total_tokens / (ms / 1e3)
+    k_achieved = EXPERT_FLOP_PER_TOKEN * T / (kms / 1e3) / 1e12
+    traffic = load_traffic()
+    line = dict(
+        metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+        ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+        data="synthetic",
+        config=dict(workload="config 2: ETHOS expert layer forward (router + experts), 262144 experts, "
+                             "k=16 x 8 heads, d_model 1024, d_latent 128, d_hidden 512, BN eval",
+                    tokens_per_gpu=T, global_batch=total_tokens, parallelism=f"dp{world} (token shards)",
+                    l2="flushed between timed steps (256 MiB write)"),
+        layer_tflops=FLOP_PER_TOKEN * T / (ms / 1e3) / 1e12,
+        expert_kernel_ms=kms,
+        roofline=dict(bound="tensor", kernel="k_expert_fwd", achieved=k_achieved, peak=peaks["bf16_tflops"],
+                      unit="TFLOP/s", frac=k_achieved / peaks["bf16_tflops"],
+                      traffic=traffic, peak_source=peaks["source"] + " (bf16 burst)",
+                      algorithmic_flop_per_token=EXPERT_FLOP_PER_TOKEN,
+                      algorithmic_bytes_per_token=EXPERT_BYTES_PER_TOKEN,
+                      hbm_gbs=EXPERT_BYTES_PER_TOKEN * T / (kms / 1e3) / 1e9),
+        e2e=dict(value=total_tokens / (ems / 1e3), unit=UNIT, h2d_bytes_per_step=x_host.numel() * 2,
+                 d2h_bytes_per_step=y_host.numel() * 2),
+        gpu_launches=5 * args.steps,
+        clocks=clocks,
+    )
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

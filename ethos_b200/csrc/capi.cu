@@ -1,0 +1,478 @@
+// C ABI of the ETHOS expert layer (declared in include/ethos_b200.h).
+//
+// Host-side orchestration only: argument checks, workspace partitioning,
+// TMA tensor-map encoding and kernel launches on the caller's stream.  No
+// device memory is allocated here.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "ethos_b200.h"
+#include "expert.cuh"
+#include "gemm.cuh"
+#include "router.cuh"
+
+using namespace ethos;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+
+// ------------------------------------------------------------ device cache --
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0;
+  bool attrs_set = false;
+};
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ETHOS_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sm_count == 0) {
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return ETHOS_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return ETHOS_ERR_CUDA;
+    d.sm_count = sms;
+    d.major = major;
+  }
+  if (d.major != 10) return ETHOS_ERR_NO_DEVICE;
+  if (!d.attrs_set) {
+    bool ok = true;
+    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiStoreBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GEMM_SMEM_BYTES) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiStoreF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GEMM_SMEM_BYTES) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiProj>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GEMM_SMEM_BYTES) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_score_topk<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTER_SMEM_BYTES) ==
+          cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_score_topk<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTER_SMEM_BYTES) ==
+          cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_score_topk<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTER_SMEM_BYTES) ==
+          cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_expert_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, EX_SMEM_BYTES) ==
+          cudaSuccess;
+    if (!ok) return ETHOS_ERR_CUDA;
+    d.attrs_set = true;
+  }
+  *out = &d;
+  return ETHOS_OK;
+}
+
+// ------------------------------------------------------------- tensor maps --
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] read in boxes of 64 columns x box_rows
+// rows with the 128-byte swizzle that the UMMA descriptors expect.
+int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return ETHOS_ERR_TENSOR_MAP;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || (cols * 2) % 16 != 0) return ETHOS_ERR_ALIGNMENT;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ETHOS_OK : ETHOS_ERR_TENSOR_MAP;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ETHOS_OK : ETHOS_ERR_CUDA;
+}
+
+template <class Epi>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int* err,
+                cudaStream_t stream, const DeviceInfo& dev) {
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / GEMM_BN);
+  const int grid = tiles < dev.sm_count ? tiles : dev.sm_count;
+  if (grid <= 0) return ETHOS_OK;
+  k_gemm_bf16_tn<Epi><<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, stream>>>(ta, tb, M, N, K, epi, err);
+  return launch_status();
+}
+
+// ------------------------------------------------------- workspace layout --
+struct Carve {
+  char* base;
+  size_t off = 0;
+  size_t cap;
+  template <class T>
+  T* take(size_t count) {
+    off = (off + 255) & ~static_cast<size_t>(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+struct FwdScratch {
+  __nv_bfloat16* qs;
+  float4* colp;
+  float* xp;
+  __nv_bfloat16* hacc;
+  float* qpre;
+  float* save_bn;
+  float* bn_part;
+  int slabs;
+};
+
+void carve_forward(Carve& c, const ethos_dims& d, int bn_training, bool need_xp, bool need_hacc, bool need_qpre,
+                   bool need_bn, FwdScratch* s) {
+  const int64_t T = d.tokens, HQ = d.num_heads * d.d_query;
+  s->qs = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.d_query));
+  s->colp = c.take<float4>(static_cast<size_t>(HQ));
+  s->xp = need_xp ? c.take<float>(static_cast<size_t>(T * d.d_hidden)) : nullptr;
+  s->hacc = need_hacc ? c.take<__nv_bfloat16>(static_cast<size_t>(T * d.d_hidden)) : nullptr;
+  s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
+  if (bn_training) {
+    s->qpre = need_qpre ? c.take<float>(static_cast<size_t>(T * HQ)) : nullptr;
+    s->save_bn = need_bn ? c.take<float>(static_cast<size_t>(2 * HQ)) : nullptr;
+    s->bn_part = c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2);
+  } else {
+    s->qpre = nullptr;
+    s->save_bn = nullptr;
+    s->bn_part = nullptr;
+  }
+}
+
+int check_dims_impl(const ethos_dims* d) {
+  if (d == nullptr) return ETHOS_ERR_INVALID_ARG;
+  if (d->tokens < 1 || d->tokens > (int64_t(1) << 24)) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d->d_latent != EX_DL || d->d_hidden != EX_DH) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  const int64_t R = d->num_heads * d->top_k;
+  if (d->num_heads < 1 || R > EX_ROWS || R % 4 != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d->top_k != 4 && d->top_k != 8 && d->top_k != 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d->num_sub_keys * d->num_sub_keys != d->num_experts) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d->num_sub_keys % 32 != 0 || d->num_sub_keys > 512 || d->num_sub_keys < d->top_k)
+    return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d->d_query % 64 != 0 || d->d_query < 64) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d->d_model % 256 != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if ((d->num_heads * d->d_query + d->d_hidden) % 256 != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if ((d->num_heads * d->d_query) % 256 != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  return ETHOS_OK;
+}
+
+template <int TOPK>
+int launch_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g, int32_t* ids, float* w,
+                 int* err, cudaStream_t stream, const DeviceInfo& dev) {
+  const int items = g.H * ((g.T + 127) / 128);
+  const int grid = items < dev.sm_count ? items : dev.sm_count;
+  k_score_topk<TOPK><<<grid, ROUTER_THREADS, ROUTER_SMEM_BYTES, stream>>>(ta, tb, g, ids, w, err);
+  return launch_status();
+}
+
+int run_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g, int top_k, int32_t* ids,
+              float* w, int* err, cudaStream_t stream, const DeviceInfo& dev) {
+  switch (top_k) {
+    case 4: return launch_score<4>(ta, tb, g, ids, w, err, stream, dev);
+    case 8: return launch_score<8>(ta, tb, g, ids, w, err, stream, dev);
+    case 16: return launch_score<16>(ta, tb, g, ids, w, err, stream, dev);
+    default: return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  }
+}
+
+// Router part shared by ethos_layer_forward and ethos_router_forward:
+// projection GEMM (queries, plus x_proj when with_xp), BatchNorm, scoring and
+// top-k.
+int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn, float bn_eps, float bn_momentum,
+                int bn_training, const void* key_cat, int32_t* ids, float* weights, bool with_xp, float* xp_out,
+                const FwdScratch& s, float* qpre, float* save_bn, int* err, cudaStream_t stream,
+                const DeviceInfo& dev) {
+  const int T = static_cast<int>(d.tokens);
+  const int HQ = static_cast<int>(d.num_heads * d.d_query);
+  const int dq = static_cast<int>(d.d_query);
+  const int dh = static_cast<int>(d.d_hidden);
+  const int ncat = with_xp ? HQ + dh : HQ;
+  CUtensorMap tm_x, tm_w, tm_q, tm_k;
+  int st;
+  if ((st = make_tmap_bf16(&tm_x, x, T, d.d_model, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_w, w_cat, ncat, d.d_model, 256)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_q, s.qs, static_cast<int64_t>(d.num_heads) * 2 * T, dq, 128)) != ETHOS_OK)
+    return st;
+  const int box_keys = d.num_sub_keys < 256 ? static_cast<int>(d.num_sub_keys) : 256;
+  if ((st = make_tmap_bf16(&tm_k, key_cat, 2 * d.num_sub_keys, dq, box_keys)) != ETHOS_OK) return st;
+
+  const int cb = 256;
+  if (!bn_training) {
+    k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(bn, HQ, bn_eps, s.colp);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  EpiProj epi;
+  epi.M = T;
+  epi.HQ = HQ;
+  epi.dq = dq;
+  epi.dh = dh;
+  epi.mode = bn_training ? 1 : 0;
+  epi.bias = bn;
+  epi.colp = s.colp;
+  epi.qs = s.qs;
+  epi.qpre = qpre;
+  epi.xp = xp_out;
+  if ((st = launch_gemm(tm_x, tm_w, T, ncat, static_cast<int>(d.d_model), epi, err, stream, dev)) != ETHOS_OK)
+    return st;
+  if (bn_training) {
+    dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+    k_bn_partial<<<grid_p, cb, 0, stream>>>(qpre, T, HQ, s.bn_part);
+    k_bn_finalize<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(qpre, s.bn_part, T, HQ, s.slabs, bn + HQ, bn + 2 * HQ,
+                                                         bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, save_bn,
+                                                         s.colp);
+    const int64_t groups = static_cast<int64_t>(T) * (HQ / 8);
+    k_bn_apply<<<static_cast<unsigned>((groups + cb - 1) / cb), cb, 0, stream>>>(qpre, s.colp, T,
+                                                                                static_cast<int>(d.num_heads), dq,
+                                                                                s.qs);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  RouterGeom g;
+  g.T = T;
+  g.H = static_cast<int>(d.num_heads);
+  g.K = static_cast<int>(d.num_sub_keys);
+  g.KA = dq;
+  g.a_stride_h = 2 * T;
+  g.a_stride_p = T;
+  g.a_col_p = 0;
+  return run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, err, stream, dev);
+}
+
+}  // namespace
+
+// =================================================================== ABI ==
+extern "C" {
+
+int ethos_abi_version(void) { return kAbiVersion; }
+
+const char* ethos_status_string(int status) {
+  switch (status) {
+    case ETHOS_OK: return "ok";
+    case ETHOS_ERR_INVALID_ARG: return "invalid argument";
+    case ETHOS_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+    case ETHOS_ERR_ALIGNMENT: return "pointer or row pitch not 16-byte aligned";
+    case ETHOS_ERR_WORKSPACE: return "workspace too small";
+    case ETHOS_ERR_CUDA: return "CUDA runtime error";
+    case ETHOS_ERR_TENSOR_MAP: return "tensor map encoding failed";
+    case ETHOS_ERR_NO_DEVICE: return "no sm_100 device is current";
+    case ETHOS_ERR_ID_OUT_OF_RANGE: return "expert id out of range (device)";
+    default:
+      if (status >= ETHOS_ERR_TIMEOUT_BASE) return "bounded device wait timed out";
+      return "unknown status";
+  }
+}
+
+int ethos_read_device_error(int* dev_err, int* host_code, int reset, void* stream) {
+  if (dev_err == nullptr || host_code == nullptr) return ETHOS_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  if (cudaMemcpyAsync(&v, dev_err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return ETHOS_ERR_CUDA;
+  *host_code = v;
+  if (reset && v != 0) {
+    if (cudaMemsetAsync(dev_err, 0, sizeof(int), s) != cudaSuccess) return ETHOS_ERR_CUDA;
+  }
+  return ETHOS_OK;
+}
+
+int ethos_check_dims(const ethos_dims* dims) { return check_dims_impl(dims); }
+
+size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training) {
+  if (check_dims_impl(dims) != ETHOS_OK) return 0;
+  Carve c{nullptr, 0, 0};
+  FwdScratch s;
+  carve_forward(c, *dims, bn_training, true, true, true, true, &s);
+  return c.off + 256;
+}
+
+int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
+                        float bn_momentum, int bn_training, const void* key_cat, const void* latents,
+                        const void* w1, const void* wv, void* y, int32_t* ids, float* weights, float* save_xp,
+                        void* save_hacc, float* save_dot, float* save_qpre, float* save_bn, void* workspace,
+                        size_t workspace_bytes, int* dev_err, void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !y || !ids || !weights || !workspace || !dev_err)
+    return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(latents) ||
+      !aligned16(w1) || !aligned16(wv) || !aligned16(y) || !aligned16(ids) || !aligned16(weights) ||
+      !aligned16(workspace) || (save_xp && !aligned16(save_xp)) || (save_hacc && !aligned16(save_hacc)) ||
+      (save_qpre && !aligned16(save_qpre)))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training)) return ETHOS_ERR_WORKSPACE;
+  const ethos_dims& d = *dims;
+  cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  FwdScratch s;
+  carve_forward(c, d, bn_training, save_xp == nullptr, save_hacc == nullptr, save_qpre == nullptr,
+                save_bn == nullptr, &s);
+  float* xp = save_xp ? save_xp : s.xp;
+  __nv_bfloat16* hacc = save_hacc ? static_cast<__nv_bfloat16*>(save_hacc) : s.hacc;
+  float* qpre = save_qpre ? save_qpre : s.qpre;
+  float* sbn = save_bn ? save_bn : s.save_bn;
+  const int T = static_cast<int>(d.tokens);
+
+  if ((st = router_core(d, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, true, xp, s, qpre,
+                        sbn, dev_err, stream_, *dev)) != ETHOS_OK)
+    return st;
+
+  // reordered experts
+  CUtensorMap tm_w1, tm_h, tm_v;
+  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_h, hacc, T, EX_DH, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_v, wv, d.d_model, EX_DH, 256)) != ETHOS_OK) return st;
+  ExpertFwdArgs ea;
+  ea.latents = static_cast<const __nv_bfloat16*>(latents);
+  ea.ids = ids;
+  ea.w = weights;
+  ea.xp = xp;
+  ea.hacc = hacc;
+  ea.save_dot = save_dot;
+  ea.T = T;
+  ea.R = static_cast<int>(d.num_heads * d.top_k);
+  ea.N = static_cast<int>(d.num_experts);
+  const int grid = T < dev->sm_count ? T : dev->sm_count;
+  k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, stream_>>>(tm_w1, ea, dev_err);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+
+  // y = hacc @ W_v / H   (model.py:332-341)
+  EpiStoreBF16 ey;
+  ey.out = static_cast<__nv_bfloat16*>(y);
+  ey.ldo = d.d_model;
+  ey.M = T;
+  ey.scale = 1.0f / static_cast<float>(d.num_heads);
+  return launch_gemm(tm_h, tm_v, T, static_cast<int>(d.d_model), EX_DH, ey, dev_err, stream_, *dev);
+}
+
+int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
+                         float bn_momentum, int bn_training, const void* key_cat, int32_t* ids, float* weights,
+                         float* save_qpre, float* save_bn, void* workspace, size_t workspace_bytes, int* dev_err,
+                         void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!x || !w_cat || !bn || !key_cat || !ids || !weights || !workspace || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(ids) ||
+      !aligned16(weights) || !aligned16(workspace) || (save_qpre && !aligned16(save_qpre)))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training)) return ETHOS_ERR_WORKSPACE;
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  FwdScratch s;
+  carve_forward(c, *dims, bn_training, false, false, save_qpre == nullptr, save_bn == nullptr, &s);
+  float* qpre = save_qpre ? save_qpre : s.qpre;
+  float* sbn = save_bn ? save_bn : s.save_bn;
+  return router_core(*dims, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, false, nullptr,
+                     s, qpre, sbn, dev_err, static_cast<cudaStream_t>(stream), *dev);
+}
+
+int ethos_expert_forward(const ethos_dims* dims, const void* latents, const void* w1, const int32_t* ids,
+                         const float* weights, const float* xp, void* hacc, float* dot, int* dev_err,
+                         void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!latents || !w1 || !ids || !weights || !xp || !hacc || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(latents) || !aligned16(w1) || !aligned16(ids) || !aligned16(weights) || !aligned16(xp) ||
+      !aligned16(hacc))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  CUtensorMap tm_w1;
+  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
+  ExpertFwdArgs ea;
+  ea.latents = static_cast<const __nv_bfloat16*>(latents);
+  ea.ids = ids;
+  ea.w = weights;
+  ea.xp = xp;
+  ea.hacc = static_cast<__nv_bfloat16*>(hacc);
+  ea.save_dot = dot;
+  ea.T = static_cast<int>(dims->tokens);
+  ea.R = static_cast<int>(dims->num_heads * dims->top_k);
+  ea.N = static_cast<int>(dims->num_experts);
+  const int grid = ea.T < dev->sm_count ? ea.T : dev->sm_count;
+  k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tm_w1, ea, dev_err);
+  return launch_status();
+}
+
+int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* keys, int32_t* ids, float* weights,
+                           int* dev_err, void* stream) {
+  if (dims == nullptr || !q || !keys || !ids || !weights || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  const ethos_dims& d = *dims;
+  if (d.tokens < 1 || d.num_heads < 1) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d.top_k != 4 && d.top_k != 8 && d.top_k != 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (d.num_sub_keys % 32 != 0 || d.num_sub_keys > 512 || d.num_sub_keys < d.top_k)
+    return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if ((d.d_query / 2) % 64 != 0 || d.d_query % 2 != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(q) || !aligned16(keys) || !aligned16(ids) || !aligned16(weights)) return ETHOS_ERR_ALIGNMENT;
+  int st;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  const int T = static_cast<int>(d.tokens);
+  const int half = static_cast<int>(d.d_query / 2);
+  CUtensorMap tm_q, tm_k;
+  if ((st = make_tmap_bf16(&tm_q, q, d.num_heads * T, d.d_query, 128)) != ETHOS_OK) return st;
+  const int box_keys = d.num_sub_keys < 256 ? static_cast<int>(d.num_sub_keys) : 256;
+  if ((st = make_tmap_bf16(&tm_k, keys, 2 * d.num_sub_keys, half, box_keys)) != ETHOS_OK) return st;
+  RouterGeom g;
+  g.T = T;
+  g.H = static_cast<int>(d.num_heads);
+  g.K = static_cast<int>(d.num_sub_keys);
+  g.KA = half;
+  g.a_stride_h = T;
+  g.a_stride_p = 0;
+  g.a_col_p = half;
+  return run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, dev_err,
+                   static_cast<cudaStream_t>(stream), *dev);
+}
+
+int ethos_gemm_bf16(const void* a, const void* b, void* dptr, int64_t M, int64_t N, int64_t K, float scale,
+                    int out_dtype, int* dev_err, void* stream) {
+  if (!a || !b || !dptr || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (M < 1 || N % GEMM_BN != 0 || N < GEMM_BN || K % GEMM_BK != 0 || K < GEMM_BK || M > (int64_t(1) << 30))
+    return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(dptr)) return ETHOS_ERR_ALIGNMENT;
+  int st;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  CUtensorMap ta, tb;
+  if ((st = make_tmap_bf16(&ta, a, M, K, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tb, b, N, K, 256)) != ETHOS_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (out_dtype == 1) {
+    EpiStoreBF16 e;
+    e.out = static_cast<__nv_bfloat16*>(dptr);
+    e.ldo = N;
+    e.M = static_cast<int>(M);
+    e.scale = scale;
+    return launch_gemm(ta, tb, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), e, dev_err, s, *dev);
+  }
+  EpiStoreF32 e;
+  e.out = static_cast<float*>(dptr);
+  e.ldo = N;
+  e.M = static_cast<int>(M);
+  e.scale = scale;
+  e.accumulate = 0;
+  return launch_gemm(ta, tb, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), e, dev_err, s, *dev);
+}
+
+}  // extern "C"

@@ -1,0 +1,184 @@
+"""Torch-tensor wrappers over the C ABI (device pointers in, device pointers out).
+
+PyTorch only provides device memory and the current stream here; every
+computation runs in ``libethos_b200.so``.  All tensors must already live on a
+CUDA device: there is no CPU path.
+"""
+
+import ctypes
+
+import torch
+
+from ._lib import EthosDims, EthosError, check, lib
+
+__all__ = [
+    "make_dims", "gemm_bf16", "product_key_topk", "expert_forward", "router_forward", "layer_forward",
+    "device_error_word", "check_device_error", "PackedWeights",
+]
+
+_ERR_WORDS = {}
+
+
+def _vp(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(t, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor: the ETHOS B200 layer has no CPU path")
+
+
+def device_error_word(device):
+    """The per-device int32 word where kernels record bounds/timeout errors."""
+    device = torch.device(device)
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    w = _ERR_WORDS.get(key)
+    if w is None:
+        w = torch.zeros(4, dtype=torch.int32, device=device)
+        _ERR_WORDS[key] = w
+    return w
+
+
+def check_device_error(device, reset=True):
+    """Synchronises the current stream and raises EthosError if a kernel set
+    the device error word (expert id out of range, bounded wait timeout)."""
+    w = device_error_word(device)
+    code = ctypes.c_int(0)
+    check(lib().ethos_read_device_error(_vp(w), ctypes.byref(code), 1 if reset else 0,
+                                        _stream(w.device)), "ethos_read_device_error")
+    if code.value != 0:
+        raise EthosError(code.value, "device error word")
+
+
+def make_dims(tokens, d):
+    return EthosDims(tokens=int(tokens), d_model=d["d_model"], num_experts=d["num_experts"],
+                     num_sub_keys=d["num_sub_keys"], d_query=d["d_query"], d_latent=d["d_latent"],
+                     d_hidden=d["d_hidden"], num_heads=d["num_heads"], top_k=d["top_k"])
+
+
+def gemm_bf16(a, b, scale=1.0, out_dtype=torch.float32):
+    """``a [M, K] @ b[N, K]^T * scale`` on the tcgen05 GEMM (bf16 in, fp32 acc)."""
+    _require_cuda(a, "a")
+    _require_cuda(b, "b")
+    a = a.contiguous()
+    b = b.contiguous()
+    M, K = a.shape
+    N = b.shape[0]
+    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    err = device_error_word(a.device)
+    check(lib().ethos_gemm_bf16(_vp(a), _vp(b), _vp(out), M, N, K, float(scale),
+                                1 if out_dtype == torch.bfloat16 else 0, _vp(err), _stream(a.device)),
+          "ethos_gemm_bf16")
+    return out
+
+
+def product_key_topk(q, keys, top_k):
+    """Product-key selection from normalised queries.
+
+    ``q`` bf16 ``[H, T, dq]``, ``keys`` bf16 ``[2, K, dq/2]``.  Returns
+    ``(weights fp32 [T, H, k], ids int32 [T, H, k])`` (model.py:217-245)."""
+    _require_cuda(q, "q")
+    H, T, dq = q.shape
+    K = keys.shape[1]
+    dims = EthosDims(tokens=T, d_model=0, num_experts=K * K, num_sub_keys=K, d_query=dq,
+                     d_latent=0, d_hidden=0, num_heads=H, top_k=int(top_k))
+    ids = torch.empty((T, H, top_k), dtype=torch.int32, device=q.device)
+    w = torch.empty((T, H, top_k), dtype=torch.float32, device=q.device)
+    err = device_error_word(q.device)
+    check(lib().ethos_product_key_topk(ctypes.byref(dims), _vp(q.contiguous()), _vp(keys.contiguous()),
+                                       _vp(ids), _vp(w), _vp(err), _stream(q.device)),
+          "ethos_product_key_topk")
+    return w, ids
+
+
+def expert_forward(latents, w1, ids, weights, xp, dims, save_dot=False):
+    """Experts alone on given routing decisions: returns ``(hacc bf16 [T, dh],
+    dot fp32 [T, H*k] or None)``.  ``ids`` int32 / ``weights`` fp32 ``[T, H, k]``."""
+    _require_cuda(ids, "ids")
+    T = ids.shape[0]
+    ed = make_dims(T, dims)
+    hacc = torch.empty((T, dims["d_hidden"]), dtype=torch.bfloat16, device=ids.device)
+    dot = (torch.empty((T, dims["num_heads"] * dims["top_k"]), dtype=torch.float32, device=ids.device)
+           if save_dot else None)
+    err = device_error_word(ids.device)
+    check(lib().ethos_expert_forward(ctypes.byref(ed), _vp(latents), _vp(w1), _vp(ids.contiguous()),
+                                     _vp(weights.contiguous()), _vp(xp.contiguous()), _vp(hacc), _vp(dot),
+                                     _vp(err), _stream(ids.device)), "ethos_expert_forward")
+    return hacc, dot
+
+
+class PackedWeights:
+    """Kernel-layout copies of the layer parameters (derived caches, never
+    state): bf16 ``w_cat [H*dq + dh, d]`` (query projections stacked, then
+    ``W_u^T``), ``key_cat [2, K, dq]`` (each sub-key row written twice for the
+    split-bf16 scoring), ``latents [N, dl]``, ``w1 [dh, dl]``, ``wv [d, dh]``,
+    and the fp32 ``bn [5, H*dq]`` (bias, gamma, beta, running mean, running
+    var)."""
+
+    __slots__ = ("w_cat", "key_cat", "latents", "w1", "wv", "bn", "dims")
+
+    def __init__(self, w_cat, key_cat, latents, w1, wv, bn, dims):
+        self.w_cat, self.key_cat, self.latents = w_cat, key_cat, latents
+        self.w1, self.wv, self.bn, self.dims = w1, wv, bn, dims
+
+
+def router_forward(x2d, pw, bn_training, eps, momentum, save_qpre=None, save_bn=None):
+    """``(weights fp32 [T,H,k], ids int32 [T,H,k])`` for bf16 ``x2d [T, d]``."""
+    _require_cuda(x2d, "x")
+    d = pw.dims
+    T = x2d.shape[0]
+    dims = make_dims(T, d)
+    L = lib()
+    ws_bytes = L.ethos_forward_workspace_size(ctypes.byref(dims), 1 if bn_training else 0)
+    if ws_bytes == 0:
+        check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2d.device)
+    ids = torch.empty((T, d["num_heads"], d["top_k"]), dtype=torch.int32, device=x2d.device)
+    w = torch.empty((T, d["num_heads"], d["top_k"]), dtype=torch.float32, device=x2d.device)
+    err = device_error_word(x2d.device)
+    check(L.ethos_router_forward(ctypes.byref(dims), _vp(x2d), _vp(pw.w_cat), _vp(pw.bn), float(eps),
+                                 float(momentum), 1 if bn_training else 0, _vp(pw.key_cat), _vp(ids), _vp(w),
+                                 _vp(save_qpre), _vp(save_bn), _vp(ws), ws_bytes, _vp(err),
+                                 _stream(x2d.device)), "ethos_router_forward")
+    return w, ids
+
+
+def layer_forward(x2d, pw, bn_training, eps, momentum, save=False):
+    """Router + experts.  Returns a dict with ``y`` (bf16 [T, d]), ``ids``,
+    ``weights`` and, when ``save``, the tensors the backward pass needs."""
+    _require_cuda(x2d, "x")
+    d = pw.dims
+    T = x2d.shape[0]
+    dev = x2d.device
+    dims = make_dims(T, d)
+    L = lib()
+    ws_bytes = L.ethos_forward_workspace_size(ctypes.byref(dims), 1 if bn_training else 0)
+    if ws_bytes == 0:
+        check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    H, k, dh, HQ = d["num_heads"], d["top_k"], d["d_hidden"], d["num_heads"] * d["d_query"]
+    out = dict(
+        y=torch.empty((T, d["d_model"]), dtype=torch.bfloat16, device=dev),
+        ids=torch.empty((T, H, k), dtype=torch.int32, device=dev),
+        weights=torch.empty((T, H, k), dtype=torch.float32, device=dev),
+    )
+    if save:
+        out["xp"] = torch.empty((T, dh), dtype=torch.float32, device=dev)
+        out["hacc"] = torch.empty((T, dh), dtype=torch.bfloat16, device=dev)
+        out["dot"] = torch.empty((T, H * k), dtype=torch.float32, device=dev)
+        if bn_training:
+            out["qpre"] = torch.empty((T, HQ), dtype=torch.float32, device=dev)
+            out["bn_stats"] = torch.empty((2, HQ), dtype=torch.float32, device=dev)
+    g = out.get
+    err = device_error_word(dev)
+    check(L.ethos_layer_forward(ctypes.byref(dims), _vp(x2d), _vp(pw.w_cat), _vp(pw.bn), float(eps),
+                                float(momentum), 1 if bn_training else 0, _vp(pw.key_cat), _vp(pw.latents),
+                                _vp(pw.w1), _vp(pw.wv), _vp(out["y"]), _vp(out["ids"]), _vp(out["weights"]),
+                                _vp(g("xp")), _vp(g("hacc")), _vp(g("dot")), _vp(g("qpre")),
+                                _vp(g("bn_stats")), _vp(ws), ws_bytes, _vp(err), _stream(dev)),
+          "ethos_layer_forward")
+    return out

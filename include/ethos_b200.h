@@ -1,0 +1,156 @@
+/*
+ * ethos_b200.h -- C ABI of the B200-native ETHOS expert layer.
+ *
+ * The reference (wrmedford/ETHOS) is pure Python: its expert layer is the
+ * nn.Module pair SimplifiedHypernetMoE (model.py:267-343) /
+ * FusedLowRankMoE_Reordered (kernels.py:123-221) with ProductKeyRouter
+ * (model.py:182-254), and its only kernel is the Triton moe_reorder_kernel
+ * (kernels.py:18-120) launched from kernels.py:179-215.  The entry points below
+ * replace those calls; each cites the reference code it stands in for.  The
+ * Python host (ethos_b200/_lib.py) binds them with ctypes.
+ *
+ * Conventions
+ *  - All tensor arguments are raw DEVICE pointers to contiguous row-major
+ *    buffers owned by the caller (the library never allocates or frees device
+ *    memory); sizes are int64; `stream` is a cudaStream_t (NULL = legacy).
+ *  - bf16 buffers hold IEEE bfloat16 values (2 bytes each).
+ *  - Every entry point returns an ethos status (0 = OK) and never throws.
+ *    Device-side faults of the data (an expert id out of range) and bounded
+ *    wait timeouts are recorded in the caller-provided device error word
+ *    `dev_err` (an int32, zero-initialised by the caller) and read back with
+ *    ethos_read_device_error().
+ *  - Calls are stateless and re-entrant; the only process-wide state is a
+ *    lazily initialised per-device attribute cache.
+ *  - Entry points only launch work on `stream`; they do not synchronise.
+ */
+#ifndef ETHOS_B200_H
+#define ETHOS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------- status -- */
+#define ETHOS_OK 0
+#define ETHOS_ERR_INVALID_ARG 1       /* null pointer, negative size          */
+#define ETHOS_ERR_UNSUPPORTED_SHAPE 2 /* dims outside the compiled kernels    */
+#define ETHOS_ERR_ALIGNMENT 3         /* pointer not 16-byte aligned          */
+#define ETHOS_ERR_WORKSPACE 4         /* workspace smaller than required      */
+#define ETHOS_ERR_CUDA 5              /* a CUDA runtime call failed           */
+#define ETHOS_ERR_TENSOR_MAP 6        /* cuTensorMapEncodeTiled failed        */
+#define ETHOS_ERR_NO_DEVICE 7         /* no sm_100 device current             */
+/* device-side codes (reported through dev_err) */
+#define ETHOS_ERR_ID_OUT_OF_RANGE 16  /* an expert id outside [0, N)          */
+#define ETHOS_ERR_TIMEOUT_BASE 1000   /* + site: a bounded wait gave up       */
+
+/* Layer dimensions (names follow the reference config, train.py:33-48). */
+typedef struct ethos_dims {
+  int64_t tokens;       /* T = batch * seq                                    */
+  int64_t d_model;      /* d                                                   */
+  int64_t num_experts;  /* N = K * K                                           */
+  int64_t num_sub_keys; /* K                                                   */
+  int64_t d_query;      /* dq (split into two halves of dq/2)                  */
+  int64_t d_latent;     /* dl                                                  */
+  int64_t d_hidden;     /* dh = d_intermediate_hypernet                        */
+  int64_t num_heads;    /* H = num_routing_heads                               */
+  int64_t top_k;        /* k                                                   */
+} ethos_dims;
+
+int ethos_abi_version(void);
+const char* ethos_status_string(int status);
+
+/* Copies the device error word to *host_code (synchronising `stream`) and,
+ * when reset != 0, clears it. */
+int ethos_read_device_error(int* dev_err, int* host_code, int reset, void* stream);
+
+/* Checks `dims` against the compiled kernels; returns ETHOS_OK or
+ * ETHOS_ERR_UNSUPPORTED_SHAPE.  Supported: d_latent 128, d_hidden 512,
+ * num_heads * top_k <= 128 (multiple of 4), top_k in {4, 8, 16},
+ * num_sub_keys a multiple of 32 up to 512 with num_sub_keys >= top_k,
+ * d_query/2 a multiple of 32, d_model a multiple of 256,
+ * (num_heads * d_query + d_hidden) a multiple of 256. */
+int ethos_check_dims(const ethos_dims* dims);
+
+/* --------------------------------------------------------- forward -- */
+/* Scratch bytes needed by ethos_layer_forward / ethos_router_forward. */
+size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training);
+
+/* Router + reordered expert forward of one layer.
+ *
+ * Replaces SimplifiedHypernetMoE.forward (model.py:288-343) and
+ * FusedLowRankMoE_Reordered.forward (kernels.py:145-221, including the
+ * per-head Triton launches kernels.py:167-217) together with the router call
+ * ProductKeyRouter.forward (model.py:208-254).
+ *
+ *  x         bf16 [T, d]
+ *  w_cat     bf16 [H*dq + dh, d]: row block h = query_projs[h].weight
+ *            (model.py:195-197); last dh rows = net.2.weight[:d]^T (W_u of
+ *            model.py:299, transposed to [dh, d])
+ *  bn        fp32 [5, H*dq]: rows = query_projs bias, query_norms weight,
+ *            query_norms bias, running_mean, running_var (model.py:195-202).
+ *            In training mode the running rows are updated in place
+ *            (momentum `bn_momentum`, unbiased variance), as BatchNorm1d does.
+ *  key_cat   bf16 [2, K, dq]: [p][key] = sub_keys_{p+1}.weight[key] written
+ *            twice ([hi | lo] operand layout of the split-bf16 fp32 scoring)
+ *  latents   bf16 [N, dl]   expert_latents.weight
+ *  w1        bf16 [dh, dl]  generation_network.net.0.weight
+ *  wv        bf16 [d, dh]   generation_network.net.2.weight[d:]
+ *  y         bf16 [T, d]    output (already divided by H, model.py:341)
+ *  ids       int32 [T, H, k] selected expert ids (i1*K + i2, model.py:245)
+ *  weights   fp32 [T, H, k]  softmax routing weights (model.py:234, fp32)
+ *  save_*    optional (may be NULL) tensors kept for the backward pass:
+ *            save_xp fp32 [T, dh] (x @ W_u), save_hacc bf16 [T, dh]
+ *            (sum_{h,k} a*h), save_dot fp32 [T, H*k] (h . x_proj),
+ *            save_qpre fp32 [T, H*dq] (pre-BatchNorm queries; training only),
+ *            save_bn fp32 [2, H*dq] (batch mean, 1/sqrt(var+eps); training only)
+ */
+int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
+                        float bn_momentum, int bn_training, const void* key_cat, const void* latents,
+                        const void* w1, const void* wv, void* y, int32_t* ids, float* weights,
+                        float* save_xp, void* save_hacc, float* save_dot, float* save_qpre,
+                        float* save_bn, void* workspace, size_t workspace_bytes, int* dev_err,
+                        void* stream);
+
+/* Router alone: ProductKeyRouter.forward (model.py:208-254) on x [T, d]
+ * (bf16).  Arguments as for ethos_layer_forward; w_cat needs only its first
+ * H*dq rows.  Outputs ids int32 [T, H, k] and fp32 softmax weights. */
+int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
+                         float bn_momentum, int bn_training, const void* key_cat, int32_t* ids,
+                         float* weights, float* save_qpre, float* save_bn, void* workspace,
+                         size_t workspace_bytes, int* dev_err, void* stream);
+
+/* Reordered experts alone, given routing decisions (the per-head Triton
+ * launches of kernels.py:167-217 / the expert loop of model.py:306-336):
+ *  latents bf16 [N, dl]; w1 bf16 [dh, dl]; ids int32 [T, H*k];
+ *  weights fp32 [T, H*k]; xp fp32 [T, dh] (x @ W_u)
+ *  hacc   bf16 [T, dh] out: sum_{h,k} gelu(h.xp)*w*h;  dot fp32 [T, H*k] out
+ *         (optional, may be NULL)
+ * Ids outside [0, N) are not dereferenced: they set ETHOS_ERR_ID_OUT_OF_RANGE
+ * in dev_err and gather row 0 instead. */
+int ethos_expert_forward(const ethos_dims* dims, const void* latents, const void* w1, const int32_t* ids,
+                         const float* weights, const float* xp, void* hacc, float* dot, int* dev_err,
+                         void* stream);
+
+/* Product-key top-k from already normalised queries (the scoring, per-half
+ * top-k, candidate-grid top-k, softmax and id decode of model.py:217-245).
+ *  q     bf16 [H, T, dq]  normalised queries
+ *  keys  bf16 [2, K, dq/2] sub_keys_1.weight, sub_keys_2.weight
+ *  ids   int32 [T, H, k];  weights fp32 [T, H, k]
+ * Scores are accumulated in fp32 from the bf16 operands. */
+int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* keys, int32_t* ids,
+                           float* weights, int* dev_err, void* stream);
+
+/* Plain bf16 GEMM D[M, N] = A[M, K] B[N, K]^T * scale on the tcgen05 path
+ * (fp32 accumulate), used by the layer and exposed for tests.  out_dtype 0 =
+ * fp32, 1 = bf16.  M >= 1, N % 256 == 0, K % 64 == 0. */
+int ethos_gemm_bf16(const void* a, const void* b, void* d, int64_t M, int64_t N, int64_t K, float scale,
+                    int out_dtype, int* dev_err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ETHOS_B200_H */

@@ -1,0 +1,136 @@
+"""Generate the golden fixtures by running the REFERENCE itself.
+
+Run in a container where the reference checkout exists (it is not needed
+afterwards; the fixtures are committed):
+
+    python tests/golden/make_golden.py --reference /path/to/ETHOS
+
+It imports the reference's ``model.py`` and runs ``SimplifiedHypernetMoE``
+(the non-Triton path, ``model.py:267-343``, with ``ProductKeyRouter``,
+``model.py:182-254``) in fp32 on CPU, with the seeded initialisation of
+``ethos_b200.init`` and seeded inputs / upstream gradients, and stores inputs,
+outputs, router decisions, BatchNorm running-stat updates and autograd
+gradients of every parameter and of ``x``.
+
+Small cases store every tensor.  The config-1 case (d_model 512, 4096
+experts, 256 tokens) stores the forward outputs in full and, for a 32-token
+backward, the full gradients of the small parameters plus norms and a fixed
+sample of entries of the large ones (to keep the fixture small); the
+parameters themselves are regenerated from the seed and checked against a
+stored checksum.
+"""
+
+import argparse
+import os
+import sys
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from ethos_b200.config import EthosConfig  # noqa: E402
+from ethos_b200.init import seeded_init_, seeded_input, tensor_generator  # noqa: E402
+
+CASES = {
+    "tiny": dict(cfg=dict(d_model=64, num_experts=64, top_k=4, num_routing_heads=2,
+                          d_latent=16, d_intermediate_hypernet=32, d_query=32),
+                 tokens=10, batch=2, full=True, bwd_tokens=10),
+    "small": dict(cfg=dict(d_model=128, num_experts=256, top_k=8, num_routing_heads=4,
+                           d_latent=32, d_intermediate_hypernet=64, d_query=64),
+                  tokens=24, batch=2, full=True, bwd_tokens=24),
+    "cfg1": dict(cfg=dict(d_model=512, num_experts=4096, top_k=16, num_routing_heads=8,
+                          d_latent=128, d_intermediate_hypernet=512, d_query=512),
+                 tokens=256, batch=2, full=False, bwd_tokens=32),
+}
+
+SAMPLE = 4096
+
+
+def checksum(sd):
+    out = {}
+    for k, v in sd.items():
+        v = v.double()
+        out[k] = torch.tensor([v.sum().item(), (v * v).sum().item()], dtype=torch.float64)
+    return out
+
+
+def sample_idx(numel, name):
+    g = tensor_generator(7, "sample." + name)
+    return torch.randint(0, numel, (min(SAMPLE, numel),), generator=g)
+
+
+def run_case(model_mod, name, spec):
+    cfg = EthosConfig(**spec["cfg"])
+    torch.manual_seed(0)
+    ref = model_mod.SimplifiedHypernetMoE(cfg)
+    seeded_init_(ref, seed=0)
+    sd0 = {k: v.detach().clone() for k, v in ref.state_dict().items()}
+    T, B = spec["tokens"], spec["batch"]
+    x = seeded_input(T, cfg.d_model, seed=0)
+    rec = dict(cfg=spec["cfg"], tokens=T, full=spec["full"], checksum=checksum(sd0))
+    if spec["full"]:
+        rec["state_dict"] = sd0
+        rec["x"] = x.clone()
+
+    # ---- eval-mode forward over all tokens -------------------------------
+    ref.eval()
+    t0 = time.time()
+    with torch.no_grad():
+        scores, ids = ref.router(x)
+        y = ref(x.view(B, T // B, cfg.d_model)).reshape(T, cfg.d_model)
+    rec["eval"] = dict(y=y.clone(), scores=scores.clone(), ids=ids.to(torch.int32).clone())
+    print(f"[{name}] eval forward {time.time() - t0:.1f}s")
+
+    # ---- train-mode forward + backward on a token prefix -----------------
+    for mode in ("train", "eval_bwd"):
+        ref.load_state_dict(sd0)
+        ref.train(mode == "train")
+        Tb = spec["bwd_tokens"]
+        xb = x[:Tb].clone().requires_grad_(True)
+        ref.zero_grad(set_to_none=True)
+        t0 = time.time()
+        yb = ref(xb.view(1, Tb, cfg.d_model)).reshape(Tb, cfg.d_model)
+        g = torch.randn(yb.shape, generator=tensor_generator(0, "upstream." + mode))
+        (yb * g).sum().backward()
+        print(f"[{name}] {mode} fwd+bwd {time.time() - t0:.1f}s")
+        grads = {n: p.grad.detach().clone() for n, p in ref.named_parameters() if p.grad is not None}
+        entry = dict(tokens=Tb, y=yb.detach().clone(), upstream=g, x_grad=xb.grad.detach().clone())
+        if mode == "train":
+            entry["running"] = {k: v.detach().clone() for k, v in ref.state_dict().items()
+                                if "running" in k or "num_batches" in k}
+        if spec["full"]:
+            entry["grads"] = grads
+        else:
+            small, big = {}, {}
+            for n, gr in grads.items():
+                if gr.numel() <= 65536 * 2:
+                    small[n] = gr
+                else:
+                    idx = sample_idx(gr.numel(), n)
+                    big[n] = dict(norm=gr.double().norm().item(),
+                                  vals=gr.flatten()[idx].clone(), shape=tuple(gr.shape))
+            entry["grads"] = small
+            entry["grads_sampled"] = big
+        rec[mode] = entry
+    return rec
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("ETHOS_REFERENCE", "/root/reference"))
+    ap.add_argument("--cases", default=",".join(CASES))
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    import model as model_mod  # the reference's model.py
+    torch.set_num_threads(os.cpu_count() or 1)
+    for name in args.cases.split(","):
+        rec = run_case(model_mod, name, CASES[name])
+        path = os.path.join(HERE, f"golden_{name}.pt")
+        torch.save(rec, path)
+        print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")
+
+
+if __name__ == "__main__":
+    main()

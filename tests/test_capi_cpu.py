@@ -1,0 +1,100 @@
+"""CPU-side checks of the C ABI: the library loads, exports every entry point
+that include/ethos_b200.h declares, and its host-only functions (dimension
+checks, workspace sizing, status strings) behave.  No kernel is launched."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from ethos_b200 import _lib
+from ethos_b200.build import LIB_PATH, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "ethos_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\s*\*)\s*(ethos_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    build()
+    return _lib.lib()
+
+
+def test_library_built_in_tree():
+    build()
+    assert os.path.exists(LIB_PATH)
+
+
+def test_every_declared_symbol_is_exported(L):
+    names = declared_functions()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.EXPORTS), "ctypes table and header disagree"
+
+
+def test_abi_version_and_status_strings(L):
+    assert L.ethos_abi_version() >= 1
+    assert L.ethos_status_string(0) == b"ok"
+    assert b"unsupported" in L.ethos_status_string(2)
+    assert b"timed out" in L.ethos_status_string(1003)
+
+
+def _dims(**kw):
+    base = dict(tokens=16384, d_model=1024, num_experts=512 * 512, num_sub_keys=512, d_query=512,
+                d_latent=128, d_hidden=512, num_heads=8, top_k=16)
+    base.update(kw)
+    return _lib.EthosDims(**base)
+
+
+@pytest.mark.parametrize("kw,ok", [
+    ({}, True),
+    (dict(d_model=512, num_experts=4096, num_sub_keys=64), True),      # config 1
+    (dict(tokens=1), True),
+    (dict(d_latent=64), False),
+    (dict(d_hidden=256), False),
+    (dict(top_k=32), False),
+    (dict(top_k=12), False),
+    (dict(num_experts=512 * 511), False),
+    (dict(num_sub_keys=1024, num_experts=1024 * 1024), False),
+    (dict(d_query=96), False),
+    (dict(d_model=1000), False),
+    (dict(tokens=0), False),
+])
+def test_check_dims(L, kw, ok):
+    d = _dims(**kw)
+    st = L.ethos_check_dims(ctypes.byref(d))
+    assert (st == 0) == ok, (kw, st)
+
+
+def test_workspace_size(L):
+    d = _dims()
+    ev = L.ethos_forward_workspace_size(ctypes.byref(d), 0)
+    tr = L.ethos_forward_workspace_size(ctypes.byref(d), 1)
+    T, H, dq, dh = 16384, 8, 512, 512
+    assert ev >= H * 2 * T * dq * 2 + T * dh * (4 + 2)
+    assert tr >= ev + T * H * dq * 4
+    bad = _dims(top_k=32)
+    assert L.ethos_forward_workspace_size(ctypes.byref(bad), 0) == 0
+
+
+def test_null_arguments_rejected_without_gpu(L):
+    d = _dims()
+    st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None,
+                               None, None, None, None, None, None, None, None, None, 0, None, None)
+    assert st == 1  # ETHOS_ERR_INVALID_ARG
+
+
+def test_no_cpu_fallback():
+    """The ops refuse CPU tensors instead of computing on the host."""
+    import torch
+    from ethos_b200 import ops
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        ops.gemm_bf16(torch.zeros(128, 64, dtype=torch.bfloat16), torch.zeros(256, 64, dtype=torch.bfloat16))
