@@ -36,8 +36,8 @@ constexpr int EX_ZSTAGES = 2;
 constexpr int EX_OFF_Z = EX_W1_BYTES;
 constexpr int EX_OFF_XP = EX_OFF_Z + EX_ZSTAGES * EX_Z_BYTES;
 constexpr int EX_OFF_W = EX_OFF_XP + EX_ZSTAGES * EX_DH * 4;
-constexpr int EX_OFF_HACC = EX_OFF_W + EX_ZSTAGES * EX_ROWS * 4;
-constexpr int EX_OFF_DOTP = EX_OFF_HACC + EX_DH * 4;
+constexpr int EX_OFF_HACC = EX_OFF_W + EX_ZSTAGES * EX_ROWS * 4;   // [4 quarters][512] partials
+constexpr int EX_OFF_DOTP = EX_OFF_HACC + 4 * EX_DH * 4;
 constexpr int EX_OFF_CTL = EX_OFF_DOTP + 2 * EX_ROWS * 4;
 
 struct ExpertCtl {
@@ -100,10 +100,9 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
     ctl->abort = 0;
     fence_mbar_init();
   }
-  // zero the A tiles (rows >= R stay zero) and the hidden accumulator
+  // zero the A tiles (rows >= R stay zero)
   for (int i = threadIdx.x; i < EX_ZSTAGES * EX_Z_BYTES / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(z_s)[i] = make_uint4(0, 0, 0, 0);
-  for (int i = threadIdx.x; i < EX_DH; i += blockDim.x) hacc_s[i] = 0.f;
   fence_proxy_async_smem();
   if (warp == 2) {
     tmem_alloc(&ctl->tmem_base, 512);
@@ -249,8 +248,9 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
           tmem_ld32(tmem_addr(tmem, q * 32, c * 32), v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = valid ? a * v[e] : 0.f;
-          const float colsum = warp_transpose_reduce32(v, lane);
-          atomicAdd(&hacc_s[c * 32 + lane], colsum);
+          // column sums of this warp's 32 rows; quarters are combined in a
+          // fixed order below, so the result is deterministic
+          hacc_s[q * EX_DH + c * 32 + lane] = warp_transpose_reduce32(v, lane);
         }
         tc_fence_before();
         __syncwarp();
@@ -260,9 +260,12 @@ __global__ void __launch_bounds__(EX_THREADS, 1)
       named_bar_sync(1, 256);
       {
         const int j = etid * 2;
-        const float h0 = hacc_s[j], h1 = hacc_s[j + 1];
-        hacc_s[j] = 0.f;
-        hacc_s[j + 1] = 0.f;
+        const float2 p0 = *reinterpret_cast<const float2*>(hacc_s + j);
+        const float2 p1 = *reinterpret_cast<const float2*>(hacc_s + EX_DH + j);
+        const float2 p2 = *reinterpret_cast<const float2*>(hacc_s + 2 * EX_DH + j);
+        const float2 p3 = *reinterpret_cast<const float2*>(hacc_s + 3 * EX_DH + j);
+        const float h0 = (p0.x + p1.x) + (p2.x + p3.x);
+        const float h1 = (p0.y + p1.y) + (p2.y + p3.y);
         *reinterpret_cast<uint32_t*>(args.hacc + static_cast<int64_t>(t) * EX_DH + j) = pack_bf16x2(h0, h1);
       }
     }

@@ -43,6 +43,11 @@ CASES = {
     "cfg1": dict(cfg=dict(d_model=512, num_experts=4096, top_k=16, num_routing_heads=8,
                           d_latent=128, d_intermediate_hypernet=512, d_query=512),
                  tokens=256, batch=2, full=False, bwd_tokens=32),
+    # the GPU parity protocol: the reference in fp32 on bf16-ROUNDED params
+    # and inputs (what the bf16 kernels consume); forward only
+    "cfg1_bf16r": dict(cfg=dict(d_model=512, num_experts=4096, top_k=16, num_routing_heads=8,
+                                d_latent=128, d_intermediate_hypernet=512, d_query=512),
+                       tokens=256, batch=2, full=False, bwd_tokens=32, round_bf16=True, fwd_only=True),
 }
 
 SAMPLE = 4096
@@ -66,10 +71,18 @@ def run_case(model_mod, name, spec):
     torch.manual_seed(0)
     ref = model_mod.SimplifiedHypernetMoE(cfg)
     seeded_init_(ref, seed=0)
+    rnd = spec.get("round_bf16", False)
+    if rnd:
+        with torch.no_grad():
+            for v in ref.state_dict().values():
+                if v.is_floating_point():
+                    v.copy_(v.to(torch.bfloat16).float())
     sd0 = {k: v.detach().clone() for k, v in ref.state_dict().items()}
     T, B = spec["tokens"], spec["batch"]
     x = seeded_input(T, cfg.d_model, seed=0)
-    rec = dict(cfg=spec["cfg"], tokens=T, full=spec["full"], checksum=checksum(sd0))
+    if rnd:
+        x = x.to(torch.bfloat16).float()
+    rec = dict(cfg=spec["cfg"], tokens=T, full=spec["full"], checksum=checksum(sd0), round_bf16=rnd)
     if spec["full"]:
         rec["state_dict"] = sd0
         rec["x"] = x.clone()
@@ -84,7 +97,7 @@ def run_case(model_mod, name, spec):
     print(f"[{name}] eval forward {time.time() - t0:.1f}s")
 
     # ---- train-mode forward + backward on a token prefix -----------------
-    for mode in ("train", "eval_bwd"):
+    for mode in (() if spec.get("fwd_only") else ("train", "eval_bwd")):
         ref.load_state_dict(sd0)
         ref.train(mode == "train")
         Tb = spec["bwd_tokens"]

@@ -49,6 +49,8 @@ def reference_state_dict(rec):
     from ethos_b200.layer import EthosExpertLayer
     layer = EthosExpertLayer(EthosConfig(**rec["cfg"]))
     sd = seeded_state_dict(layer, seed=0)
+    if rec.get("round_bf16"):
+        sd = {k: (v.to(torch.bfloat16).float() if v.is_floating_point() else v) for k, v in sd.items()}
     for k, (s, ss) in rec["checksum"].items():
         v = sd[k].double()
         assert abs(v.sum().item() - s.item()) <= 1e-9 * max(1.0, abs(s.item())) + 1e-9, k
@@ -59,7 +61,10 @@ def reference_state_dict(rec):
 def golden_input(rec):
     if "x" in rec:
         return rec["x"]
-    return seeded_input(rec["tokens"], rec["cfg"]["d_model"], seed=0)
+    x = seeded_input(rec["tokens"], rec["cfg"]["d_model"], seed=0)
+    if rec.get("round_bf16"):
+        x = x.to(torch.bfloat16).float()
+    return x
 
 
 def dims_of(cfg):

@@ -37,8 +37,13 @@ def test_seeded_params_checksum(golden):
     reference_state_dict(rec)  # asserts the checksum for regenerated cases
 
 
-def test_eval_forward_matches_reference(golden):
+@pytest.mark.parametrize("extra", [None, "cfg1_bf16r"])
+def test_eval_forward_matches_reference(golden, extra):
     name, rec = golden
+    if extra is not None:
+        if name != "cfg1":
+            pytest.skip("extra fixture checked once")
+        name, rec = extra, load_golden(extra)
     dims, p = _params(rec)
     x = golden_input(rec)
     with torch.no_grad():
