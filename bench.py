@@ -39,14 +39,30 @@ METRIC = "expert-layer tokens/s (262K experts, k=16x8 heads)"
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20
 
-# algorithmic work per token at config 2 (router + experts forward)
+# Algorithmic work at config 2 (router + experts forward), per token:
 #   MACs: q-proj 8*512*1024, scoring 8*2*512*256, x_proj 1024*512,
 #         expansion 128*128*512, dot + weighted sum 2*128*512, W_v 512*1024
 FLOP_PER_TOKEN = 2 * (8 * 512 * 1024 + 8 * 2 * 512 * 256 + 1024 * 512 + 128 * 128 * 512
                       + 2 * 128 * 512 + 512 * 1024)
-# expert kernel alone (gather + expansion + GELU + dot + weighted sum)
-EXPERT_FLOP_PER_TOKEN = 2 * (128 * 128 * 512 + 2 * 128 * 512)
-EXPERT_BYTES_PER_TOKEN = 128 * 256 + 512 * 4 + 128 * 8 + 512 * 2  # rows, xp, ids+w, hacc
+N_EXPERTS = 512 * 512
+# per-stage algorithmic work for the kernel roofline (kind, amount per step as
+# a function of T): GEMM stages in FLOPs, the table gather in HBM bytes
+#   projection   x @ [Wq_0..Wq_7 | W_u]       2 * 1024 * 4608 per token
+#   topk         sub-key scores q . K          2 * 8 * 2 * 512 * 256 per token
+#   expert_table gelu(E @ W1^T), once per expert  2 * N * 128 * 512 per step
+#   experts      per token: 128 selected 1 KB fp16 table rows + xp (2 KB fp32)
+#                + ids/weights (1 KB) + hacc out (1 KB bf16)
+#   end          hacc @ W_v                     2 * 512 * 1024 per token
+STAGE_WORK = {
+    "projection": ("tensor", lambda T: 2.0 * 1024 * 4608 * T),
+    "topk": ("tensor", lambda T: 2.0 * 8 * 2 * 512 * 256 * T),
+    "expert_table": ("tensor", lambda T: 2.0 * N_EXPERTS * 128 * 512),
+    "experts": ("hbm", lambda T: (128 * 1024 + 512 * 4 + 128 * 8 + 512 * 2) * float(T)),
+    "end": ("tensor", lambda T: 2.0 * 512 * 1024 * T),
+}
+STAGE_KERNEL = {"projection": "k_gemm_bf16_tn<EpiProj>", "topk": "k_score_topk<16>",
+                "expert_table": "k_gemm_bf16_tn<EpiGeluF16>", "experts": "k_expert_gather",
+                "end": "k_gemm_bf16_tn<EpiStoreBF16>"}
 
 
 def load_peaks():
@@ -61,10 +77,10 @@ def load_peaks():
         return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, source="fallback")
 
 
-def load_traffic():
-    """Per-launch DRAM bytes of the expert kernel from the committed ncu
-    summary (profiles/expert_fwd_config2.md, line 'dram_bytes_per_launch:')."""
-    path = os.path.join(ROOT, "profiles", "expert_fwd_config2.md")
+def load_traffic(stage):
+    """Per-launch DRAM bytes of a stage's kernel from its committed ncu summary
+    (profiles/<stage>_config2.md, line 'dram_bytes_per_launch: <bytes>')."""
+    path = os.path.join(ROOT, "profiles", f"{stage}_config2.md")
     try:
         with open(path) as f:
             for line in f:
@@ -259,22 +275,35 @@ def main():
         ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
         ms = max_over_ranks(ms)
 
-        # ---------------- expert kernel alone (roofline) ------------------
+        # ---------------- per-kernel stage timing (roofline) ---------------
         pw = layer._packed(dev)
-        out = ops.layer_forward(x_dev, pw, False, 1e-5, 0.1, save=True)
-        for _ in range(3):
-            ops.expert_forward(pw.latents, pw.w1, out["ids"], out["weights"], out["xp"], pw.dims)
-        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(max(5, min(args.steps, 20)))]
-        for s, e in kev:
+        n_ev = len(ops.STAGES)
+        sev = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(max(5, min(args.steps, 20)))]
+        for _ in range(2):
+            ops.layer_forward(x_dev, pw, False, 1e-5, 0.1, path=layer.expert_path)
+        for evs in sev:
             flush.zero_()
-            s.record(stream)
-            ops.expert_forward(pw.latents, pw.w1, out["ids"], out["weights"], out["xp"], pw.dims)
-            e.record(stream)
+            ops.layer_forward(x_dev, pw, False, 1e-5, 0.1, path=layer.expert_path, stage_events=evs)
         torch.cuda.synchronize()
         ops.check_device_error(dev)
-        kms = sum(s.elapsed_time(e) for s, e in kev) / len(kev)
-        kms = max_over_ranks(kms)
+        stage_ms = {}
+        for i in range(1, n_ev):
+            name = ops.STAGES[i]
+            v = sum(evs[i - 1].elapsed_time(evs[i]) for evs in sev) / len(sev)
+            stage_ms[name] = max_over_ranks(v)
+        # the fused per-token expert path on the same routing, for comparison
+        out = ops.layer_forward(x_dev, pw, False, 1e-5, 0.1, save=True)
+        fev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(3)]
+        ops.expert_forward(pw.latents, pw.w1, out["ids"], out["weights"], out["xp"], pw.dims, path=ops.EXPERT_FUSED)
+        for s_, e_ in fev:
+            flush.zero_()
+            s_.record(stream)
+            ops.expert_forward(pw.latents, pw.w1, out["ids"], out["weights"], out["xp"], pw.dims,
+                               path=ops.EXPERT_FUSED)
+            e_.record(stream)
+        torch.cuda.synchronize()
+        fused_ms = max_over_ranks(sum(s_.elapsed_time(e_) for s_, e_ in fev) / len(fev))
+        del out
 
         # ---------------- end to end through the public API ---------------
         e2e_steps = max(3, min(args.steps, 20))
@@ -299,8 +328,24 @@ def main():
     peaks = load_peaks()
     total_tokens = T * world
     value = total_tokens / (ms / 1e3)
-    k_achieved = EXPERT_FLOP_PER_TOKEN * T / (kms / 1e3) / 1e12
-    traffic = load_traffic()
+    # roofline of the dominant kernel (largest stage of the step)
+    stages = {k: v for k, v in stage_ms.items() if k in STAGE_WORK and v > 0}
+    dom = max(stages, key=stages.get)
+    kind, work = STAGE_WORK[dom]
+    amount = work(T)
+    if kind == "tensor":
+        achieved, peak, unit = amount / (stages[dom] / 1e3) / 1e12, peaks["bf16_tflops"], "TFLOP/s"
+    else:
+        achieved, peak, unit = amount / (stages[dom] / 1e3) / 1e9, peaks["hbm_gbs"], "GB/s"
+    traffic = load_traffic(dom)
+    stage_report = {}
+    for k, v in stages.items():
+        kk, ww = STAGE_WORK[k]
+        a = ww(T) / (v / 1e3)
+        stage_report[k] = dict(ms=v, kernel=STAGE_KERNEL[k],
+                               achieved=a / (1e12 if kk == "tensor" else 1e9),
+                               unit="TFLOP/s" if kk == "tensor" else "GB/s",
+                               frac=(a / 1e12 / peaks["bf16_tflops"]) if kk == "tensor" else (a / 1e9 / peaks["hbm_gbs"]))
     line = dict(
         metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
@@ -308,18 +353,16 @@ def main():
         config=dict(workload="config 2: ETHOS expert layer forward (router + experts), 262144 experts, "
                              "k=16 x 8 heads, d_model 1024, d_latent 128, d_hidden 512, BN eval",
                     tokens_per_gpu=T, global_batch=total_tokens, parallelism=f"dp{world} (token shards)",
-                    l2="flushed between timed steps (256 MiB write)"),
+                    l2="flushed between timed steps (256 MiB write)", expert_path="auto (table at this size)"),
         layer_tflops=FLOP_PER_TOKEN * T / (ms / 1e3) / 1e12,
-        expert_kernel_ms=kms,
-        roofline=dict(bound="tensor", kernel="k_expert_fwd", achieved=k_achieved, peak=peaks["bf16_tflops"],
-                      unit="TFLOP/s", frac=k_achieved / peaks["bf16_tflops"],
-                      traffic=traffic, peak_source=peaks["source"] + " (bf16 burst)",
-                      algorithmic_flop_per_token=EXPERT_FLOP_PER_TOKEN,
-                      algorithmic_bytes_per_token=EXPERT_BYTES_PER_TOKEN,
-                      hbm_gbs=EXPERT_BYTES_PER_TOKEN * T / (kms / 1e3) / 1e9),
+        roofline=dict(bound=kind, kernel=STAGE_KERNEL[dom], stage=dom, achieved=achieved, peak=peak, unit=unit,
+                      frac=achieved / peak, traffic=traffic,
+                      peak_source=peaks["source"] + (" bf16 burst" if kind == "tensor" else " HBM copy")),
+        stages=stage_report,
+        fused_expert_path_ms=fused_ms,
         e2e=dict(value=total_tokens / (ems / 1e3), unit=UNIT, h2d_bytes_per_step=x_host.numel() * 2,
                  d2h_bytes_per_step=y_host.numel() * 2),
-        gpu_launches=5 * args.steps,
+        gpu_launches=6 * args.steps,
         clocks=clocks,
     )
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

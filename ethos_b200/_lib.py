@@ -54,12 +54,13 @@ EXPORTS = {
     "ethos_status_string": (ctypes.c_char_p, [_I]),
     "ethos_read_device_error": (_I, [_P, ctypes.POINTER(_I), _I, _P]),
     "ethos_check_dims": (_I, [_DIMS]),
-    "ethos_forward_workspace_size": (_SZ, [_DIMS, _I]),
-    "ethos_layer_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _P, _P, _P,
-                                 _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "ethos_forward_workspace_size": (_SZ, [_DIMS, _I, _I]),
+    "ethos_expert_workspace_size": (_SZ, [_DIMS, _I]),
+    "ethos_layer_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _I, _P, _P, _P,
+                                 _P, _P, _P, _P, _P, _P, _SZ, _P, _P, _P]),
     "ethos_router_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _P, _P, _SZ,
                                   _P, _P]),
-    "ethos_expert_forward": (_I, [_DIMS, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "ethos_expert_forward": (_I, [_DIMS, _I, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "ethos_product_key_topk": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _F, _I, _P, _P]),
 }

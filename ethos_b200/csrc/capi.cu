@@ -10,6 +10,7 @@
 
 #include "ethos_b200.h"
 #include "expert.cuh"
+#include "expert_table.cuh"
 #include "gemm.cuh"
 #include "router.cuh"
 
@@ -48,6 +49,8 @@ int device_info(DeviceInfo** out) {
     ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiStoreF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                GEMM_SMEM_BYTES) == cudaSuccess;
     ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiProj>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GEMM_SMEM_BYTES) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiGeluF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                GEMM_SMEM_BYTES) == cudaSuccess;
     ok &= cudaFuncSetAttribute(k_score_topk<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTER_SMEM_BYTES) ==
           cudaSuccess;
@@ -99,6 +102,12 @@ int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Optional per-stage timing: records stage_events[i] (a cudaEvent_t) on the
+// stream at stage boundary i when the caller passed an array.
+void mark(void* const* ev, int i, cudaStream_t s) {
+  if (ev != nullptr && ev[i] != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s);
+}
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? ETHOS_OK : ETHOS_ERR_CUDA;
@@ -129,8 +138,9 @@ struct Carve {
 };
 
 struct FwdScratch {
+  __half* table;
   __nv_bfloat16* qs;
-  float4* colp;
+  float2* colp;
   float* xp;
   __nv_bfloat16* hacc;
   float* qpre;
@@ -140,10 +150,11 @@ struct FwdScratch {
 };
 
 void carve_forward(Carve& c, const ethos_dims& d, int bn_training, bool need_xp, bool need_hacc, bool need_qpre,
-                   bool need_bn, FwdScratch* s) {
+                   bool need_bn, bool need_table, FwdScratch* s) {
   const int64_t T = d.tokens, HQ = d.num_heads * d.d_query;
+  s->table = need_table ? c.take<__half>(static_cast<size_t>(d.num_experts) * EX_DH) : nullptr;
   s->qs = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.d_query));
-  s->colp = c.take<float4>(static_cast<size_t>(HQ));
+  s->colp = c.take<float2>(static_cast<size_t>(HQ));
   s->xp = need_xp ? c.take<float>(static_cast<size_t>(T * d.d_hidden)) : nullptr;
   s->hacc = need_hacc ? c.take<__nv_bfloat16>(static_cast<size_t>(T * d.d_hidden)) : nullptr;
   s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
@@ -175,6 +186,65 @@ int check_dims_impl(const ethos_dims* d) {
   return ETHOS_OK;
 }
 
+// ------------------------------------------------------------ experts --
+// Expert execution path: 1 = fused per-token (gather latents, expand on
+// tcgen05, GELU in the epilogue), 2 = expert table (expand + GELU once per
+// expert, then gather hidden rows per token).  0 picks the table once the
+// step makes at least one selection per expert on average.
+int resolve_expert_path(const ethos_dims& d, int path) {
+  if (path == 1 || path == 2) return path;
+  const int64_t sel = d.tokens * d.num_heads * d.top_k;
+  return sel >= d.num_experts ? 2 : 1;
+}
+
+size_t expert_table_bytes(const ethos_dims& d) {
+  return static_cast<size_t>(d.num_experts) * EX_DH * sizeof(__half);
+}
+
+int run_experts(const ethos_dims& d, int path, const void* latents, const void* w1, const int32_t* ids,
+                const float* weights, const float* xp, __nv_bfloat16* hacc, float* dot, __half* table, int* err,
+                cudaStream_t stream, const DeviceInfo& dev, void* const* ev = nullptr) {
+  const int T = static_cast<int>(d.tokens);
+  const int R = static_cast<int>(d.num_heads * d.top_k);
+  const int N = static_cast<int>(d.num_experts);
+  int st;
+  if (path == 1) {
+    CUtensorMap tm_w1;
+    if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
+    ExpertFwdArgs ea;
+    ea.latents = static_cast<const __nv_bfloat16*>(latents);
+    ea.ids = ids;
+    ea.w = weights;
+    ea.xp = xp;
+    ea.hacc = hacc;
+    ea.save_dot = dot;
+    ea.T = T;
+    ea.R = R;
+    ea.N = N;
+    const int grid = T < dev.sm_count ? T : dev.sm_count;
+    mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
+    k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, stream>>>(tm_w1, ea, err);
+    return launch_status();
+  }
+  // phase A: H = fp16(gelu(E @ W1^T))   [N, 512]
+  CUtensorMap tm_e, tm_w1;
+  if ((st = make_tmap_bf16(&tm_e, latents, N, EX_DL, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
+  EpiGeluF16 eg;
+  eg.out = table;
+  eg.ldo = EX_DH;
+  eg.M = N;
+  if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
+  mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
+  // phase B: per-token gather, dot, activation, weighted sum
+  const int warps_needed = T;
+  int blocks = (warps_needed + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
+  const int max_blocks = dev.sm_count * 2;
+  if (blocks > max_blocks) blocks = max_blocks;
+  k_expert_gather<<<blocks, GATHER_THREADS, 0, stream>>>(table, ids, weights, xp, hacc, dot, T, R, N, err);
+  return launch_status();
+}
+
 template <int TOPK>
 int launch_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g, int32_t* ids, float* w,
                  int* err, cudaStream_t stream, const DeviceInfo& dev) {
@@ -200,7 +270,7 @@ int run_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g,
 int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn, float bn_eps, float bn_momentum,
                 int bn_training, const void* key_cat, int32_t* ids, float* weights, bool with_xp, float* xp_out,
                 const FwdScratch& s, float* qpre, float* save_bn, int* err, cudaStream_t stream,
-                const DeviceInfo& dev) {
+                const DeviceInfo& dev, void* const* ev = nullptr) {
   const int T = static_cast<int>(d.tokens);
   const int HQ = static_cast<int>(d.num_heads * d.d_query);
   const int dq = static_cast<int>(d.d_query);
@@ -233,6 +303,7 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   epi.xp = xp_out;
   if ((st = launch_gemm(tm_x, tm_w, T, ncat, static_cast<int>(d.d_model), epi, err, stream, dev)) != ETHOS_OK)
     return st;
+  mark(ev, ETHOS_STAGE_PROJECTION, stream);
   if (bn_training) {
     dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
     k_bn_partial<<<grid_p, cb, 0, stream>>>(qpre, T, HQ, s.bn_part);
@@ -245,6 +316,7 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
                                                                                 s.qs);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
+  mark(ev, ETHOS_STAGE_BATCHNORM, stream);
   RouterGeom g;
   g.T = T;
   g.H = static_cast<int>(d.num_heads);
@@ -253,7 +325,9 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   g.a_stride_h = 2 * T;
   g.a_stride_p = T;
   g.a_col_p = 0;
-  return run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, err, stream, dev);
+  st = run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, err, stream, dev);
+  mark(ev, ETHOS_STAGE_TOPK, stream);
+  return st;
 }
 
 }  // namespace
@@ -295,23 +369,30 @@ int ethos_read_device_error(int* dev_err, int* host_code, int reset, void* strea
 
 int ethos_check_dims(const ethos_dims* dims) { return check_dims_impl(dims); }
 
-size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training) {
+size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training, int expert_path) {
   if (check_dims_impl(dims) != ETHOS_OK) return 0;
   Carve c{nullptr, 0, 0};
   FwdScratch s;
-  carve_forward(c, *dims, bn_training, true, true, true, true, &s);
+  carve_forward(c, *dims, bn_training, true, true, true, true, resolve_expert_path(*dims, expert_path) == 2, &s);
   return c.off + 256;
+}
+
+size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path) {
+  if (check_dims_impl(dims) != ETHOS_OK) return 0;
+  return resolve_expert_path(*dims, expert_path) == 2 ? expert_table_bytes(*dims) + 256 : 256;
 }
 
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
-                        const void* w1, const void* wv, void* y, int32_t* ids, float* weights, float* save_xp,
-                        void* save_hacc, float* save_dot, float* save_qpre, float* save_bn, void* workspace,
-                        size_t workspace_bytes, int* dev_err, void* stream) {
+                        const void* w1, const void* wv, int expert_path, void* y, int32_t* ids, float* weights,
+                        float* save_xp, void* save_hacc, float* save_dot, float* save_qpre, float* save_bn,
+                        void* workspace, size_t workspace_bytes, int* dev_err, void* const* stage_events,
+                        void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (!x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !y || !ids || !weights || !workspace || !dev_err)
     return ETHOS_ERR_INVALID_ARG;
+  if (expert_path < 0 || expert_path > 2) return ETHOS_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(latents) ||
       !aligned16(w1) || !aligned16(wv) || !aligned16(y) || !aligned16(ids) || !aligned16(weights) ||
       !aligned16(workspace) || (save_xp && !aligned16(save_xp)) || (save_hacc && !aligned16(save_hacc)) ||
@@ -319,49 +400,41 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
     return ETHOS_ERR_ALIGNMENT;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
-  if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training)) return ETHOS_ERR_WORKSPACE;
   const ethos_dims& d = *dims;
+  const int path = resolve_expert_path(d, expert_path);
+  if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training, path)) return ETHOS_ERR_WORKSPACE;
   cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
   Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
   FwdScratch s;
   carve_forward(c, d, bn_training, save_xp == nullptr, save_hacc == nullptr, save_qpre == nullptr,
-                save_bn == nullptr, &s);
+                save_bn == nullptr, path == 2, &s);
   float* xp = save_xp ? save_xp : s.xp;
   __nv_bfloat16* hacc = save_hacc ? static_cast<__nv_bfloat16*>(save_hacc) : s.hacc;
   float* qpre = save_qpre ? save_qpre : s.qpre;
   float* sbn = save_bn ? save_bn : s.save_bn;
   const int T = static_cast<int>(d.tokens);
-
+  void* const* ev = stage_events;
+  mark(ev, ETHOS_STAGE_START, stream_);
   if ((st = router_core(d, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, true, xp, s, qpre,
-                        sbn, dev_err, stream_, *dev)) != ETHOS_OK)
+                        sbn, dev_err, stream_, *dev, ev)) != ETHOS_OK)
     return st;
-
-  // reordered experts
-  CUtensorMap tm_w1, tm_h, tm_v;
-  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tm_h, hacc, T, EX_DH, 128)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tm_v, wv, d.d_model, EX_DH, 256)) != ETHOS_OK) return st;
-  ExpertFwdArgs ea;
-  ea.latents = static_cast<const __nv_bfloat16*>(latents);
-  ea.ids = ids;
-  ea.w = weights;
-  ea.xp = xp;
-  ea.hacc = hacc;
-  ea.save_dot = save_dot;
-  ea.T = T;
-  ea.R = static_cast<int>(d.num_heads * d.top_k);
-  ea.N = static_cast<int>(d.num_experts);
-  const int grid = T < dev->sm_count ? T : dev->sm_count;
-  k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, stream_>>>(tm_w1, ea, dev_err);
-  if ((st = launch_status()) != ETHOS_OK) return st;
+  if ((st = run_experts(d, path, latents, w1, ids, weights, xp, hacc, save_dot, s.table, dev_err, stream_, *dev,
+                        ev)) != ETHOS_OK)
+    return st;
+  mark(ev, ETHOS_STAGE_EXPERTS, stream_);
 
   // y = hacc @ W_v / H   (model.py:332-341)
+  CUtensorMap tm_h, tm_v;
+  if ((st = make_tmap_bf16(&tm_h, hacc, T, EX_DH, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_v, wv, d.d_model, EX_DH, 256)) != ETHOS_OK) return st;
   EpiStoreBF16 ey;
   ey.out = static_cast<__nv_bfloat16*>(y);
   ey.ldo = d.d_model;
   ey.M = T;
   ey.scale = 1.0f / static_cast<float>(d.num_heads);
-  return launch_gemm(tm_h, tm_v, T, static_cast<int>(d.d_model), EX_DH, ey, dev_err, stream_, *dev);
+  st = launch_gemm(tm_h, tm_v, T, static_cast<int>(d.d_model), EX_DH, ey, dev_err, stream_, *dev);
+  mark(ev, ETHOS_STAGE_END, stream_);
+  return st;
 }
 
 int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
@@ -376,42 +449,33 @@ int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_ca
     return ETHOS_ERR_ALIGNMENT;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
-  if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training)) return ETHOS_ERR_WORKSPACE;
+  if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training, 1)) return ETHOS_ERR_WORKSPACE;
   Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
   FwdScratch s;
-  carve_forward(c, *dims, bn_training, false, false, save_qpre == nullptr, save_bn == nullptr, &s);
+  carve_forward(c, *dims, bn_training, false, false, save_qpre == nullptr, save_bn == nullptr, false, &s);
   float* qpre = save_qpre ? save_qpre : s.qpre;
   float* sbn = save_bn ? save_bn : s.save_bn;
   return router_core(*dims, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, false, nullptr,
                      s, qpre, sbn, dev_err, static_cast<cudaStream_t>(stream), *dev);
 }
 
-int ethos_expert_forward(const ethos_dims* dims, const void* latents, const void* w1, const int32_t* ids,
-                         const float* weights, const float* xp, void* hacc, float* dot, int* dev_err,
-                         void* stream) {
+int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* latents, const void* w1,
+                         const int32_t* ids, const float* weights, const float* xp, void* hacc, float* dot,
+                         void* workspace, size_t workspace_bytes, int* dev_err, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (!latents || !w1 || !ids || !weights || !xp || !hacc || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (expert_path < 0 || expert_path > 2) return ETHOS_ERR_INVALID_ARG;
   if (!aligned16(latents) || !aligned16(w1) || !aligned16(ids) || !aligned16(weights) || !aligned16(xp) ||
-      !aligned16(hacc))
+      !aligned16(hacc) || (workspace && !aligned16(workspace)))
     return ETHOS_ERR_ALIGNMENT;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
-  CUtensorMap tm_w1;
-  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
-  ExpertFwdArgs ea;
-  ea.latents = static_cast<const __nv_bfloat16*>(latents);
-  ea.ids = ids;
-  ea.w = weights;
-  ea.xp = xp;
-  ea.hacc = static_cast<__nv_bfloat16*>(hacc);
-  ea.save_dot = dot;
-  ea.T = static_cast<int>(dims->tokens);
-  ea.R = static_cast<int>(dims->num_heads * dims->top_k);
-  ea.N = static_cast<int>(dims->num_experts);
-  const int grid = ea.T < dev->sm_count ? ea.T : dev->sm_count;
-  k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tm_w1, ea, dev_err);
-  return launch_status();
+  const int path = resolve_expert_path(*dims, expert_path);
+  if (path == 2 && (workspace == nullptr || workspace_bytes < expert_table_bytes(*dims)))
+    return ETHOS_ERR_WORKSPACE;
+  return run_experts(*dims, path, latents, w1, ids, weights, xp, static_cast<__nv_bfloat16*>(hacc), dot,
+                     static_cast<__half*>(workspace), dev_err, static_cast<cudaStream_t>(stream), *dev);
 }
 
 int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* keys, int32_t* ids, float* weights,

@@ -1,12 +1,15 @@
 // Persistent tcgen05 GEMM  D[M, N] = A[M, K] * B[N, K]^T  (bf16 in, fp32 TMEM
 // accumulate) with a pluggable per-row epilogue.
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31;
+// warps 2-5 take columns 0-127 of the tile, warps 6-9 columns 128-255).
 // Tiles are 128 x 256 x 64 with a 4-stage TMA ring (48 KB per stage, 128-byte
 // swizzle) and two 256-column TMEM accumulators, so the epilogue of tile i
 // overlaps the main loop of tile i+1.
 #pragma once
+
+#include <cuda_fp16.h>
 
 #include "sm100.cuh"
 
@@ -19,7 +22,8 @@ constexpr int GEMM_STAGES = 4;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
 constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 320;
+constexpr int GEMM_EPI_THREADS = 256;
 
 struct GemmCtl {
   uint64_t full[GEMM_STAGES];
@@ -92,8 +96,9 @@ struct EpiStoreF32 {
 // Router query projection + token projection sharing one A operand (x):
 // columns [0, HQ) are the H heads' queries (query_projs, model.py:215),
 // columns [HQ, HQ + dh) are x_proj = x @ W_u (model.py:326).
-//  mode 0 (BatchNorm eval): q_hat = ((v + bias) - mean) * scale + shift is
-//    written as a bf16 hi/lo pair into the scoring operand
+//  mode 0 (BatchNorm eval): q_hat = v * scale + offset, with the bias and the
+//    running statistics folded into (scale, offset) per column, is written as
+//    a bf16 hi/lo pair into the scoring operand
 //    qs[(h*2 + half)][row][0..dq/2) = hi, [dq/2..dq) = lo.
 //  mode 1 (BatchNorm train): qpre[row][col] = v + bias (fp32) for the batch
 //    statistics pass.
@@ -104,8 +109,8 @@ struct EpiProj {
   int dq;
   int dh;
   int mode;
-  const float* bias;   // [HQ]
-  const float4* colp;  // [HQ] (unused, mean, scale, shift) for mode 0
+  const float* bias;    // [HQ]
+  const float2* colp;   // [HQ] (scale, offset) for mode 0
   __nv_bfloat16* qs;
   float* qpre;
   float* xp;
@@ -119,11 +124,11 @@ struct EpiProj {
     }
     if (mode == 1) {
       float4* dst = reinterpret_cast<float4*>(qpre + static_cast<int64_t>(row) * HQ + col);
+      const float4* b4 = reinterpret_cast<const float4*>(bias + col);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        dst[j] = make_float4(v[4 * j] + __ldg(bias + col + 4 * j), v[4 * j + 1] + __ldg(bias + col + 4 * j + 1),
-                             v[4 * j + 2] + __ldg(bias + col + 4 * j + 2),
-                             v[4 * j + 3] + __ldg(bias + col + 4 * j + 3));
+        const float4 b = __ldg(b4 + j);
+        dst[j] = make_float4(v[4 * j] + b.x, v[4 * j + 1] + b.y, v[4 * j + 2] + b.z, v[4 * j + 3] + b.w);
       }
       return;
     }
@@ -133,21 +138,18 @@ struct EpiProj {
     const int p = e >= half ? 1 : 0;
     const int i0 = e - p * half;
     __nv_bfloat16* base = qs + (static_cast<int64_t>(h * 2 + p) * M + row) * dq;
+    const float4* cp4 = reinterpret_cast<const float4*>(colp + col);
     uint32_t hi[16], lo[16];
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      float qn[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const float4 cp = __ldg(colp + col + i + u);
-        const float b = __ldg(bias + col + i + u);
-        qn[u] = ((v[i + u] + b) - cp.y) * cp.z + cp.w;
-      }
-      const __nv_bfloat162 h2 = __floats2bfloat162_rn(qn[0], qn[1]);
+    for (int i = 0; i < 16; ++i) {
+      const float4 c = __ldg(cp4 + i);
+      const float q0 = fmaf(v[2 * i], c.x, c.y);
+      const float q1 = fmaf(v[2 * i + 1], c.z, c.w);
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(q0, q1);
       const float2 hf = __bfloat1622float2(h2);
-      const __nv_bfloat162 l2 = __floats2bfloat162_rn(qn[0] - hf.x, qn[1] - hf.y);
-      hi[i >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
-      lo[i >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
+      const __nv_bfloat162 l2 = __floats2bfloat162_rn(q0 - hf.x, q1 - hf.y);
+      hi[i] = *reinterpret_cast<const uint32_t*>(&h2);
+      lo[i] = *reinterpret_cast<const uint32_t*>(&l2);
     }
     uint4* dh_ = reinterpret_cast<uint4*>(base + i0);
     uint4* dl_ = reinterpret_cast<uint4*>(base + half + i0);
@@ -155,6 +157,29 @@ struct EpiProj {
     for (int j = 0; j < 4; ++j) {
       dh_[j] = make_uint4(hi[4 * j], hi[4 * j + 1], hi[4 * j + 2], hi[4 * j + 3]);
       dl_[j] = make_uint4(lo[4 * j], lo[4 * j + 1], lo[4 * j + 2], lo[4 * j + 3]);
+    }
+  }
+};
+
+// Expert hidden table: out[row][col] = fp16(gelu_erf(v)) for the expert-
+// expansion GEMM E @ W1^T (row = expert id, col = hidden unit; model.py:323
+// evaluated once per expert instead of once per selection).
+struct EpiGeluF16 {
+  __half* out;
+  int64_t ldo;
+  int M;
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32]) const {
+    if (row >= M) return;
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ldo + col);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __half2 hh = __floats2half2_rn(gelu_erf(v[8 * j + 2 * u]), gelu_erf(v[8 * j + 2 * u + 1]));
+        w[u] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 };
@@ -181,7 +206,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->acc_full[b], 1);
-      mbar_init(&ctl->acc_empty[b], 128);
+      mbar_init(&ctl->acc_empty[b], GEMM_EPI_THREADS);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -266,6 +291,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int q = warp & 3;
+    const int ch = (warp - 2) >> 2;  // column half of the tile
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -277,7 +303,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < GEMM_BN / 32; ++c) {
+      for (int c = ch * 4; c < ch * 4 + 4; ++c) {
         float v[32];
         tmem_ld32(tmem_addr(tmem, q * 32, buf * GEMM_BN + c * 32), v);
         epi(row, n0 + c * 32, v);

@@ -10,11 +10,11 @@
 namespace ethos {
 
 // ----------------------------------------------------------- top-k lists --
-// Sorted-descending insertion into a register list of N entries.  Strict '>'
-// keeps the earlier of two equal scores first.
+// Branch-free sorted-descending insertion into a register list of N entries.
+// A score not above the last entry (or -inf) leaves the list unchanged; strict
+// '>' keeps the earlier of two equal scores first.
 template <int N>
 __device__ __forceinline__ void topk_insert(float (&v)[N], int (&ix)[N], float s, int id) {
-  if (!(s > v[N - 1])) return;
   bool c[N];
 #pragma unroll
   for (int j = 0; j < N; ++j) c[j] = s > v[j];
@@ -27,21 +27,52 @@ __device__ __forceinline__ void topk_insert(float (&v)[N], int (&ix)[N], float s
   ix[0] = c[0] ? id : ix[0];
 }
 
+// Folds 32 scores of this lane's row (s[i] for key key0 + i) into the list.
+// Candidates (scores above the current N-th best) are marked in a bitmask and
+// inserted in a warp-uniform loop that runs max-over-lanes(#candidates)
+// times; the chunk is staged in this warp's shared buffer `stage` ([i][lane]
+// layout, conflict-free) so each lane can fetch its i-th candidate.
+template <int N>
+__device__ __forceinline__ void topk_fold_chunk(float (&v)[N], int (&ix)[N], const float (&s)[32], int key0,
+                                                float* stage, int lane) {
+  const float thr = v[N - 1];
+  uint32_t mask = 0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) mask |= (s[i] > thr ? 1u : 0u) << i;
+  if (!__any_sync(0xffffffffu, mask != 0u)) return;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) stage[i * 32 + lane] = s[i];
+  __syncwarp();
+  while (__any_sync(0xffffffffu, mask != 0u)) {
+    const int i = mask ? __ffs(mask) - 1 : 0;
+    const float sv = mask ? stage[i * 32 + lane] : -INFINITY;
+    mask &= mask - 1u;
+    topk_insert<N>(v, ix, sv, key0 + i);
+  }
+  __syncwarp();
+}
+
 // ------------------------------------------------------ scoring + top-k --
 // One work item = (head h, tile of 128 tokens).  For each half p in {0, 1}
 // and each chunk of up to 256 sub-keys, the MMA warp computes
 //   S[t, key] = sum_c A[t, c] * B[key, c]
-// into one of two 256-column TMEM buffers while the 4 epilogue warps (one
-// token row per thread) fold the previous chunk into that row's top-k list.
+// into one of two 256-column TMEM buffers while 8 epilogue warps fold the
+// previous chunk into per-row top-k lists (warps 2-5 own keys 0-127 of each
+// chunk, warps 6-9 keys 128-255; one token row per thread).  At the end of an
+// item the second group hands its lists over shared memory to the first,
+// which merges them, forms the candidate grid, the softmax and the ids.
 // A rows come from the query operand tensor map at row
 // h*a_stride_h + p*a_stride_p + t and column offset p*a_col_p; B rows from
 // the key tensor map at p*K + key.  With the split-bf16 layout A = [hi | lo]
 // and B = [keys | keys], so S is the fp32 query . key product to ~2^-16.
-constexpr int ROUTER_THREADS = 192;
-constexpr int ROUTER_STAGES = 4;
+constexpr int ROUTER_THREADS = 320;
+constexpr int ROUTER_EPI_THREADS = 256;
+constexpr int ROUTER_STAGES = 3;
 constexpr int ROUTER_A_BYTES = 128 * 64 * 2;
 constexpr int ROUTER_B_BYTES_MAX = 256 * 64 * 2;
 constexpr int ROUTER_STAGE_BYTES = ROUTER_A_BYTES + ROUTER_B_BYTES_MAX;
+constexpr int ROUTER_CAND_BYTES = 8 * 32 * 32 * 4;      // per epilogue warp: 32 x 32 fp32
+constexpr int ROUTER_XCHG_BYTES = 2 * 2 * 16 * 128 * 4; // [value|id][half][16][128 rows]
 
 struct RouterCtl {
   uint64_t full[ROUTER_STAGES];
@@ -52,7 +83,10 @@ struct RouterCtl {
   uint32_t tmem_base;
   int abort;
 };
-constexpr int ROUTER_SMEM_BYTES = ROUTER_STAGES * ROUTER_STAGE_BYTES + 1024 + static_cast<int>(sizeof(RouterCtl));
+constexpr int ROUTER_OFF_CAND = ROUTER_STAGES * ROUTER_STAGE_BYTES;
+constexpr int ROUTER_OFF_XCHG = ROUTER_OFF_CAND + ROUTER_CAND_BYTES;
+constexpr int ROUTER_OFF_CTL = ROUTER_OFF_XCHG + ROUTER_XCHG_BYTES;
+constexpr int ROUTER_SMEM_BYTES = ROUTER_OFF_CTL + static_cast<int>(sizeof(RouterCtl)) + 1024;
 
 struct RouterGeom {
   int T;          // tokens
@@ -64,13 +98,17 @@ struct RouterGeom {
   int a_col_p;    // A column offset per half
 };
 
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 template <int TOPK>
 __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     k_score_topk(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RouterGeom g,
                  int32_t* __restrict__ ids_out, float* __restrict__ w_out, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  RouterCtl* ctl = reinterpret_cast<RouterCtl*>(smem + ROUTER_STAGES * ROUTER_STAGE_BYTES);
+  RouterCtl* ctl = reinterpret_cast<RouterCtl*>(smem + ROUTER_OFF_CTL);
   const int warp = warp_id();
   const int lane = lane_id();
   const int num_mt = (g.T + 127) / 128;
@@ -87,7 +125,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->acc_full[b], 1);
-      mbar_init(&ctl->acc_empty[b], 128);
+      mbar_init(&ctl->acc_empty[b], ROUTER_EPI_THREADS);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -177,12 +215,22 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
       }
     }
   } else {
+    // ----------------------------------------------------------- epilogue
+    // Every epilogue warp walks all items and hits both named barriers of
+    // each item, also after an abort (work is skipped, barriers are not).
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int kh = ew >> 2;  // which 128 keys of each 256-key chunk
+    const int row = q * 32 + lane;
+    float* stage = reinterpret_cast<float*>(smem + ROUTER_OFF_CAND) + ew * 32 * 32;
+    float* xv = reinterpret_cast<float*>(smem + ROUTER_OFF_XCHG);        // [2][16][128]
+    int* xi = reinterpret_cast<int*>(smem + ROUTER_OFF_XCHG) + 2 * 16 * 128;
     int it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < num_items; item += gridDim.x) {
+    bool first = true;
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       const int h = item / num_mt;
-      const int t = (item - h * num_mt) * 128 + q * 32 + lane;
+      const int t = (item - h * num_mt) * 128 + row;
       float lv[2][TOPK];
       int li[2][TOPK];
 #pragma unroll
@@ -195,62 +243,78 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
         for (int nc = 0; nc < num_chunks; ++nc, ++it) {
           const int buf = it & 1;
           const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
-          const bool got = mbar_wait(&ctl->acc_full[buf], acc_phase, abort, err, 14);
-          if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            break;
-          }
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], acc_phase, abort, err, 14));
+          if (!ok) continue;
           tc_fence_after();
           const int valid = min(256, g.K - nc * 256);
 #pragma unroll 1
-          for (int c = 0; c < valid / 32; ++c) {
-            float s[32];
-            tmem_ld32(tmem_addr(tmem, q * 32, buf * 256 + c * 32), s);
-            const int key0 = nc * 256 + c * 32;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) topk_insert<TOPK>(lv[p], li[p], s[i], key0 + i);
+          for (int c = kh * 4; c < kh * 4 + 4; ++c) {
+            if (c * 32 >= valid) break;
+            float sc[32];
+            tmem_ld32(tmem_addr(tmem, q * 32, buf * 256 + c * 32), sc);
+            topk_fold_chunk<TOPK>(lv[p], li[p], sc, nc * 256 + c * 32, stage, lane);
           }
           tc_fence_before();
           mbar_arrive(&ctl->acc_empty[buf]);
         }
-        if (!ok) break;
       }
-      if (!ok) break;
-      // Top-k of the candidate grid lv[0][i] + lv[1][j].  Only pairs with
-      // (i+1)(j+1) <= TOPK can rank in the top TOPK (every (i', j') with
-      // i' <= i, j' <= j scores at least as high), so only those are scanned.
-      float fv[TOPK];
-      int fid[TOPK];
+      // hand the second key group's lists to the first
+      const bool more = item + static_cast<int>(gridDim.x) < num_items;
+      if (kh == 1) {
+        if (!first) named_bar_sync(2, ROUTER_EPI_THREADS);  // previous item's lists were read
 #pragma unroll
-      for (int j = 0; j < TOPK; ++j) {
-        fv[j] = -INFINITY;
-        fid[j] = 0;
-      }
+        for (int p = 0; p < 2; ++p)
 #pragma unroll
-      for (int i = 0; i < TOPK; ++i) {
+          for (int j = 0; j < TOPK; ++j) {
+            xv[(p * 16 + j) * 128 + row] = lv[p][j];
+            xi[(p * 16 + j) * 128 + row] = li[p][j];
+          }
+        named_bar_sync(1, ROUTER_EPI_THREADS);
+      } else {
+        named_bar_sync(1, ROUTER_EPI_THREADS);
 #pragma unroll
-        for (int j = 0; (i + 1) * (j + 1) <= TOPK; ++j) {
-          topk_insert<TOPK>(fv, fid, lv[0][i] + lv[1][j], li[0][i] * g.K + li[1][j]);
-        }
-      }
-      if (t < g.T) {
-        // fp32 softmax over the selected scores (model.py:234)
-        float e[TOPK];
-        float sum = 0.f;
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int j = 0; j < TOPK; ++j)
+            topk_insert<TOPK>(lv[p], li[p], xv[(p * 16 + j) * 128 + row], xi[(p * 16 + j) * 128 + row]);
+        if (more) named_bar_arrive(2, ROUTER_EPI_THREADS);
+        // Top-k of the candidate grid lv[0][i] + lv[1][j].  Only pairs with
+        // (i+1)(j+1) <= TOPK can rank in the top TOPK (every (i', j') with
+        // i' <= i, j' <= j scores at least as high), so only those are scanned.
+        float fv[TOPK];
+        int fid[TOPK];
 #pragma unroll
         for (int j = 0; j < TOPK; ++j) {
-          e[j] = expf(fv[j] - fv[0]);
-          sum += e[j];
+          fv[j] = -INFINITY;
+          fid[j] = 0;
         }
-        const int64_t o = (static_cast<int64_t>(t) * g.H + h) * TOPK;
-        int4* di = reinterpret_cast<int4*>(ids_out + o);
-        float4* dw = reinterpret_cast<float4*>(w_out + o);
 #pragma unroll
-        for (int j = 0; j < TOPK / 4; ++j) {
-          di[j] = make_int4(fid[4 * j], fid[4 * j + 1], fid[4 * j + 2], fid[4 * j + 3]);
-          dw[j] = make_float4(e[4 * j] / sum, e[4 * j + 1] / sum, e[4 * j + 2] / sum, e[4 * j + 3] / sum);
+        for (int i = 0; i < TOPK; ++i) {
+#pragma unroll
+          for (int j = 0; (i + 1) * (j + 1) <= TOPK; ++j) {
+            topk_insert<TOPK>(fv, fid, lv[0][i] + lv[1][j], li[0][i] * g.K + li[1][j]);
+          }
+        }
+        if (ok && t < g.T) {
+          // fp32 softmax over the selected scores (model.py:234)
+          float e[TOPK];
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < TOPK; ++j) {
+            e[j] = expf(fv[j] - fv[0]);
+            sum += e[j];
+          }
+          const int64_t o = (static_cast<int64_t>(t) * g.H + h) * TOPK;
+          int4* di = reinterpret_cast<int4*>(ids_out + o);
+          float4* dw = reinterpret_cast<float4*>(w_out + o);
+#pragma unroll
+          for (int j = 0; j < TOPK / 4; ++j) {
+            di[j] = make_int4(fid[4 * j], fid[4 * j + 1], fid[4 * j + 2], fid[4 * j + 3]);
+            dw[j] = make_float4(e[4 * j] / sum, e[4 * j + 1] / sum, e[4 * j + 2] / sum, e[4 * j + 3] / sum);
+          }
         }
       }
+      first = false;
     }
   }
   __syncthreads();
@@ -286,12 +350,12 @@ __global__ void k_bn_partial(const float* __restrict__ qpre, int T, int C, float
 
 // Combines the slab sums (in double), writes the batch mean and 1/sqrt(var +
 // eps) (biased variance, as BatchNorm1d normalises), the fused per-column
-// (bias, mean, scale, shift) for the normalisation pass, and updates the
-// running statistics with the unbiased variance.
+// (scale, offset) of the normalisation pass, and updates the running
+// statistics with the unbiased variance.
 __global__ void k_bn_finalize(const float* __restrict__ qpre, const float* __restrict__ part, int T, int C,
                               int slabs, const float* __restrict__ gamma, const float* __restrict__ beta,
                               float* __restrict__ run_mean, float* __restrict__ run_var, float eps,
-                              float momentum, float* __restrict__ save_bn, float4* __restrict__ colp) {
+                              float momentum, float* __restrict__ save_bn, float2* __restrict__ colp) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= C) return;
   double s = 0.0, ss = 0.0;
@@ -307,24 +371,27 @@ __global__ void k_bn_finalize(const float* __restrict__ qpre, const float* __res
   const float invstd = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
   save_bn[col] = mean;
   save_bn[C + col] = invstd;
-  colp[col] = make_float4(0.f, mean, invstd * gamma[col], beta[col]);
+  const float scale = invstd * gamma[col];
+  colp[col] = make_float2(scale, beta[col] - mean * scale);
   const double unbiased = T > 1 ? var * T / (T - 1) : var;
   run_mean[col] = (1.f - momentum) * run_mean[col] + momentum * mean;
   run_var[col] = (1.f - momentum) * run_var[col] + momentum * static_cast<float>(unbiased);
 }
 
-// Eval-mode fused column parameters from the running statistics.
-__global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, float4* __restrict__ colp) {
+// Eval-mode per-column (scale, offset) from the bias and running statistics:
+// ((v + bias) - rm) * gamma / sqrt(rv + eps) + beta = v * scale + offset.
+__global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, float2* __restrict__ colp) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= C) return;
-  const float gamma = bn[1 * C + col], beta = bn[2 * C + col];
+  const float bias = bn[col], gamma = bn[1 * C + col], beta = bn[2 * C + col];
   const float rm = bn[3 * C + col], rv = bn[4 * C + col];
-  colp[col] = make_float4(0.f, rm, gamma / sqrtf(rv + eps), beta);
+  const float scale = gamma / sqrtf(rv + eps);
+  colp[col] = make_float2(scale, beta - (rm - bias) * scale);
 }
 
 // Normalisation pass of training mode: qpre [T, C] -> split-bf16 scoring
 // operand qs[(h*2 + p)][t][hi | lo].  One thread per 8 consecutive columns.
-__global__ void k_bn_apply(const float* __restrict__ qpre, const float4* __restrict__ colp, int T, int H, int dq,
+__global__ void k_bn_apply(const float* __restrict__ qpre, const float2* __restrict__ colp, int T, int H, int dq,
                            __nv_bfloat16* __restrict__ qs) {
   const int C = H * dq;
   const int groups = C / 8;
@@ -346,8 +413,8 @@ __global__ void k_bn_apply(const float* __restrict__ qpre, const float4* __restr
     float qn[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const float4 cp = colp[col + i + u];
-      qn[u] = (v[i + u] - cp.y) * cp.z + cp.w;
+      const float2 cp = colp[col + i + u];
+      qn[u] = fmaf(v[i + u], cp.x, cp.y);
     }
     const __nv_bfloat162 h2 = __floats2bfloat162_rn(qn[0], qn[1]);
     const float2 hf = __bfloat1622float2(h2);

@@ -150,7 +150,7 @@ class _EthosLayerFunction(torch.autograd.Function):
         training = layer.router._bn_training()
         need_grad = any(ctx.needs_input_grad)
         x16 = x2d.to(torch.bfloat16).contiguous()
-        out = ops.layer_forward(x16, pw, training, eps, mom, save=need_grad)
+        out = ops.layer_forward(x16, pw, training, eps, mom, save=need_grad, path=layer.expert_path)
         if training:
             layer.router._write_back_running(pw.bn)
         ctx.layer = layer
@@ -183,6 +183,10 @@ class EthosExpertLayer(nn.Module):
         self.expert_latents = nn.Embedding(dims["num_experts"], dims["d_latent"])
         self.generation_network = ExpertGenerationNetwork(dims["d_latent"], dims["d_model"], dims["d_hidden"])
         self.router = ProductKeyRouter(config)
+        # expert execution path (ops.EXPERT_AUTO / EXPERT_FUSED / EXPERT_TABLE):
+        # AUTO evaluates gelu(E @ W1^T) once per expert when a step makes at
+        # least one selection per expert on average, else per selection
+        self.expert_path = ops.EXPERT_AUTO
         self._cache_key = None
         self._cache = None
 

@@ -27,6 +27,19 @@ def _stream(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _events(evs):
+    """ctypes array of raw cudaEvent_t handles (events are created on first
+    record, so each is recorded once here if it has no handle yet)."""
+    if evs is None:
+        return None
+    handles = []
+    for e in evs:
+        if e.cuda_event == 0:
+            e.record()
+        handles.append(e.cuda_event)
+    return (ctypes.c_void_p * len(handles))(*handles)
+
+
 def _require_cuda(t, name):
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor: the ETHOS B200 layer has no CPU path")
@@ -95,19 +108,27 @@ def product_key_topk(q, keys, top_k):
     return w, ids
 
 
-def expert_forward(latents, w1, ids, weights, xp, dims, save_dot=False):
+EXPERT_AUTO, EXPERT_FUSED, EXPERT_TABLE = 0, 1, 2
+
+
+def expert_forward(latents, w1, ids, weights, xp, dims, save_dot=False, path=EXPERT_AUTO):
     """Experts alone on given routing decisions: returns ``(hacc bf16 [T, dh],
-    dot fp32 [T, H*k] or None)``.  ``ids`` int32 / ``weights`` fp32 ``[T, H, k]``."""
+    dot fp32 [T, H*k] or None)``.  ``ids`` int32 / ``weights`` fp32 ``[T, H, k]``.
+    ``path``: EXPERT_FUSED (per token), EXPERT_TABLE (per-expert hidden
+    table) or EXPERT_AUTO."""
     _require_cuda(ids, "ids")
     T = ids.shape[0]
     ed = make_dims(T, dims)
+    L = lib()
     hacc = torch.empty((T, dims["d_hidden"]), dtype=torch.bfloat16, device=ids.device)
     dot = (torch.empty((T, dims["num_heads"] * dims["top_k"]), dtype=torch.float32, device=ids.device)
            if save_dot else None)
+    ws_bytes = L.ethos_expert_workspace_size(ctypes.byref(ed), int(path))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=ids.device)
     err = device_error_word(ids.device)
-    check(lib().ethos_expert_forward(ctypes.byref(ed), _vp(latents), _vp(w1), _vp(ids.contiguous()),
-                                     _vp(weights.contiguous()), _vp(xp.contiguous()), _vp(hacc), _vp(dot),
-                                     _vp(err), _stream(ids.device)), "ethos_expert_forward")
+    check(L.ethos_expert_forward(ctypes.byref(ed), int(path), _vp(latents), _vp(w1), _vp(ids.contiguous()),
+                                 _vp(weights.contiguous()), _vp(xp.contiguous()), _vp(hacc), _vp(dot), _vp(ws),
+                                 ws_bytes, _vp(err), _stream(ids.device)), "ethos_expert_forward")
     return hacc, dot
 
 
@@ -133,7 +154,7 @@ def router_forward(x2d, pw, bn_training, eps, momentum, save_qpre=None, save_bn=
     T = x2d.shape[0]
     dims = make_dims(T, d)
     L = lib()
-    ws_bytes = L.ethos_forward_workspace_size(ctypes.byref(dims), 1 if bn_training else 0)
+    ws_bytes = L.ethos_forward_workspace_size(ctypes.byref(dims), 1 if bn_training else 0, EXPERT_FUSED)
     if ws_bytes == 0:
         check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2d.device)
@@ -147,16 +168,21 @@ def router_forward(x2d, pw, bn_training, eps, momentum, save_qpre=None, save_bn=
     return w, ids
 
 
-def layer_forward(x2d, pw, bn_training, eps, momentum, save=False):
+STAGES = ("start", "projection", "batchnorm", "topk", "expert_table", "experts", "end")
+
+
+def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_AUTO, stage_events=None):
     """Router + experts.  Returns a dict with ``y`` (bf16 [T, d]), ``ids``,
-    ``weights`` and, when ``save``, the tensors the backward pass needs."""
+    ``weights`` and, when ``save``, the tensors the backward pass needs.
+    ``stage_events``: optional list of len(STAGES) ``torch.cuda.Event`` that
+    the library records at each stage boundary (per-kernel timing)."""
     _require_cuda(x2d, "x")
     d = pw.dims
     T = x2d.shape[0]
     dev = x2d.device
     dims = make_dims(T, d)
     L = lib()
-    ws_bytes = L.ethos_forward_workspace_size(ctypes.byref(dims), 1 if bn_training else 0)
+    ws_bytes = L.ethos_forward_workspace_size(ctypes.byref(dims), 1 if bn_training else 0, int(path))
     if ws_bytes == 0:
         check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
@@ -177,8 +203,10 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False):
     err = device_error_word(dev)
     check(L.ethos_layer_forward(ctypes.byref(dims), _vp(x2d), _vp(pw.w_cat), _vp(pw.bn), float(eps),
                                 float(momentum), 1 if bn_training else 0, _vp(pw.key_cat), _vp(pw.latents),
-                                _vp(pw.w1), _vp(pw.wv), _vp(out["y"]), _vp(out["ids"]), _vp(out["weights"]),
+                                _vp(pw.w1), _vp(pw.wv), int(path), _vp(out["y"]), _vp(out["ids"]),
+                                _vp(out["weights"]),
                                 _vp(g("xp")), _vp(g("hacc")), _vp(g("dot")), _vp(g("qpre")),
-                                _vp(g("bn_stats")), _vp(ws), ws_bytes, _vp(err), _stream(dev)),
+                                _vp(g("bn_stats")), _vp(ws), ws_bytes, _vp(err), _events(stage_events),
+                                _stream(dev)),
           "ethos_layer_forward")
     return out

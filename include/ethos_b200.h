@@ -75,8 +75,31 @@ int ethos_read_device_error(int* dev_err, int* host_code, int reset, void* strea
 int ethos_check_dims(const ethos_dims* dims);
 
 /* --------------------------------------------------------- forward -- */
+/* Expert execution paths (argument `expert_path`):
+ *  1 = fused per token: gather the selected latent rows, expand them on
+ *      tcgen05 and apply GELU in the epilogue (no scratch);
+ *  2 = expert table: expand + GELU once per expert into an fp16 [N, dh]
+ *      table (scratch), then gather hidden rows per token;
+ *  0 = automatic: the table once tokens*heads*top_k >= num_experts. */
+#define ETHOS_EXPERT_AUTO 0
+#define ETHOS_EXPERT_FUSED 1
+#define ETHOS_EXPERT_TABLE 2
+
+/* Stage boundaries of ethos_layer_forward (indices into stage_events). */
+#define ETHOS_STAGE_START 0
+#define ETHOS_STAGE_PROJECTION 1   /* after the query + x_proj GEMM            */
+#define ETHOS_STAGE_BATCHNORM 2    /* after the training-mode BatchNorm kernels */
+#define ETHOS_STAGE_TOPK 3         /* after scoring + top-k + softmax           */
+#define ETHOS_STAGE_EXPERT_TABLE 4 /* after the expert-table GEMM (table path)  */
+#define ETHOS_STAGE_EXPERTS 5      /* after the per-token expert kernel         */
+#define ETHOS_STAGE_END 6          /* after the W_v up-projection GEMM          */
+#define ETHOS_STAGE_COUNT 7
+
 /* Scratch bytes needed by ethos_layer_forward / ethos_router_forward. */
-size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training);
+size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training, int expert_path);
+
+/* Scratch bytes needed by ethos_expert_forward. */
+size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path);
 
 /* Router + reordered expert forward of one layer.
  *
@@ -98,9 +121,13 @@ size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training);
  *  latents   bf16 [N, dl]   expert_latents.weight
  *  w1        bf16 [dh, dl]  generation_network.net.0.weight
  *  wv        bf16 [d, dh]   generation_network.net.2.weight[d:]
+ *  expert_path  ETHOS_EXPERT_AUTO / _FUSED / _TABLE (see above)
  *  y         bf16 [T, d]    output (already divided by H, model.py:341)
  *  ids       int32 [T, H, k] selected expert ids (i1*K + i2, model.py:245)
  *  weights   fp32 [T, H, k]  softmax routing weights (model.py:234, fp32)
+ *  stage_events  optional (may be NULL) array of ETHOS_STAGE_COUNT cudaEvent_t:
+ *            event i is recorded on `stream` at stage boundary i (below), so a
+ *            caller can time each kernel of the real call with no extra sync
  *  save_*    optional (may be NULL) tensors kept for the backward pass:
  *            save_xp fp32 [T, dh] (x @ W_u), save_hacc bf16 [T, dh]
  *            (sum_{h,k} a*h), save_dot fp32 [T, H*k] (h . x_proj),
@@ -109,10 +136,10 @@ size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training);
  */
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
-                        const void* w1, const void* wv, void* y, int32_t* ids, float* weights,
-                        float* save_xp, void* save_hacc, float* save_dot, float* save_qpre,
-                        float* save_bn, void* workspace, size_t workspace_bytes, int* dev_err,
-                        void* stream);
+                        const void* w1, const void* wv, int expert_path, void* y, int32_t* ids,
+                        float* weights, float* save_xp, void* save_hacc, float* save_dot,
+                        float* save_qpre, float* save_bn, void* workspace, size_t workspace_bytes,
+                        int* dev_err, void* const* stage_events, void* stream);
 
 /* Router alone: ProductKeyRouter.forward (model.py:208-254) on x [T, d]
  * (bf16).  Arguments as for ethos_layer_forward; w_cat needs only its first
@@ -128,11 +155,13 @@ int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_ca
  *  weights fp32 [T, H*k]; xp fp32 [T, dh] (x @ W_u)
  *  hacc   bf16 [T, dh] out: sum_{h,k} gelu(h.xp)*w*h;  dot fp32 [T, H*k] out
  *         (optional, may be NULL)
+ *  workspace: ethos_expert_workspace_size() bytes (the fp16 expert table for
+ *         the table path; may be NULL for the fused path)
  * Ids outside [0, N) are not dereferenced: they set ETHOS_ERR_ID_OUT_OF_RANGE
- * in dev_err and gather row 0 instead. */
-int ethos_expert_forward(const ethos_dims* dims, const void* latents, const void* w1, const int32_t* ids,
-                         const float* weights, const float* xp, void* hacc, float* dot, int* dev_err,
-                         void* stream);
+ * in dev_err and read row 0 instead. */
+int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* latents, const void* w1,
+                         const int32_t* ids, const float* weights, const float* xp, void* hacc, float* dot,
+                         void* workspace, size_t workspace_bytes, int* dev_err, void* stream);
 
 /* Product-key top-k from already normalised queries (the scoring, per-half
  * top-k, candidate-grid top-k, softmax and id decode of model.py:217-245).

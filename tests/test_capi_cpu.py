@@ -76,19 +76,28 @@ def test_check_dims(L, kw, ok):
 
 def test_workspace_size(L):
     d = _dims()
-    ev = L.ethos_forward_workspace_size(ctypes.byref(d), 0)
-    tr = L.ethos_forward_workspace_size(ctypes.byref(d), 1)
-    T, H, dq, dh = 16384, 8, 512, 512
+    T, H, dq, dh, N = 16384, 8, 512, 512, 512 * 512
+    ev = L.ethos_forward_workspace_size(ctypes.byref(d), 0, 1)
+    tr = L.ethos_forward_workspace_size(ctypes.byref(d), 1, 1)
+    tab = L.ethos_forward_workspace_size(ctypes.byref(d), 0, 2)
+    auto = L.ethos_forward_workspace_size(ctypes.byref(d), 0, 0)
     assert ev >= H * 2 * T * dq * 2 + T * dh * (4 + 2)
     assert tr >= ev + T * H * dq * 4
+    assert tab >= ev + N * dh * 2
+    assert auto == tab  # 16384 * 128 selections >= 262144 experts: table path
+    small = _dims(tokens=64)
+    assert L.ethos_forward_workspace_size(ctypes.byref(small), 0, 0) == \
+        L.ethos_forward_workspace_size(ctypes.byref(small), 0, 1)
+    assert L.ethos_expert_workspace_size(ctypes.byref(d), 2) >= N * dh * 2
+    assert L.ethos_expert_workspace_size(ctypes.byref(d), 1) < 4096
     bad = _dims(top_k=32)
-    assert L.ethos_forward_workspace_size(ctypes.byref(bad), 0) == 0
+    assert L.ethos_forward_workspace_size(ctypes.byref(bad), 0, 0) == 0
 
 
 def test_null_arguments_rejected_without_gpu(L):
     d = _dims()
-    st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None,
-                               None, None, None, None, None, None, None, None, None, 0, None, None)
+    st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None, 0,
+                               None, None, None, None, None, None, None, None, None, 0, None, None, None)
     assert st == 1  # ETHOS_ERR_INVALID_ARG
 
 
