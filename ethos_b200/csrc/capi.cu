@@ -60,6 +60,8 @@ int device_info(DeviceInfo** out) {
           cudaSuccess;
     ok &= cudaFuncSetAttribute(k_expert_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, EX_SMEM_BYTES) ==
           cudaSuccess;
+    ok &= cudaFuncSetAttribute(k_expert_gather, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GATHER_SMEM_BYTES) == cudaSuccess;
     if (!ok) return ETHOS_ERR_CUDA;
     d.attrs_set = true;
   }
@@ -192,9 +194,11 @@ int check_dims_impl(const ethos_dims* d) {
 // expert, then gather hidden rows per token).  0 picks the table once the
 // step makes at least one selection per expert on average.
 int resolve_expert_path(const ethos_dims& d, int path) {
-  if (path == 1 || path == 2) return path;
-  const int64_t sel = d.tokens * d.num_heads * d.top_k;
-  return sel >= d.num_experts ? 2 : 1;
+  if (path == 1) return 1;
+  if (path == 2) return d.num_heads * d.top_k >= 16 ? 2 : 1;
+  const int64_t R = d.num_heads * d.top_k;
+  const int64_t sel = d.tokens * R;
+  return (sel >= d.num_experts && R >= 16) ? 2 : 1;
 }
 
 size_t expert_table_bytes(const ethos_dims& d) {
@@ -237,11 +241,10 @@ int run_experts(const ethos_dims& d, int path, const void* latents, const void* 
   if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
   mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
   // phase B: per-token gather, dot, activation, weighted sum
-  const int warps_needed = T;
-  int blocks = (warps_needed + (GATHER_THREADS / 32) - 1) / (GATHER_THREADS / 32);
-  const int max_blocks = dev.sm_count * 2;
-  if (blocks > max_blocks) blocks = max_blocks;
-  k_expert_gather<<<blocks, GATHER_THREADS, 0, stream>>>(table, ids, weights, xp, hacc, dot, T, R, N, err);
+  int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
+  if (blocks > dev.sm_count) blocks = dev.sm_count;
+  k_expert_gather<<<blocks, GATHER_THREADS, GATHER_SMEM_BYTES, stream>>>(table, ids, weights, xp, hacc, dot, T, R,
+                                                                         N, err);
   return launch_status();
 }
 

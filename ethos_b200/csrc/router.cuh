@@ -27,52 +27,96 @@ __device__ __forceinline__ void topk_insert(float (&v)[N], int (&ix)[N], float s
   ix[0] = c[0] ? id : ix[0];
 }
 
-// Folds 32 scores of this lane's row (s[i] for key key0 + i) into the list.
-// Candidates (scores above the current N-th best) are marked in a bitmask and
-// inserted in a warp-uniform loop that runs max-over-lanes(#candidates)
-// times; the chunk is staged in this warp's shared buffer `stage` ([i][lane]
-// layout, conflict-free) so each lane can fetch its i-th candidate.
-template <int N>
-__device__ __forceinline__ void topk_fold_chunk(float (&v)[N], int (&ix)[N], const float (&s)[32], int key0,
-                                                float* stage, int lane) {
+// Folds 32 scores of this lane's row (s[i] for key key0 + i) into the list,
+// considering only scores >= tau.  Candidates (>= tau and above the current
+// N-th best) are marked in a bitmask and inserted in a warp-uniform loop that
+// runs max-over-lanes(#candidates) times; the chunk is staged in this warp's
+// shared buffer `stage` ([i][lane] layout, conflict-free) so each lane can
+// fetch its i-th candidate.
+template <int N, bool kExplicitIds>
+__device__ __forceinline__ void topk_fold_chunk(float (&v)[N], int (&ix)[N], const float (&s)[32], const int* id,
+                                                int key0, float tau, float* stage, int* stage_id, int lane) {
   const float thr = v[N - 1];
   uint32_t mask = 0;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) mask |= (s[i] > thr ? 1u : 0u) << i;
+  for (int i = 0; i < 32; ++i) mask |= ((s[i] >= tau && s[i] > thr) ? 1u : 0u) << i;
   if (!__any_sync(0xffffffffu, mask != 0u)) return;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) stage[i * 32 + lane] = s[i];
+  for (int i = 0; i < 32; ++i) {
+    stage[i * 32 + lane] = s[i];
+    if (kExplicitIds) stage_id[i * 32 + lane] = id[i];
+  }
   __syncwarp();
   while (__any_sync(0xffffffffu, mask != 0u)) {
     const int i = mask ? __ffs(mask) - 1 : 0;
     const float sv = mask ? stage[i * 32 + lane] : -INFINITY;
+    const int si = kExplicitIds ? stage_id[i * 32 + lane] : key0 + i;
     mask &= mask - 1u;
-    topk_insert<N>(v, ix, sv, key0 + i);
+    topk_insert<N>(v, ix, sv, si);
   }
   __syncwarp();
 }
 
+// N-th largest of the 2N values a[0..N) and b[0..N) (N a power of two): sort
+// both descending with a bitonic network, then the N-th largest of the union
+// is min_i max(a[i], b[N-1-i]).
+template <int N>
+__device__ __forceinline__ void bitonic_sort_desc(float (&a)[N]) {
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const bool desc = (i & k) == 0;
+          const float x = a[i], y = a[l];
+          a[i] = desc ? fmaxf(x, y) : fminf(x, y);
+          a[l] = desc ? fminf(x, y) : fmaxf(x, y);
+        }
+      }
+    }
+  }
+}
+template <int N>
+__device__ __forceinline__ float nth_largest_of_union(float (&a)[N], float (&b)[N]) {
+  bitonic_sort_desc<N>(a);
+  bitonic_sort_desc<N>(b);
+  float t = INFINITY;
+#pragma unroll
+  for (int i = 0; i < N; ++i) t = fminf(t, fmaxf(a[i], b[N - 1 - i]));
+  return t;
+}
+
 // ------------------------------------------------------ scoring + top-k --
-// One work item = (head h, tile of 128 tokens).  For each half p in {0, 1}
-// and each chunk of up to 256 sub-keys, the MMA warp computes
-//   S[t, key] = sum_c A[t, c] * B[key, c]
-// into one of two 256-column TMEM buffers while 8 epilogue warps fold the
-// previous chunk into per-row top-k lists (warps 2-5 own keys 0-127 of each
-// chunk, warps 6-9 keys 128-255; one token row per thread).  At the end of an
-// item the second group hands its lists over shared memory to the first,
-// which merges them, forms the candidate grid, the softmax and the ids.
-// A rows come from the query operand tensor map at row
-// h*a_stride_h + p*a_stride_p + t and column offset p*a_col_p; B rows from
-// the key tensor map at p*K + key.  With the split-bf16 layout A = [hi | lo]
-// and B = [keys | keys], so S is the fp32 query . key product to ~2^-16.
+// One work item = (head h, tile of 128 tokens); per item two halves p, per
+// half the sub-keys in units of up to 256 (TMEM buffer = unit parity).
+// The MMA warp computes S[t, key] = sum_c A[t, c] * B[key, c] into the
+// unit's 256-column TMEM buffer; 8 epilogue warps (one token row per thread,
+// group kh = 0/1 owning the first/second 256 keys of a half) select the
+// half's top-k per row exactly in three steps:
+//   1. maxima of the 16-key groups of the row (one FMNMX per score);
+//   2. tau = k-th largest of those 32 maxima (a lower bound on the k-th
+//      largest score, since the maxima are k+ distinct scores of the row);
+//   3. fold only scores >= tau into a sorted register list (the threshold
+//      leaves ~20 candidates per 512 keys instead of ~150).
+// Group 1 then hands its list to group 0, which merges the two, and after
+// both halves forms the candidate grid, the fp32 softmax and the ids.  A
+// rows come from the query tensor map at h*a_stride_h + p*a_stride_p + t,
+// column offset p*a_col_p; B rows from the key tensor map at p*K + key.
+// With the split-bf16 layout A = [hi | lo] and B = [keys | keys], so S is the
+// fp32 query . key product to ~2^-16.
 constexpr int ROUTER_THREADS = 320;
-constexpr int ROUTER_EPI_THREADS = 256;
 constexpr int ROUTER_STAGES = 3;
 constexpr int ROUTER_A_BYTES = 128 * 64 * 2;
 constexpr int ROUTER_B_BYTES_MAX = 256 * 64 * 2;
 constexpr int ROUTER_STAGE_BYTES = ROUTER_A_BYTES + ROUTER_B_BYTES_MAX;
-constexpr int ROUTER_CAND_BYTES = 8 * 32 * 32 * 4;      // per epilogue warp: 32 x 32 fp32
-constexpr int ROUTER_XCHG_BYTES = 2 * 2 * 16 * 128 * 4; // [value|id][half][16][128 rows]
+// candidate staging: 32 x 32 fp32 scores per epilogue warp, plus 32 x 32 int
+// ids for the 4 warps of group 0 (merges and the candidate grid)
+constexpr int ROUTER_CAND_BYTES = 8 * 32 * 32 * 4 + 4 * 32 * 32 * 4;
+constexpr int ROUTER_XMAX_BYTES = 2 * 16 * 128 * 4;     // [group][16 maxima][128 rows]
+constexpr int ROUTER_XLIST_BYTES = 2 * 16 * 128 * 4;    // [value|id][16][128 rows]
 
 struct RouterCtl {
   uint64_t full[ROUTER_STAGES];
@@ -84,8 +128,9 @@ struct RouterCtl {
   int abort;
 };
 constexpr int ROUTER_OFF_CAND = ROUTER_STAGES * ROUTER_STAGE_BYTES;
-constexpr int ROUTER_OFF_XCHG = ROUTER_OFF_CAND + ROUTER_CAND_BYTES;
-constexpr int ROUTER_OFF_CTL = ROUTER_OFF_XCHG + ROUTER_XCHG_BYTES;
+constexpr int ROUTER_OFF_XMAX = ROUTER_OFF_CAND + ROUTER_CAND_BYTES;
+constexpr int ROUTER_OFF_XLIST = ROUTER_OFF_XMAX + ROUTER_XMAX_BYTES;
+constexpr int ROUTER_OFF_CTL = ROUTER_OFF_XLIST + ROUTER_XLIST_BYTES;
 constexpr int ROUTER_SMEM_BYTES = ROUTER_OFF_CTL + static_cast<int>(sizeof(RouterCtl)) + 1024;
 
 struct RouterGeom {
@@ -113,8 +158,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
   const int lane = lane_id();
   const int num_mt = (g.T + 127) / 128;
   const int num_items = g.H * num_mt;
-  const int box_rows = g.K < 256 ? g.K : 256;   // keys per chunk (TMA box rows, MMA N)
-  const int num_chunks = (g.K + 255) / 256;
+  const int box_rows = g.K < 256 ? g.K : 256;   // keys per unit (TMA box rows, MMA N)
+  const int num_chunks = (g.K + 255) / 256;     // units per half (1 or 2)
   const int num_kb = g.KA / 64;
   const uint32_t stage_tx = ROUTER_A_BYTES + box_rows * 128;
 
@@ -125,7 +170,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->acc_full[b], 1);
-      mbar_init(&ctl->acc_empty[b], ROUTER_EPI_THREADS);
+      mbar_init(&ctl->acc_empty[b], 128);  // one warp group (4 warps) consumes a unit
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -216,105 +261,204 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    // Every epilogue warp walks all items and hits both named barriers of
-    // each item, also after an abort (work is skipped, barriers are not).
+    // Every participating warp walks all items and hits every named barrier,
+    // also after an abort (work is skipped, barriers are not).
     const int ew = warp - 2;
     const int q = warp & 3;
-    const int kh = ew >> 2;  // which 128 keys of each 256-key chunk
-    const int row = q * 32 + lane;
-    float* stage = reinterpret_cast<float*>(smem + ROUTER_OFF_CAND) + ew * 32 * 32;
-    float* xv = reinterpret_cast<float*>(smem + ROUTER_OFF_XCHG);        // [2][16][128]
-    int* xi = reinterpret_cast<int*>(smem + ROUTER_OFF_XCHG) + 2 * 16 * 128;
-    int it = 0;
-    bool ok = true;
-    bool first = true;
-    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
-      const int h = item / num_mt;
-      const int t = (item - h * num_mt) * 128 + row;
-      float lv[2][TOPK];
-      int li[2][TOPK];
+    const int kh = ew >> 2;  // key group: units with nc == kh
+    const bool two = num_chunks == 2;
+    if (!two && kh == 1) {
+      // one unit per half: group 0 alone handles every unit
+    } else {
+      const int row = q * 32 + lane;
+      float* stage = reinterpret_cast<float*>(smem + ROUTER_OFF_CAND) + ew * 32 * 32;
+      int* stage_id = reinterpret_cast<int*>(smem + ROUTER_OFF_CAND + 8 * 32 * 32 * 4) + (ew & 3) * 32 * 32;
+      float* xmax = reinterpret_cast<float*>(smem + ROUTER_OFF_XMAX);   // [2][16][128]
+      float* xlv = reinterpret_cast<float*>(smem + ROUTER_OFF_XLIST);   // [16][128]
+      int* xli = reinterpret_cast<int*>(smem + ROUTER_OFF_XLIST) + 16 * 128;
+      int m = 0;  // units consumed by this group
+      bool ok = true;
+      for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+        const int h = item / num_mt;
+        const int t = (item - h * num_mt) * 128 + row;
+        float lv[2][TOPK];
+        int li[2][TOPK];
 #pragma unroll
-      for (int p = 0; p < 2; ++p) {
+        for (int p = 0; p < 2; ++p) {
 #pragma unroll
-        for (int j = 0; j < TOPK; ++j) {
-          lv[p][j] = -INFINITY;
-          li[p][j] = 0;
-        }
-        for (int nc = 0; nc < num_chunks; ++nc, ++it) {
-          const int buf = it & 1;
-          const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
-          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], acc_phase, abort, err, 14));
-          if (!ok) continue;
-          tc_fence_after();
-          const int valid = min(256, g.K - nc * 256);
+          for (int j = 0; j < TOPK; ++j) {
+            lv[p][j] = -INFINITY;
+            li[p][j] = 0;
+          }
+          for (int nc = (two ? kh : 0); nc < num_chunks; nc += (two ? 2 : 1), ++m) {
+            // unit index within this CTA's sequence: two groups alternate
+            // buffers 0/1 (two == true) or one group walks both buffers
+            const int buf = two ? kh : (m & 1);
+            const uint32_t ph = two ? (static_cast<uint32_t>(m) & 1u) : (static_cast<uint32_t>(m >> 1) & 1u);
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], ph, abort, err, 14));
+            const int valid = min(256, g.K - nc * 256);
+            const int key_base = nc * 256;
+            const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256);
+            if (ok) tc_fence_after();
+            // 1. maxima of 16-key groups
+            float mx[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mx[i] = -INFINITY;
+            if (ok) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                if (c * 32 < valid) {
+                  float sc[32];
+                  tmem_ld32(cbase + c * 32, sc);
+                  float m0 = sc[0], m1 = sc[16];
+#pragma unroll
+                  for (int i = 1; i < 16; ++i) {
+                    m0 = fmaxf(m0, sc[i]);
+                    m1 = fmaxf(m1, sc[16 + i]);
+                  }
+                  mx[2 * c] = m0;
+                  mx[2 * c + 1] = m1;
+                }
+              }
+            }
+            // 2. tau = TOPK-th largest of the row's 16-key maxima (both groups)
+            float tau;
+            if (two) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) xmax[(kh * 16 + i) * 128 + row] = mx[i];
+              named_bar_sync(1, 256);
+              float other[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) other[i] = xmax[((kh ^ 1) * 16 + i) * 128 + row];
+              if (TOPK == 16) {
+                tau = nth_largest_of_union<16>(mx, other);
+              } else {
+                bitonic_sort_desc<16>(mx);
+                bitonic_sort_desc<16>(other);
+                float u[2 * TOPK];  // TOPK-th largest of the merged top lists
+#pragma unroll
+                for (int i = 0; i < TOPK; ++i) {
+                  u[i] = mx[i];
+                  u[TOPK + i] = other[i];
+                }
+                float a_[TOPK], b_[TOPK];
+#pragma unroll
+                for (int i = 0; i < TOPK; ++i) {
+                  a_[i] = u[i];
+                  b_[i] = u[TOPK + i];
+                }
+                tau = nth_largest_of_union<TOPK>(a_, b_);
+              }
+            } else {
+              // one unit per half: maxima of this unit only (valid/16 of them)
+              const int nmax = valid / 16;
+              if (nmax >= TOPK) {
+                bitonic_sort_desc<16>(mx);
+                tau = mx[TOPK - 1];
+              } else {
+                tau = -INFINITY;
+              }
+            }
+            // 3. fold scores >= tau
+            if (ok) {
 #pragma unroll 1
-          for (int c = kh * 4; c < kh * 4 + 4; ++c) {
-            if (c * 32 >= valid) break;
-            float sc[32];
-            tmem_ld32(tmem_addr(tmem, q * 32, buf * 256 + c * 32), sc);
-            topk_fold_chunk<TOPK>(lv[p], li[p], sc, nc * 256 + c * 32, stage, lane);
+              for (int c = 0; c < 8; ++c) {
+                if (c * 32 >= valid) break;
+                float sc[32];
+                tmem_ld32(cbase + c * 32, sc);
+                topk_fold_chunk<TOPK, false>(lv[p], li[p], sc, nullptr, key_base + c * 32, tau, stage, stage_id,
+                                             lane);
+              }
+              tc_fence_before();
+              mbar_arrive(&ctl->acc_empty[buf]);
+            }
           }
-          tc_fence_before();
-          mbar_arrive(&ctl->acc_empty[buf]);
-        }
-      }
-      // hand the second key group's lists to the first
-      const bool more = item + static_cast<int>(gridDim.x) < num_items;
-      if (kh == 1) {
-        if (!first) named_bar_sync(2, ROUTER_EPI_THREADS);  // previous item's lists were read
+          if (two) {
+            // group 1 hands its half-p list to group 0
+            if (kh == 1) {
 #pragma unroll
-        for (int p = 0; p < 2; ++p)
+              for (int j = 0; j < TOPK; ++j) {
+                xlv[j * 128 + row] = lv[p][j];
+                xli[j * 128 + row] = li[p][j];
+              }
+              named_bar_sync(2, 256);
+            } else {
+              named_bar_sync(2, 256);
+              float ov[32];
+              int oi[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                ov[j] = j < TOPK ? xlv[j * 128 + row] : -INFINITY;
+                oi[j] = j < TOPK ? xli[j * 128 + row] : 0;
+              }
+              topk_fold_chunk<TOPK, true>(lv[p], li[p], ov, oi, 0, -INFINITY, stage, stage_id, lane);
+            }
+          }
+        }
+        if (kh == 0) {
+          // Top-k of the candidate grid lv[0][i] + lv[1][j].  Only pairs with
+          // (i+1)(j+1) <= TOPK can rank in the top TOPK (every (i', j') with
+          // i' <= i, j' <= j scores at least as high); tau_c = max(a_0 +
+          // b_{k-1}, a_{k-1} + b_0) bounds the k-th largest sum from below.
+          constexpr int NC = (TOPK == 16) ? 50 : (TOPK == 8 ? 20 : 8);
+          float cv[64];
+          int ci[64];
+          int n = 0;
+#pragma unroll
+          for (int i = 0; i < TOPK; ++i) {
+#pragma unroll
+            for (int j = 0; (i + 1) * (j + 1) <= TOPK; ++j) {
+              cv[n] = lv[0][i] + lv[1][j];
+              ci[n] = li[0][i] * g.K + li[1][j];
+              ++n;
+            }
+          }
+#pragma unroll
+          for (int j = NC; j < 64; ++j) {
+            cv[j] = -INFINITY;
+            ci[j] = 0;
+          }
+          const float tau_c = fmaxf(lv[0][0] + lv[1][TOPK - 1], lv[0][TOPK - 1] + lv[1][0]);
+          float fv[TOPK];
+          int fid[TOPK];
 #pragma unroll
           for (int j = 0; j < TOPK; ++j) {
-            xv[(p * 16 + j) * 128 + row] = lv[p][j];
-            xi[(p * 16 + j) * 128 + row] = li[p][j];
+            fv[j] = -INFINITY;
+            fid[j] = 0;
           }
-        named_bar_sync(1, ROUTER_EPI_THREADS);
-      } else {
-        named_bar_sync(1, ROUTER_EPI_THREADS);
+          {
+            float c0[32], c1[32];
+            int d0[32], d1[32];
 #pragma unroll
-        for (int p = 0; p < 2; ++p)
-#pragma unroll
-          for (int j = 0; j < TOPK; ++j)
-            topk_insert<TOPK>(lv[p], li[p], xv[(p * 16 + j) * 128 + row], xi[(p * 16 + j) * 128 + row]);
-        if (more) named_bar_arrive(2, ROUTER_EPI_THREADS);
-        // Top-k of the candidate grid lv[0][i] + lv[1][j].  Only pairs with
-        // (i+1)(j+1) <= TOPK can rank in the top TOPK (every (i', j') with
-        // i' <= i, j' <= j scores at least as high), so only those are scanned.
-        float fv[TOPK];
-        int fid[TOPK];
-#pragma unroll
-        for (int j = 0; j < TOPK; ++j) {
-          fv[j] = -INFINITY;
-          fid[j] = 0;
-        }
-#pragma unroll
-        for (int i = 0; i < TOPK; ++i) {
-#pragma unroll
-          for (int j = 0; (i + 1) * (j + 1) <= TOPK; ++j) {
-            topk_insert<TOPK>(fv, fid, lv[0][i] + lv[1][j], li[0][i] * g.K + li[1][j]);
+            for (int j = 0; j < 32; ++j) {
+              c0[j] = cv[j];
+              d0[j] = ci[j];
+              c1[j] = cv[32 + j];
+              d1[j] = ci[32 + j];
+            }
+            topk_fold_chunk<TOPK, true>(fv, fid, c0, d0, 0, tau_c, stage, stage_id, lane);
+            topk_fold_chunk<TOPK, true>(fv, fid, c1, d1, 0, tau_c, stage, stage_id, lane);
           }
-        }
-        if (ok && t < g.T) {
-          // fp32 softmax over the selected scores (model.py:234)
-          float e[TOPK];
-          float sum = 0.f;
+          if (ok && t < g.T) {
+            // fp32 softmax over the selected scores (model.py:234)
+            float e[TOPK];
+            float sum = 0.f;
 #pragma unroll
-          for (int j = 0; j < TOPK; ++j) {
-            e[j] = expf(fv[j] - fv[0]);
-            sum += e[j];
-          }
-          const int64_t o = (static_cast<int64_t>(t) * g.H + h) * TOPK;
-          int4* di = reinterpret_cast<int4*>(ids_out + o);
-          float4* dw = reinterpret_cast<float4*>(w_out + o);
+            for (int j = 0; j < TOPK; ++j) {
+              e[j] = expf(fv[j] - fv[0]);
+              sum += e[j];
+            }
+            const int64_t o = (static_cast<int64_t>(t) * g.H + h) * TOPK;
+            int4* di = reinterpret_cast<int4*>(ids_out + o);
+            float4* dw = reinterpret_cast<float4*>(w_out + o);
 #pragma unroll
-          for (int j = 0; j < TOPK / 4; ++j) {
-            di[j] = make_int4(fid[4 * j], fid[4 * j + 1], fid[4 * j + 2], fid[4 * j + 3]);
-            dw[j] = make_float4(e[4 * j] / sum, e[4 * j + 1] / sum, e[4 * j + 2] / sum, e[4 * j + 3] / sum);
+            for (int j = 0; j < TOPK / 4; ++j) {
+              di[j] = make_int4(fid[4 * j], fid[4 * j + 1], fid[4 * j + 2], fid[4 * j + 3]);
+              dw[j] = make_float4(e[4 * j] / sum, e[4 * j + 1] / sum, e[4 * j + 2] / sum, e[4 * j + 3] / sum);
+            }
           }
         }
       }
-      first = false;
     }
   }
   __syncthreads();
