@@ -1,0 +1,499 @@
+// Backward pass of the ETHOS expert layer.
+//
+// Reference: autograd through SimplifiedHypernetMoE.forward (model.py:288-343)
+// and ProductKeyRouter.forward (model.py:208-254).  With a_r = gelu(dot_r) w_r,
+// h_r = gelu(pre_r), pre_r = E[id_r] W1^T, dot_r = h_r . xp_t:
+//   dhacc_t = dy_t W_v / H                         (GEMM)
+//   da_r    = dhacc_t . h_r
+//   dw_r    = da_r gelu(dot_r)                     (routing-weight gradient)
+//   ddot_r  = da_r w_r gelu'(dot_r)
+//   dxp_t   = sum_r ddot_r h_r
+//   dh_r    = a_r dhacc_t + ddot_r xp_t
+//   dpre_r  = dh_r * gelu'(pre_r)
+// Because pre_r depends only on the expert e = id_r, the expert-side
+// gradients aggregate per expert: dP[e] = gelu'(P[e]) * sum_{r: id_r = e} dh_r,
+// after which dE = dP W1 and dW1 = dP^T E are dense GEMMs.  The selections
+// are grouped by expert with a counting sort; dhacc and xp (64 MB at the
+// default size) stay L2-resident while each expert sums its selections.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "expert_table.cuh"
+#include "router.cuh"
+
+namespace ethos {
+
+// ------------------------------------------------------------------------
+// Per-token backward gather: the forward gather kernel's structure with the
+// token vector dhacc in place of xp.  Per selection it writes dw, a and ddot;
+// per token dxp (fp32) and its bf16 copy into the GEMM operand du[:, off:].
+constexpr int BGATHER_STAGE_BYTES = GATHER_ROWS * 1024 + 32;  // rows + 4 weights + 4 dots
+constexpr int BGATHER_WARP_BYTES = GATHER_STAGES * BGATHER_STAGE_BYTES + 2 * 2048;
+constexpr int BGATHER_SMEM_BYTES = GATHER_WARPS * BGATHER_WARP_BYTES;
+
+__global__ void __launch_bounds__(GATHER_THREADS, 1)
+    k_expert_bwd_gather(const __half* __restrict__ table, const int32_t* __restrict__ ids,
+                        const float* __restrict__ w, const float* __restrict__ dot, const float* __restrict__ dhacc,
+                        float* __restrict__ dw_out, float* __restrict__ ca_out, float* __restrict__ cd_out,
+                        float* __restrict__ dxp_out, __nv_bfloat16* __restrict__ du, int64_t ldu, int du_off, int T,
+                        int R, int N, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  uint8_t* wbase = smem_raw + wib * BGATHER_WARP_BYTES;
+  uint8_t* vbuf = wbase + GATHER_STAGES * BGATHER_STAGE_BYTES;
+  const int gw = blockIdx.x * GATHER_WARPS + wib;
+  const int nw = gridDim.x * GATHER_WARPS;
+  const int nbt = R / GATHER_ROWS;
+  const int ntok = T > gw ? (T - 1 - gw) / nw + 1 : 0;
+  const int nb = ntok * nbt;
+  const int b3 = (lane >> 3) & 1, b4 = (lane >> 4) & 1;
+  const int grp = (lane >> 3) & 3;
+
+  auto load_ids = [&](int b) -> int4 {
+    if (b >= nb) return make_int4(0, 0, 0, 0);
+    const int t = gw + (b / nbt) * nw;
+    const int r0 = (b % nbt) * GATHER_ROWS;
+    return __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(t) * R + r0));
+  };
+  auto issue = [&](int b, int4 id4) {
+    const int t = gw + (b / nbt) * nw;
+    const int r0 = (b % nbt) * GATHER_ROWS;
+    uint8_t* st = wbase + (b % GATHER_STAGES) * BGATHER_STAGE_BYTES;
+    const int idv[4] = {id4.x, id4.y, id4.z, id4.w};
+#pragma unroll
+    for (int u = 0; u < GATHER_ROWS; ++u) {
+      int id = idv[u];
+      if (id < 0 || id >= N) {
+        if (lane == 0) record_error(err, ETHOS_ERR_ID_OUT_OF_RANGE);
+        id = 0;
+      }
+      const char* src = reinterpret_cast<const char*>(table + static_cast<int64_t>(id) * 512);
+      cp_async_16(st + u * 1024 + 16 * lane, src + 16 * lane);
+      cp_async_16(st + u * 1024 + 512 + 16 * lane, src + 512 + 16 * lane);
+    }
+    if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
+    if (lane == 1) cp_async_16(st + GATHER_ROWS * 1024 + 16, dot + static_cast<int64_t>(t) * R + r0);
+    if (r0 == 0) {
+      const char* xs = reinterpret_cast<const char*>(dhacc + static_cast<int64_t>(t) * 512);
+      uint8_t* xd = vbuf + ((b / nbt) & 1) * 2048;
+      cp_async_16(xd + 32 * lane, xs + 32 * lane);
+      cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
+      cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
+      cp_async_16(xd + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
+    }
+  };
+
+  int4 next_ids = load_ids(0);
+#pragma unroll 1
+  for (int b = 0; b < GATHER_STAGES - 1; ++b) {
+    const int4 cur = next_ids;
+    next_ids = load_ids(b + 1);
+    if (b < nb) issue(b, cur);
+    cp_async_commit();
+  }
+  float gv[16];
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll 1
+  for (int b = 0; b < nb; ++b) {
+    {
+      const int bi = b + GATHER_STAGES - 1;
+      const int4 cur = next_ids;
+      next_ids = load_ids(bi + 1);
+      if (bi < nb) issue(bi, cur);
+      cp_async_commit();
+    }
+    cp_async_wait_group<GATHER_STAGES - 1>();
+    const int t = gw + (b / nbt) * nw;
+    const int r0 = (b % nbt) * GATHER_ROWS;
+    const uint8_t* st = wbase + (b % GATHER_STAGES) * BGATHER_STAGE_BYTES;
+    if (r0 == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(vbuf + ((b / nbt) & 1) * 2048);
+      const float4 a0 = x4[2 * lane], a1 = x4[2 * lane + 1], c0 = x4[64 + 2 * lane], c1 = x4[64 + 2 * lane + 1];
+      gv[0] = a0.x; gv[1] = a0.y; gv[2] = a0.z; gv[3] = a0.w;
+      gv[4] = a1.x; gv[5] = a1.y; gv[6] = a1.z; gv[7] = a1.w;
+      gv[8] = c0.x; gv[9] = c0.y; gv[10] = c0.z; gv[11] = c0.w;
+      gv[12] = c1.x; gv[13] = c1.y; gv[14] = c1.z; gv[15] = c1.w;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    }
+    uint4 hv[GATHER_ROWS][2];
+    float part[GATHER_ROWS];
+#pragma unroll
+    for (int u = 0; u < GATHER_ROWS; ++u) {
+      hv[u][0] = *reinterpret_cast<const uint4*>(st + u * 1024 + 16 * lane);
+      hv[u][1] = *reinterpret_cast<const uint4*>(st + u * 1024 + 512 + 16 * lane);
+      float f[8];
+      float sacc = 0.f;
+      unpack_h8(hv[u][0], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sacc = fmaf(f[i], gv[i], sacc);
+      unpack_h8(hv[u][1], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sacc = fmaf(f[i], gv[8 + i], sacc);
+      part[u] = sacc;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = b4 ? part[i] : part[i + 2];
+      const float keep = b4 ? part[i + 2] : part[i];
+      part[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    {
+      const float send = b3 ? part[0] : part[1];
+      const float keep = b3 ? part[1] : part[0];
+      part[0] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float da = part[0] + __shfl_xor_sync(0xffffffffu, part[0], 4);
+    da += __shfl_xor_sync(0xffffffffu, da, 2);
+    da += __shfl_xor_sync(0xffffffffu, da, 1);
+    const float wgt = reinterpret_cast<const float*>(st + GATHER_ROWS * 1024)[grp];
+    const float dt = reinterpret_cast<const float*>(st + GATHER_ROWS * 1024 + 16)[grp];
+    const float gd = gelu_erf(dt);
+    const float ddot = da * wgt * gelu_erf_grad(dt);
+    if ((lane & 7) == 0) {
+      const int64_t o = static_cast<int64_t>(t) * R + r0 + grp;
+      dw_out[o] = da * gd;
+      ca_out[o] = gd * wgt;
+      cd_out[o] = ddot;
+    }
+#pragma unroll
+    for (int u = 0; u < GATHER_ROWS; ++u) {
+      const float c = __shfl_sync(0xffffffffu, ddot, 8 * u);
+      float f[8];
+      unpack_h8(hv[u][0], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(c, f[i], acc[i]);
+      unpack_h8(hv[u][1], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[8 + i] = fmaf(c, f[i], acc[8 + i]);
+    }
+    if (r0 + GATHER_ROWS == R) {
+      float* dst = dxp_out + static_cast<int64_t>(t) * 512;
+      *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      *reinterpret_cast<float4*>(dst + 256 + 8 * lane) = make_float4(acc[8], acc[9], acc[10], acc[11]);
+      *reinterpret_cast<float4*>(dst + 256 + 8 * lane + 4) = make_float4(acc[12], acc[13], acc[14], acc[15]);
+      uint32_t o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        o[i] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+      __nv_bfloat16* ud = du + static_cast<int64_t>(t) * ldu + du_off;
+      *reinterpret_cast<uint4*>(ud + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(ud + 256 + 8 * lane) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  }
+  cp_async_wait_group<0>();
+}
+
+// ------------------------------------------------------------------------
+// Counting sort of the T*R selections by expert id.
+__global__ void k_count_experts(const int32_t* __restrict__ ids, int64_t n, int N, int* __restrict__ cnt, int* err) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[i];
+    if (e < 0 || e >= N) {
+      record_error(err, ETHOS_ERR_ID_OUT_OF_RANGE);
+      continue;
+    }
+    atomicAdd(cnt + e, 1);
+  }
+}
+
+// Exclusive scan in three steps: per-block scan of 1024 counts (block sums
+// out), scan of the block sums (one block), add-back.
+__global__ void k_scan_blocks(const int* __restrict__ in, int n, int* __restrict__ out, int* __restrict__ sums) {
+  __shared__ int s[1024];
+  const int i = blockIdx.x * 1024 + threadIdx.x;
+  const int v = i < n ? in[i] : 0;
+  s[threadIdx.x] = v;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int add = threadIdx.x >= off ? s[threadIdx.x - off] : 0;
+    __syncthreads();
+    s[threadIdx.x] += add;
+    __syncthreads();
+  }
+  if (i < n) out[i] = s[threadIdx.x] - v;
+  if (threadIdx.x == 1023) sums[blockIdx.x] = s[1023];
+}
+__global__ void k_scan_sums(int* __restrict__ sums, int nblocks, int* __restrict__ total_out) {
+  __shared__ int s[1024];
+  const int v = threadIdx.x < nblocks ? sums[threadIdx.x] : 0;
+  s[threadIdx.x] = v;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int add = threadIdx.x >= off ? s[threadIdx.x - off] : 0;
+    __syncthreads();
+    s[threadIdx.x] += add;
+    __syncthreads();
+  }
+  if (threadIdx.x < nblocks) sums[threadIdx.x] = s[threadIdx.x] - v;
+  if (threadIdx.x == 1023) *total_out = s[1023];
+}
+__global__ void k_scan_add(int* __restrict__ out, int n, const int* __restrict__ sums, int* __restrict__ cursor) {
+  const int i = blockIdx.x * 1024 + threadIdx.x;
+  if (i < n) {
+    const int v = out[i] + sums[blockIdx.x];
+    out[i] = v;
+    cursor[i] = v;
+  }
+}
+__global__ void k_scatter_experts(const int32_t* __restrict__ ids, int64_t n, int N, int* __restrict__ cursor,
+                                  int* __restrict__ perm) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[i];
+    if (e < 0 || e >= N) continue;
+    const int pos = atomicAdd(cursor + e, 1);
+    perm[pos] = static_cast<int>(i);
+  }
+}
+
+// ------------------------------------------------------------------------
+// Per-expert pre-activation gradient (one warp per expert, lane l owns hidden
+// columns [8l, 8l+8) and [256+8l, 256+8l+8)):
+//   dP[e] = G[e] * sum_{s in seg(e)} (a_s dhacc[t_s] + ddot_s xp[t_s])
+// written as bf16 (operand of the dE / dW1 GEMMs).  Experts without
+// selections get zeros.
+__global__ void __launch_bounds__(256) k_expert_dP(const int* __restrict__ offs, const int* __restrict__ perm,
+                                                    int total, const float* __restrict__ ca,
+                                                    const float* __restrict__ cd, const float* __restrict__ dhacc,
+                                                    const float* __restrict__ xp, const __half* __restrict__ gtab,
+                                                    __nv_bfloat16* __restrict__ dP, int N, int R) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int e = gw; e < N; e += nw) {
+    const int s0 = offs[e];
+    const int s1 = e + 1 < N ? offs[e + 1] : total;
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    for (int sidx = s0; sidx < s1; ++sidx) {
+      const int idx = __ldg(perm + sidx);
+      const int64_t t = idx / R;
+      const float a = __ldg(ca + idx), d = __ldg(cd + idx);
+      const float4* g4 = reinterpret_cast<const float4*>(dhacc + t * 512);
+      const float4* x4 = reinterpret_cast<const float4*>(xp + t * 512);
+      const float4 g0 = __ldg(g4 + 2 * lane), g1 = __ldg(g4 + 2 * lane + 1);
+      const float4 g2 = __ldg(g4 + 64 + 2 * lane), g3 = __ldg(g4 + 64 + 2 * lane + 1);
+      const float4 x0 = __ldg(x4 + 2 * lane), x1 = __ldg(x4 + 2 * lane + 1);
+      const float4 x2 = __ldg(x4 + 64 + 2 * lane), x3 = __ldg(x4 + 64 + 2 * lane + 1);
+      const float gg[16] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w,
+                            g2.x, g2.y, g2.z, g2.w, g3.x, g3.y, g3.z, g3.w};
+      const float xx[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                            x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = fmaf(a, gg[i], fmaf(d, xx[i], acc[i]));
+    }
+    const __half* gr = gtab + static_cast<int64_t>(e) * 512;
+    float gf[16];
+    {
+      float f[8];
+      unpack_h8(*reinterpret_cast<const uint4*>(gr + 8 * lane), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gf[i] = f[i];
+      unpack_h8(*reinterpret_cast<const uint4*>(gr + 256 + 8 * lane), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gf[8 + i] = f[i];
+    }
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __nv_bfloat162 bb = __floats2bfloat162_rn(acc[2 * i] * gf[2 * i], acc[2 * i + 1] * gf[2 * i + 1]);
+      o[i] = *reinterpret_cast<const uint32_t*>(&bb);
+    }
+    __nv_bfloat16* dst = dP + static_cast<int64_t>(e) * 512;
+    *reinterpret_cast<uint4*>(dst + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + 256 + 8 * lane) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// ------------------------------------------------------------------------
+// Router backward per (token, head) -- one warp each, lane l owns query
+// columns [8l, 8l+8) of each half (dq/2 = 256):
+//   dg_r  = w_r (dw_r - sum_r' w_r' dw_r')                    (softmax)
+//   dq^[t, h, :dq/2] = sum_r dg_r K1[i_r],  dq^[t, h, dq/2:] = sum_r dg_r K2[j_r]
+//   dS_p[h][t][i] = sum_{r: key_p(r) = i} dg_r               (dense, bf16)
+// with i_r = id_r / K, j_r = id_r % K.  dS feeds the dK GEMMs; its buffer is
+// zeroed beforehand and every (h, p, t, i) is written by one lane (duplicate
+// keys of a row are combined with __match_any_sync first).
+template <int TOPK>
+__global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                                     const float* __restrict__ dw,
+                                                     const __nv_bfloat16* __restrict__ keys,  // [2][K] rows
+                                                     int64_t key_ld, float* __restrict__ dqhat,
+                                                     __nv_bfloat16* __restrict__ dS, int T, int H, int K, int half) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int nl = half / 8;  // lanes covering one half in 8-column slices
+  for (int th = gw; th < T * H; th += nw) {
+    const int t = th / H, h = th - t * H;
+    const int64_t o = static_cast<int64_t>(th) * TOPK;
+    const bool act = lane < TOPK;
+    const float wr = act ? w[o + lane] : 0.f;
+    const float dwr = act ? dw[o + lane] : 0.f;
+    float s = wr * dwr;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    const float dg = act ? wr * (dwr - s) : 0.f;
+    const int id = act ? ids[o + lane] : 0;
+    const int i1 = id / K, i2 = id - i1 * K;
+    // dS scatter: lanes with the same key combine (uniform loop over the
+    // TOPK selections), the lowest such lane stores
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int key = act ? (p == 0 ? i1 : i2) : -1 - lane;
+      const unsigned same = __match_any_sync(0xffffffffu, key);
+      float tot = 0.f;
+#pragma unroll
+      for (int u = 0; u < TOPK; ++u) {
+        const float gu = __shfl_sync(0xffffffffu, dg, u);
+        const int ku = __shfl_sync(0xffffffffu, key, u);
+        tot += ku == key ? gu : 0.f;
+      }
+      if (act && (__ffs(same) - 1) == lane)
+        dS[((static_cast<int64_t>(h) * 2 + p) * T + t) * K + key] = __float2bfloat16_rn(tot);
+    }
+    // dq^ = sum_r dg_r * key rows
+    float acc0[8], acc1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc0[i] = 0.f;
+      acc1[i] = 0.f;
+    }
+#pragma unroll 4
+    for (int u = 0; u < TOPK; ++u) {
+      const float g = __shfl_sync(0xffffffffu, dg, u);
+      const int ku = __shfl_sync(0xffffffffu, id, u);
+      const int k1 = ku / K, k2 = ku - (ku / K) * K;
+      if (lane < nl) {
+        const uint4 a = *reinterpret_cast<const uint4*>(keys + static_cast<int64_t>(k1) * key_ld + 8 * lane);
+        const uint4 b = *reinterpret_cast<const uint4*>(keys + (static_cast<int64_t>(K) + k2) * key_ld + 8 * lane);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 fa = __bfloat1622float2(a2[i]);
+          const float2 fb = __bfloat1622float2(b2[i]);
+          acc0[2 * i] = fmaf(g, fa.x, acc0[2 * i]);
+          acc0[2 * i + 1] = fmaf(g, fa.y, acc0[2 * i + 1]);
+          acc1[2 * i] = fmaf(g, fb.x, acc1[2 * i]);
+          acc1[2 * i + 1] = fmaf(g, fb.y, acc1[2 * i + 1]);
+        }
+      }
+    }
+    if (lane < nl) {
+      float* dst = dqhat + static_cast<int64_t>(t) * (H * 2 * half) + static_cast<int64_t>(h) * 2 * half;
+      *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(acc0[0], acc0[1], acc0[2], acc0[3]);
+      *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(acc0[4], acc0[5], acc0[6], acc0[7]);
+      *reinterpret_cast<float4*>(dst + half + 8 * lane) = make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
+      *reinterpret_cast<float4*>(dst + half + 8 * lane + 4) = make_float4(acc1[4], acc1[5], acc1[6], acc1[7]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
+// BatchNorm backward.  x^ = (qpre - mean) * invstd (batch statistics in
+// training mode, running statistics in eval mode).  Column sums over tokens
+// of dq^ and dq^ * x^ (slab partials, then a finalize), then
+//   train: dq = gamma*invstd*(dq^ - sum(dq^)/T - x^ * sum(dq^ x^)/T), dbias = 0
+//   eval:  dq = gamma*invstd*dq^,                           dbias = sum(dq)
+// dgamma = sum(dq^ x^), dbeta = sum(dq^).  dq is written as bf16 into the
+// GEMM operand du[:, :C].
+__global__ void k_bn_bwd_partial(const float* __restrict__ dqh, const float* __restrict__ qpre,
+                                 const float* __restrict__ mean, const float* __restrict__ invstd, int T, int C,
+                                 float* __restrict__ part) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int slab = blockIdx.y;
+  if (col >= C) return;
+  const float mu = mean[col], is = invstd[col];
+  const int r0 = slab * BN_ROWS_PER_SLAB;
+  const int r1 = min(T, r0 + BN_ROWS_PER_SLAB);
+  float s = 0.f, sx = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const int64_t o = static_cast<int64_t>(r) * C + col;
+    const float g = dqh[o];
+    s += g;
+    sx = fmaf(g, (qpre[o] - mu) * is, sx);
+  }
+  part[(static_cast<int64_t>(slab) * C + col) * 2 + 0] = s;
+  part[(static_cast<int64_t>(slab) * C + col) * 2 + 1] = sx;
+}
+
+__global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int C, int T, int training,
+                                  const float* __restrict__ gamma, const float* __restrict__ invstd,
+                                  float* __restrict__ dgamma, float* __restrict__ dbeta, float* __restrict__ dbias,
+                                  float* __restrict__ coef) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= C) return;
+  double s = 0.0, sx = 0.0;
+  for (int k = 0; k < slabs; ++k) {
+    s += part[(static_cast<int64_t>(k) * C + col) * 2 + 0];
+    sx += part[(static_cast<int64_t>(k) * C + col) * 2 + 1];
+  }
+  dgamma[col] = static_cast<float>(sx);
+  dbeta[col] = static_cast<float>(s);
+  const float gi = gamma[col] * invstd[col];
+  if (training) {
+    dbias[col] = 0.f;
+    coef[3 * col + 0] = gi;
+    coef[3 * col + 1] = static_cast<float>(s / T);
+    coef[3 * col + 2] = static_cast<float>(sx / T);
+  } else {
+    dbias[col] = static_cast<float>(gi * s);
+    coef[3 * col + 0] = gi;
+    coef[3 * col + 1] = 0.f;
+    coef[3 * col + 2] = 0.f;
+  }
+}
+
+__global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __restrict__ qpre,
+                               const float* __restrict__ mean, const float* __restrict__ invstd,
+                               const float* __restrict__ coef, int T, int C, __nv_bfloat16* __restrict__ du,
+                               int64_t ldu) {
+  const int64_t n = static_cast<int64_t>(T) * C;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / C);
+    const int c = static_cast<int>(i - static_cast<int64_t>(t) * C);
+    const float xh = (qpre[i] - mean[c]) * invstd[c];
+    const float g = coef[3 * c] * (dqh[i] - coef[3 * c + 1] - xh * coef[3 * c + 2]);
+    du[static_cast<int64_t>(t) * ldu + c] = __float2bfloat16_rn(g);
+  }
+}
+
+// Eval-mode statistics for the backward on qpre (which contains the bias):
+// x^ = (qpre - running_mean) * 1/sqrt(running_var + eps).
+__global__ void k_bn_eval_stats(const float* __restrict__ bn, int C, float eps, float* __restrict__ mean,
+                                float* __restrict__ invstd) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= C) return;
+  mean[col] = bn[3 * C + col];
+  invstd[col] = 1.0f / sqrtf(bn[4 * C + col] + eps);
+}
+
+// out[c][j] = in[j][c] for an fp32 [rows, cols] matrix (small weight grads).
+__global__ void k_transpose_f32(const float* __restrict__ in, int rows, int cols, float* __restrict__ out,
+                                int64_t ldo) {
+  __shared__ float tile[32][33];
+  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int r = by + j, c = bx + threadIdx.x;
+    if (r < rows && c < cols) tile[j][threadIdx.x] = in[static_cast<int64_t>(r) * cols + c];
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int c = bx + j, r = by + threadIdx.x;
+    if (c < cols && r < rows) out[static_cast<int64_t>(c) * ldo + r] = tile[threadIdx.x][j];
+  }
+}
+
+}  // namespace ethos

@@ -11,6 +11,7 @@
 #include "ethos_b200.h"
 #include "expert.cuh"
 #include "expert_table.cuh"
+#include "backward.cuh"
 #include "gemm.cuh"
 #include "router.cuh"
 
@@ -44,14 +45,6 @@ int device_info(DeviceInfo** out) {
   if (d.major != 10) return ETHOS_ERR_NO_DEVICE;
   if (!d.attrs_set) {
     bool ok = true;
-    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiStoreBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               GEMM_SMEM_BYTES) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiStoreF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               GEMM_SMEM_BYTES) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiProj>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               GEMM_SMEM_BYTES) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(k_gemm_bf16_tn<EpiGeluF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               GEMM_SMEM_BYTES) == cudaSuccess;
     ok &= cudaFuncSetAttribute(k_score_topk<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTER_SMEM_BYTES) ==
           cudaSuccess;
     ok &= cudaFuncSetAttribute(k_score_topk<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTER_SMEM_BYTES) ==
@@ -66,6 +59,22 @@ int device_info(DeviceInfo** out) {
     d.attrs_set = true;
   }
   *out = &d;
+  return ETHOS_OK;
+}
+
+// Sets the dynamic shared-memory limit of a kernel once per device.
+int smem_attr_once(const void* fn, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ETHOS_ERR_NO_DEVICE;
+  static std::mutex mu;
+  static const void* seen[64][32];
+  static int nseen[64];
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < nseen[dev]; ++i)
+    if (seen[dev][i] == fn) return ETHOS_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return ETHOS_ERR_CUDA;
+  if (nseen[dev] < 32) seen[dev][nseen[dev]++] = fn;
   return ETHOS_OK;
 }
 
@@ -86,14 +95,16 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Row-major bf16 matrix [rows, cols] read in boxes of 64 columns x box_rows
-// rows with the 128-byte swizzle that the UMMA descriptors expect.
-int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+// Row-major bf16 matrix [rows, cols] (row pitch ld >= cols elements) read in
+// boxes of 64 columns x box_rows rows with the 128-byte swizzle that the UMMA
+// descriptors expect.
+int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows, int64_t ld = 0) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return ETHOS_ERR_TENSOR_MAP;
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || (cols * 2) % 16 != 0) return ETHOS_ERR_ALIGNMENT;
+  if (ld == 0) ld = cols;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || (ld * 2) % 16 != 0) return ETHOS_ERR_ALIGNMENT;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
   cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -115,14 +126,80 @@ int launch_status() {
   return e == cudaSuccess ? ETHOS_OK : ETHOS_ERR_CUDA;
 }
 
+// Operand of a GEMM: bf16 matrix stored row-major with row pitch ld; K-major
+// means stored [rows = M or N][K], MN-major means stored [K][M or N].
+struct GemmOperand {
+  const void* ptr;
+  int64_t ld;
+  bool mn_major;
+};
+
+int operand_tmap(CUtensorMap* m, const GemmOperand& o, int64_t mn, int64_t k, int mn_box) {
+  if (o.mn_major) return make_tmap_bf16(m, o.ptr, k, mn, 64, o.ld);
+  return make_tmap_bf16(m, o.ptr, mn, k, mn_box, o.ld);
+}
+
+// Launches D = A B^T on the generic kernel.  ksplit > 1 requires an epilogue
+// that accumulates (EpiAtomicF32).  BN = 256 when N allows, else 128.
+template <class Epi, bool AMN, bool BMN, int BN>
+int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit, const Epi& epi,
+                  int* err, cudaStream_t stream, const DeviceInfo& dev) {
+  auto kern = k_gemm<Epi, AMN, BMN, BN>;
+  int st = smem_attr_once(reinterpret_cast<const void*>(kern), GEMM_SMEM_BYTES);
+  if (st != ETHOS_OK) return st;
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN);
+  const int units = tiles * ksplit;
+  const int grid = units < dev.sm_count ? units : dev.sm_count;
+  if (grid <= 0) return ETHOS_OK;
+  kern<<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, stream>>>(ta, tb, M, N, K, ksplit, epi, err);
+  return launch_status();
+}
+
+template <class Epi>
+int gemm(const GemmOperand& a, const GemmOperand& b, int M, int N, int K, int ksplit, const Epi& epi, int* err,
+         cudaStream_t stream, const DeviceInfo& dev) {
+  if (M < 1 || N < 128 || N % 128 != 0 || K < 1) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (!a.mn_major && K % 8 != 0) return ETHOS_ERR_ALIGNMENT;
+  if (!b.mn_major && K % 8 != 0) return ETHOS_ERR_ALIGNMENT;
+  const bool wide = N % 256 == 0;
+  CUtensorMap ta, tb;
+  int st;
+  if ((st = operand_tmap(&ta, a, M, K, 128)) != ETHOS_OK) return st;
+  if ((st = operand_tmap(&tb, b, N, K, wide ? 256 : 128)) != ETHOS_OK) return st;
+  // never leave a K slice empty
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  if (ksplit > num_kb) ksplit = num_kb;
+  if (ksplit < 1) ksplit = 1;
+  const int kpb = (num_kb + ksplit - 1) / ksplit;
+  ksplit = (num_kb + kpb - 1) / kpb;
+#define ETHOS_GEMM_CASE(AM, BM_)                                                                     \
+  if (a.mn_major == AM && b.mn_major == BM_) {                                                      \
+    return wide ? launch_gemm_t<Epi, AM, BM_, 256>(ta, tb, M, N, K, ksplit, epi, err, stream, dev)   \
+                : launch_gemm_t<Epi, AM, BM_, 128>(ta, tb, M, N, K, ksplit, epi, err, stream, dev);  \
+  }
+  ETHOS_GEMM_CASE(false, false)
+  ETHOS_GEMM_CASE(true, false)
+  ETHOS_GEMM_CASE(false, true)
+  ETHOS_GEMM_CASE(true, true)
+#undef ETHOS_GEMM_CASE
+  return ETHOS_ERR_INVALID_ARG;
+}
+
+// Split count that fills the GPU for an accumulating GEMM with few tiles.
+int auto_ksplit(int M, int N, int K, const DeviceInfo& dev) {
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N % 256 == 0 ? N / 256 : N / 128);
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  int ks = dev.sm_count / (tiles > 0 ? tiles : 1);
+  if (ks < 1) ks = 1;
+  if (ks > num_kb) ks = num_kb;
+  return ks;
+}
+
+// Forward-path GEMM: both operands K-major (tensor maps built by the caller).
 template <class Epi>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int* err,
                 cudaStream_t stream, const DeviceInfo& dev) {
-  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / GEMM_BN);
-  const int grid = tiles < dev.sm_count ? tiles : dev.sm_count;
-  if (grid <= 0) return ETHOS_OK;
-  k_gemm_bf16_tn<Epi><<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, stream>>>(ta, tb, M, N, K, epi, err);
-  return launch_status();
+  return launch_gemm_t<Epi, false, false, 256>(ta, tb, M, N, K, 1, epi, err, stream, dev);
 }
 
 // ------------------------------------------------------- workspace layout --
@@ -270,27 +347,31 @@ int run_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g,
 // Router part shared by ethos_layer_forward and ethos_router_forward:
 // projection GEMM (queries, plus x_proj when with_xp), BatchNorm, scoring and
 // top-k.
+// `qs` is the split-bf16 scoring operand [H][2][T][dq] (scratch, or the
+// caller's save buffer).  With keep_qpre the projection always writes the
+// pre-BatchNorm queries (fp32) and normalises them in a second pass, so the
+// backward pass has them in both BatchNorm modes.
 int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn, float bn_eps, float bn_momentum,
                 int bn_training, const void* key_cat, int32_t* ids, float* weights, bool with_xp, float* xp_out,
-                const FwdScratch& s, float* qpre, float* save_bn, int* err, cudaStream_t stream,
-                const DeviceInfo& dev, void* const* ev = nullptr) {
+                const FwdScratch& s, __nv_bfloat16* qs, float* qpre, bool keep_qpre, float* save_bn, int* err,
+                cudaStream_t stream, const DeviceInfo& dev, void* const* ev = nullptr) {
   const int T = static_cast<int>(d.tokens);
   const int HQ = static_cast<int>(d.num_heads * d.d_query);
   const int dq = static_cast<int>(d.d_query);
   const int dh = static_cast<int>(d.d_hidden);
   const int ncat = with_xp ? HQ + dh : HQ;
+  const bool two_pass = bn_training || keep_qpre;
   CUtensorMap tm_x, tm_w, tm_q, tm_k;
   int st;
   if ((st = make_tmap_bf16(&tm_x, x, T, d.d_model, 128)) != ETHOS_OK) return st;
   if ((st = make_tmap_bf16(&tm_w, w_cat, ncat, d.d_model, 256)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tm_q, s.qs, static_cast<int64_t>(d.num_heads) * 2 * T, dq, 128)) != ETHOS_OK)
-    return st;
+  if ((st = make_tmap_bf16(&tm_q, qs, static_cast<int64_t>(d.num_heads) * 2 * T, dq, 128)) != ETHOS_OK) return st;
   const int box_keys = d.num_sub_keys < 256 ? static_cast<int>(d.num_sub_keys) : 256;
   if ((st = make_tmap_bf16(&tm_k, key_cat, 2 * d.num_sub_keys, dq, box_keys)) != ETHOS_OK) return st;
 
   const int cb = 256;
   if (!bn_training) {
-    k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(bn, HQ, bn_eps, s.colp);
+    k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(bn, HQ, bn_eps, two_pass ? 1 : 0, s.colp);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   EpiProj epi;
@@ -298,25 +379,27 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   epi.HQ = HQ;
   epi.dq = dq;
   epi.dh = dh;
-  epi.mode = bn_training ? 1 : 0;
+  epi.mode = two_pass ? 1 : 0;
   epi.bias = bn;
   epi.colp = s.colp;
-  epi.qs = s.qs;
+  epi.qs = qs;
   epi.qpre = qpre;
   epi.xp = xp_out;
   if ((st = launch_gemm(tm_x, tm_w, T, ncat, static_cast<int>(d.d_model), epi, err, stream, dev)) != ETHOS_OK)
     return st;
   mark(ev, ETHOS_STAGE_PROJECTION, stream);
-  if (bn_training) {
-    dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
-    k_bn_partial<<<grid_p, cb, 0, stream>>>(qpre, T, HQ, s.bn_part);
-    k_bn_finalize<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(qpre, s.bn_part, T, HQ, s.slabs, bn + HQ, bn + 2 * HQ,
-                                                         bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, save_bn,
-                                                         s.colp);
+  if (two_pass) {
+    if (bn_training) {
+      dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+      k_bn_partial<<<grid_p, cb, 0, stream>>>(qpre, T, HQ, s.bn_part);
+      k_bn_finalize<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(qpre, s.bn_part, T, HQ, s.slabs, bn + HQ, bn + 2 * HQ,
+                                                           bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, save_bn,
+                                                           s.colp);
+    }
     const int64_t groups = static_cast<int64_t>(T) * (HQ / 8);
     k_bn_apply<<<static_cast<unsigned>((groups + cb - 1) / cb), cb, 0, stream>>>(qpre, s.colp, T,
                                                                                 static_cast<int>(d.num_heads), dq,
-                                                                                s.qs);
+                                                                                qs);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   mark(ev, ETHOS_STAGE_BATCHNORM, stream);
@@ -331,6 +414,77 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   st = run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, err, stream, dev);
   mark(ev, ETHOS_STAGE_TOPK, stream);
   return st;
+}
+
+// ------------------------------------------------------- backward scratch --
+struct BwdScratch {
+  __half* htab;
+  __half* gtab;
+  float* dhacc;
+  float* dw;
+  float* ca;
+  float* cd;
+  float* dxp;
+  __nv_bfloat16* du;
+  int* cnt;
+  int* offs;
+  int* cursor;
+  int* bsums;
+  int* total;
+  int* perm;
+  __nv_bfloat16* dP;
+  float* dqhat;
+  __nv_bfloat16* dS;
+  float* part;
+  float* coef;
+  float* stats;
+  __nv_bfloat16* dy16;
+  int slabs;
+};
+
+void carve_backward(Carve& c, const ethos_dims& d, BwdScratch* s) {
+  const int64_t T = d.tokens, N = d.num_experts, R = d.num_heads * d.top_k, HQ = d.num_heads * d.d_query;
+  s->htab = c.take<__half>(static_cast<size_t>(N * EX_DH));
+  s->gtab = c.take<__half>(static_cast<size_t>(N * EX_DH));
+  s->dhacc = c.take<float>(static_cast<size_t>(T * EX_DH));
+  s->dw = c.take<float>(static_cast<size_t>(T * R));
+  s->ca = c.take<float>(static_cast<size_t>(T * R));
+  s->cd = c.take<float>(static_cast<size_t>(T * R));
+  s->dxp = c.take<float>(static_cast<size_t>(T * EX_DH));
+  s->du = c.take<__nv_bfloat16>(static_cast<size_t>(T * (HQ + EX_DH)));
+  s->cnt = c.take<int>(static_cast<size_t>(N));
+  s->offs = c.take<int>(static_cast<size_t>(N));
+  s->cursor = c.take<int>(static_cast<size_t>(N));
+  s->bsums = c.take<int>(1024);
+  s->total = c.take<int>(4);
+  s->perm = c.take<int>(static_cast<size_t>(T * R));
+  s->dP = c.take<__nv_bfloat16>(static_cast<size_t>(N * EX_DH));
+  s->dqhat = c.take<float>(static_cast<size_t>(T * HQ));
+  s->dS = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.num_sub_keys));
+  s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
+  s->part = c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2);
+  s->coef = c.take<float>(static_cast<size_t>(3 * HQ));
+  s->stats = c.take<float>(static_cast<size_t>(2 * HQ));
+  s->dy16 = c.take<__nv_bfloat16>(static_cast<size_t>(T * d.d_model));
+}
+
+__global__ void k_f32_to_bf16(const float* __restrict__ in, int64_t n, __nv_bfloat16* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = __float2bfloat16_rn(in[i]);
+}
+
+template <int TOPK>
+int launch_router_bwd(const ethos_dims& d, const int32_t* ids, const float* w, const float* dw,
+                      const __nv_bfloat16* keys, int64_t key_ld, float* dqhat, __nv_bfloat16* dS, cudaStream_t stream,
+                      const DeviceInfo& dev) {
+  const int TH = static_cast<int>(d.tokens * d.num_heads);
+  int blocks = (TH + 7) / 8;
+  if (blocks > dev.sm_count * 8) blocks = dev.sm_count * 8;
+  k_router_bwd<TOPK><<<blocks, 256, 0, stream>>>(ids, w, dw, keys, key_ld, dqhat, dS, static_cast<int>(d.tokens),
+                                                  static_cast<int>(d.num_heads), static_cast<int>(d.num_sub_keys),
+                                                  static_cast<int>(d.d_query / 2));
+  return launch_status();
 }
 
 }  // namespace
@@ -389,8 +543,8 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
                         const void* w1, const void* wv, int expert_path, void* y, int32_t* ids, float* weights,
                         float* save_xp, void* save_hacc, float* save_dot, float* save_qpre, float* save_bn,
-                        void* workspace, size_t workspace_bytes, int* dev_err, void* const* stage_events,
-                        void* stream) {
+                        void* save_qs, void* workspace, size_t workspace_bytes, int* dev_err,
+                        void* const* stage_events, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (!x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !y || !ids || !weights || !workspace || !dev_err)
@@ -399,7 +553,7 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
   if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(latents) ||
       !aligned16(w1) || !aligned16(wv) || !aligned16(y) || !aligned16(ids) || !aligned16(weights) ||
       !aligned16(workspace) || (save_xp && !aligned16(save_xp)) || (save_hacc && !aligned16(save_hacc)) ||
-      (save_qpre && !aligned16(save_qpre)))
+      (save_qpre && !aligned16(save_qpre)) || (save_qs && !aligned16(save_qs)))
     return ETHOS_ERR_ALIGNMENT;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
@@ -418,8 +572,9 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
   const int T = static_cast<int>(d.tokens);
   void* const* ev = stage_events;
   mark(ev, ETHOS_STAGE_START, stream_);
-  if ((st = router_core(d, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, true, xp, s, qpre,
-                        sbn, dev_err, stream_, *dev, ev)) != ETHOS_OK)
+  __nv_bfloat16* qs = save_qs ? static_cast<__nv_bfloat16*>(save_qs) : s.qs;
+  if ((st = router_core(d, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, true, xp, s, qs,
+                        qpre, save_qpre != nullptr, sbn, dev_err, stream_, *dev, ev)) != ETHOS_OK)
     return st;
   if ((st = run_experts(d, path, latents, w1, ids, weights, xp, hacc, save_dot, s.table, dev_err, stream_, *dev,
                         ev)) != ETHOS_OK)
@@ -459,7 +614,7 @@ int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_ca
   float* qpre = save_qpre ? save_qpre : s.qpre;
   float* sbn = save_bn ? save_bn : s.save_bn;
   return router_core(*dims, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, false, nullptr,
-                     s, qpre, sbn, dev_err, static_cast<cudaStream_t>(stream), *dev);
+                     s, s.qs, qpre, false, sbn, dev_err, static_cast<cudaStream_t>(stream), *dev);
 }
 
 int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* latents, const void* w1,
@@ -514,32 +669,262 @@ int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* ke
 
 int ethos_gemm_bf16(const void* a, const void* b, void* dptr, int64_t M, int64_t N, int64_t K, float scale,
                     int out_dtype, int* dev_err, void* stream) {
+  return ethos_gemm_bf16_ex(a, K, 0, b, K, 0, dptr, N, M, N, K, scale, out_dtype, dev_err, stream);
+}
+
+int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb, int b_mn_major,
+                       void* dptr, int64_t ldd, int64_t M, int64_t N, int64_t K, float scale, int out_mode,
+                       int* dev_err, void* stream) {
   if (!a || !b || !dptr || !dev_err) return ETHOS_ERR_INVALID_ARG;
-  if (M < 1 || N % GEMM_BN != 0 || N < GEMM_BN || K % GEMM_BK != 0 || K < GEMM_BK || M > (int64_t(1) << 30))
+  if (M < 1 || N < 128 || N % 128 != 0 || K < 1 || M > (int64_t(1) << 30) || K > (int64_t(1) << 30))
     return ETHOS_ERR_UNSUPPORTED_SHAPE;
-  if (!aligned16(dptr)) return ETHOS_ERR_ALIGNMENT;
+  if (out_mode < 0 || out_mode > 2) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(dptr) || ldd % 8 != 0) return ETHOS_ERR_ALIGNMENT;
   int st;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
-  CUtensorMap ta, tb;
-  if ((st = make_tmap_bf16(&ta, a, M, K, 128)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tb, b, N, K, 256)) != ETHOS_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (out_dtype == 1) {
+  GemmOperand oa{a, lda, a_mn_major != 0};
+  GemmOperand ob{b, ldb, b_mn_major != 0};
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  if (out_mode == 1) {
     EpiStoreBF16 e;
     e.out = static_cast<__nv_bfloat16*>(dptr);
-    e.ldo = N;
-    e.M = static_cast<int>(M);
+    e.ldo = ldd;
+    e.M = m;
     e.scale = scale;
-    return launch_gemm(ta, tb, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), e, dev_err, s, *dev);
+    return gemm(oa, ob, m, n, k, 1, e, dev_err, s, *dev);
+  }
+  if (out_mode == 2) {
+    EpiAtomicF32 e;
+    e.out = static_cast<float*>(dptr);
+    e.ldo = ldd;
+    e.M = m;
+    e.scale = scale;
+    return gemm(oa, ob, m, n, k, auto_ksplit(m, n, k, *dev), e, dev_err, s, *dev);
   }
   EpiStoreF32 e;
   e.out = static_cast<float*>(dptr);
-  e.ldo = N;
-  e.M = static_cast<int>(M);
+  e.ldo = ldd;
+  e.M = m;
   e.scale = scale;
   e.accumulate = 0;
-  return launch_gemm(ta, tb, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), e, dev_err, s, *dev);
+  return gemm(oa, ob, m, n, k, 1, e, dev_err, s, *dev);
+}
+
+size_t ethos_backward_workspace_size(const ethos_dims* dims) {
+  if (check_dims_impl(dims) != ETHOS_OK) return 0;
+  Carve c{nullptr, 0, 0};
+  BwdScratch s;
+  carve_backward(c, *dims, &s);
+  return c.off + 256;
+}
+
+int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, const void* dy, int dy_fp32,
+                         const void* x, const void* w_cat, const float* bn, const void* key_cat, const void* latents,
+                         const void* w1, const void* wv, const int32_t* ids, const float* weights,
+                         const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
+                         const float* save_bn, const void* save_qs, float* dx, float* d_latents, float* d_w1,
+                         float* d_w2, float* d_wq, float* d_bn, float* d_keys, void* workspace,
+                         size_t workspace_bytes, int* dev_err, void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (d_latents == nullptr && (dims->num_heads * dims->top_k) < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (!dy || !x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !ids || !weights || !save_xp ||
+      !save_hacc || !save_dot || !save_qpre || !save_qs || !dx || !d_latents || !d_w1 || !d_w2 || !d_wq || !d_bn ||
+      !d_keys || !workspace || !dev_err)
+    return ETHOS_ERR_INVALID_ARG;
+  if (bn_training && !save_bn) return ETHOS_ERR_INVALID_ARG;
+  if (dims->num_heads * dims->top_k < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  if (workspace_bytes < ethos_backward_workspace_size(dims)) return ETHOS_ERR_WORKSPACE;
+  const ethos_dims& d = *dims;
+  cudaStream_t sm = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  BwdScratch s;
+  carve_backward(c, d, &s);
+  const int T = static_cast<int>(d.tokens), D = static_cast<int>(d.d_model), N = static_cast<int>(d.num_experts);
+  const int H = static_cast<int>(d.num_heads), R = static_cast<int>(d.num_heads * d.top_k);
+  const int dq = static_cast<int>(d.d_query), HQ = H * dq, K = static_cast<int>(d.num_sub_keys), half = dq / 2;
+  const int LDU = HQ + EX_DH;
+  const float invH = 1.0f / static_cast<float>(H);
+  const int cb = 256;
+  const int eblocks = dev->sm_count * 8;
+
+  // outputs that are accumulated
+  if (cudaMemsetAsync(d_w1, 0, sizeof(float) * EX_DH * EX_DL, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(d_w2, 0, sizeof(float) * 2 * D * EX_DH, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(d_keys, 0, sizeof(float) * 2 * K * half, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(s.cnt, 0, sizeof(int) * N, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(s.dS, 0, sizeof(__nv_bfloat16) * static_cast<size_t>(H) * 2 * T * K, sm) != cudaSuccess)
+    return ETHOS_ERR_CUDA;
+
+  const void* dy16 = dy;
+  if (dy_fp32) {
+    k_f32_to_bf16<<<eblocks, cb, 0, sm>>>(static_cast<const float*>(dy), static_cast<int64_t>(T) * D, s.dy16);
+    dy16 = s.dy16;
+  }
+  // (1) dhacc = dy @ W_v / H            [T, dh]   (W_v read in place, MN-major)
+  {
+    EpiStoreF32 e;
+    e.out = s.dhacc;
+    e.ldo = EX_DH;
+    e.M = T;
+    e.scale = invH;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{dy16, D, false}, GemmOperand{wv, EX_DH, true}, T, EX_DH, D, 1, e, dev_err, sm,
+                   *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (2) dW_v = dy^T hacc / H  -> d_w2[d:]
+  {
+    EpiAtomicF32 e;
+    e.out = d_w2 + static_cast<int64_t>(D) * EX_DH;
+    e.ldo = EX_DH;
+    e.M = D;
+    e.scale = invH;
+    if ((st = gemm(GemmOperand{dy16, D, true}, GemmOperand{save_hacc, EX_DH, true}, D, EX_DH, T,
+                   auto_ksplit(D, EX_DH, T, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (3) per-expert tables H = gelu(E W1^T), G = gelu'(E W1^T)  (fp16)
+  {
+    EpiGeluBwdF16 e;
+    e.h_out = s.htab;
+    e.g_out = s.gtab;
+    e.ldo = EX_DH;
+    e.M = N;
+    if ((st = gemm(GemmOperand{latents, EX_DL, false}, GemmOperand{w1, EX_DL, false}, N, EX_DH, EX_DL, 1, e, dev_err,
+                   sm, *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (4) per token: dw, a, ddot per selection; dxp (fp32 + bf16 into du)
+  {
+    if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather), BGATHER_SMEM_BYTES)) != ETHOS_OK)
+      return st;
+    int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
+    if (blocks > dev->sm_count) blocks = dev->sm_count;
+    k_expert_bwd_gather<<<blocks, GATHER_THREADS, BGATHER_SMEM_BYTES, sm>>>(
+        s.htab, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du, LDU, HQ, T, R, N, dev_err);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  // (5) selections grouped by expert (counting sort)
+  {
+    const int64_t nsel = static_cast<int64_t>(T) * R;
+    k_count_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cnt, dev_err);
+    const int nblk = (N + 1023) / 1024;
+    if (nblk > 1024) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+    k_scan_blocks<<<nblk, 1024, 0, sm>>>(s.cnt, N, s.offs, s.bsums);
+    k_scan_sums<<<1, 1024, 0, sm>>>(s.bsums, nblk, s.total);
+    k_scan_add<<<nblk, 1024, 0, sm>>>(s.offs, N, s.bsums, s.cursor);
+    k_scatter_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cursor, s.perm);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
+  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.dhacc, save_xp, s.gtab, s.dP, N, R);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  // (7) dE = dP W1       (W1 read in place, MN-major)
+  {
+    EpiStoreF32 e;
+    e.out = d_latents;
+    e.ldo = EX_DL;
+    e.M = N;
+    e.scale = 1.0f;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{s.dP, EX_DH, false}, GemmOperand{w1, EX_DL, true}, N, EX_DL, EX_DH, 1, e, dev_err, sm,
+                   *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (8) dW1 = dP^T E     (both read in place, MN-major; split-K over experts)
+  {
+    EpiAtomicF32 e;
+    e.out = d_w1;
+    e.ldo = EX_DL;
+    e.M = EX_DH;
+    e.scale = 1.0f;
+    if ((st = gemm(GemmOperand{s.dP, EX_DH, true}, GemmOperand{latents, EX_DL, true}, EX_DH, EX_DL, N,
+                   auto_ksplit(EX_DH, EX_DL, N, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (9) router: softmax backward, dq^ and the dense sub-key score gradient dS
+  switch (d.top_k) {
+    case 4: st = launch_router_bwd<4>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq, s.dqhat,
+                                     s.dS, sm, *dev); break;
+    case 8: st = launch_router_bwd<8>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq, s.dqhat,
+                                     s.dS, sm, *dev); break;
+    default: st = launch_router_bwd<16>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq,
+                                        s.dqhat, s.dS, sm, *dev); break;
+  }
+  if (st != ETHOS_OK) return st;
+  // (10) dK_p += dS_{h,p}^T q^_{h,p}  (per head and half; q^ = hi part of qs)
+  for (int h = 0; h < H; ++h) {
+    for (int p = 0; p < 2; ++p) {
+      EpiAtomicF32 e;
+      e.out = d_keys + static_cast<int64_t>(p) * K * half;
+      e.ldo = half;
+      e.M = K;
+      e.scale = 1.0f;
+      const __nv_bfloat16* dSp = s.dS + (static_cast<int64_t>(h) * 2 + p) * T * K;
+      const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(save_qs) + (static_cast<int64_t>(h) * 2 + p) * T * dq;
+      if ((st = gemm(GemmOperand{dSp, K, true}, GemmOperand{qh, dq, true}, K, half, T, auto_ksplit(K, half, T, *dev),
+                     e, dev_err, sm, *dev)) != ETHOS_OK)
+        return st;
+    }
+  }
+  // (11) BatchNorm backward -> dq (bf16 into du[:, :HQ]), dbias, dgamma, dbeta
+  {
+    const float* mean = save_bn;
+    const float* invstd = save_bn ? save_bn + HQ : nullptr;
+    if (!bn_training) {
+      k_bn_eval_stats<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, s.stats, s.stats + HQ);
+      mean = s.stats;
+      invstd = s.stats + HQ;
+    }
+    dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+    k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, T, HQ, s.part);
+    k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, invstd,
+                                                        d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
+    k_bn_bwd_apply<<<eblocks, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, s.coef, T, HQ, s.du, LDU);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  // (12) dx = du @ W_cat          (W_cat read in place, MN-major)
+  {
+    EpiStoreF32 e;
+    e.out = dx;
+    e.ldo = D;
+    e.M = T;
+    e.scale = 1.0f;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{s.du, LDU, false}, GemmOperand{w_cat, D, true}, T, D, LDU, 1, e, dev_err, sm,
+                   *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (13) dWq = dq^T x   [HQ, d]
+  {
+    EpiStoreF32 e;
+    e.out = d_wq;
+    e.ldo = D;
+    e.M = HQ;
+    e.scale = 1.0f;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{s.du, LDU, true}, GemmOperand{x, D, true}, HQ, D, T, 1, e, dev_err, sm, *dev)) !=
+        ETHOS_OK)
+      return st;
+  }
+  // (14) dW_u = x^T dxp -> d_w2[:d]   [d, dh]
+  {
+    EpiStoreF32 e;
+    e.out = d_w2;
+    e.ldo = EX_DH;
+    e.M = D;
+    e.scale = 1.0f;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{x, D, true}, GemmOperand{s.du + HQ, LDU, true}, D, EX_DH, T, 1, e, dev_err, sm,
+                   *dev)) != ETHOS_OK)
+      return st;
+  }
+  return ETHOS_OK;
 }
 
 }  // extern "C"

@@ -1,12 +1,19 @@
-// Persistent tcgen05 GEMM  D[M, N] = A[M, K] * B[N, K]^T  (bf16 in, fp32 TMEM
-// accumulate) with a pluggable per-row epilogue.
+// Persistent tcgen05 GEMM  D[M, N] = sum_k A[m, k] * B[n, k]  (bf16 in, fp32
+// TMEM accumulate) with a pluggable per-row epilogue.
 //
+// Operands are either K-major (stored [M][K] / [N][K], K contiguous) or
+// MN-major (stored [K][M] / [K][N], M/N contiguous -- a transposed operand
+// read in place).  Both are staged by TMA with the 128-byte swizzle:
+//   K-major:  one box of 64 K x rows; UMMA steps K by 32 B inside the atom.
+//   MN-major: boxes of 64 M/N x 64 K (8 KB, MN blocks 8 KB apart = LBO),
+//             8-row K groups 1024 B apart (SBO); UMMA steps K by 2 KB.
 // Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
 // issuer, warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31;
-// warps 2-5 take columns 0-127 of the tile, warps 6-9 columns 128-255).
-// Tiles are 128 x 256 x 64 with a 4-stage TMA ring (48 KB per stage, 128-byte
-// swizzle) and two 256-column TMEM accumulators, so the epilogue of tile i
-// overlaps the main loop of tile i+1.
+// warps 2-5 take the first half of the tile's columns, warps 6-9 the second).
+// Tiles are 128 x BN x 64 (BN = 128 or 256) with a TMA ring and two BN-column
+// TMEM accumulators, so the epilogue of tile i overlaps the main loop of tile
+// i+1.  Split-K: work unit u covers tile u % tiles and K blocks of slice
+// u / tiles; split-K epilogues reduce into fp32 with vector atomics.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -16,7 +23,7 @@
 namespace ethos {
 
 constexpr int GEMM_BM = 128;
-constexpr int GEMM_BN = 256;
+constexpr int GEMM_BN = 256;  // widest N tile
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_STAGES = 4;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
@@ -34,7 +41,9 @@ struct GemmCtl {
   uint32_t tmem_base;
   int abort;
 };
-constexpr int GEMM_SMEM_BYTES = GEMM_STAGES * GEMM_STAGE_BYTES + 1024 + static_cast<int>(sizeof(GemmCtl));
+constexpr int GEMM_COLP_BYTES = 2 * 256 * 8;  // double-buffered per-tile column side data
+constexpr int GEMM_SMEM_BYTES =
+    GEMM_STAGES * GEMM_STAGE_BYTES + GEMM_COLP_BYTES + 1024 + static_cast<int>(sizeof(GemmCtl));
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -43,7 +52,15 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // ------------------------------------------------------------- epilogues --
 // Each functor is called per warp-chunk: `row` is this lane's output row and
 // v[0..31] the fp32 accumulators of columns col..col+31.  Rows >= M must be
-// ignored by the functor.
+// ignored by the functor.  A functor with per-column side data declares
+// kColParamBytes > 0 and load_col_params(): before each tile's accumulator is
+// read, the epilogue warps stage the tile's 256 columns of side data into
+// shared memory (double-buffered) and operator() receives it as `cp`
+// (indexed by column - n0).
+struct EpiNoColParams {
+  static constexpr int kColParamBytes = 0;
+  __device__ __forceinline__ void load_col_params(int, uint8_t*, int) const {}
+};
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -51,12 +68,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // out[row, col] = bf16(scale * v)   (row-major, leading dimension ldo)
-struct EpiStoreBF16 {
+struct EpiStoreBF16 : EpiNoColParams {
   __nv_bfloat16* out;
   int64_t ldo;
   int M;
   float scale;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32]) const {
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
     if (row >= M) return;
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ldo + col);
 #pragma unroll
@@ -72,13 +89,13 @@ struct EpiStoreBF16 {
 };
 
 // out[row, col] = scale * v  (fp32), or += when accumulate != 0
-struct EpiStoreF32 {
+struct EpiStoreF32 : EpiNoColParams {
   float* out;
   int64_t ldo;
   int M;
   float scale;
   int accumulate;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32]) const {
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
     if (row >= M) return;
     float4* dst = reinterpret_cast<float4*>(out + static_cast<int64_t>(row) * ldo + col);
 #pragma unroll
@@ -89,6 +106,25 @@ struct EpiStoreF32 {
         o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
       }
       dst[j] = o;
+    }
+  }
+};
+
+// out[row, col] += scale * v  with fp32 vector atomics (split-K partials,
+// gradient accumulation)
+struct EpiAtomicF32 : EpiNoColParams {
+  float* out;
+  int64_t ldo;
+  int M;
+  float scale;
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
+    if (row >= M) return;
+    float* dst = out + static_cast<int64_t>(row) * ldo + col;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst + 4 * j), "f"(v[4 * j] * scale),
+                   "f"(v[4 * j + 1] * scale), "f"(v[4 * j + 2] * scale), "f"(v[4 * j + 3] * scale)
+                   : "memory");
     }
   }
 };
@@ -104,6 +140,7 @@ struct EpiStoreF32 {
 //    statistics pass.
 // x_proj is always written fp32 to xp[row][0..dh).
 struct EpiProj {
+  static constexpr int kColParamBytes = 8;  // float2 (scale, offset) or (bias, -)
   int M;   // tokens
   int HQ;  // H * d_query
   int dq;
@@ -114,7 +151,14 @@ struct EpiProj {
   __nv_bfloat16* qs;
   float* qpre;
   float* xp;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32]) const {
+  // epilogue thread `tid` (0..255) stages column n0 + tid
+  __device__ __forceinline__ void load_col_params(int n0, uint8_t* dst, int tid) const {
+    const int col = n0 + tid;
+    float2 v = make_float2(0.f, 0.f);
+    if (col < HQ) v = mode == 1 ? make_float2(__ldg(bias + col), 0.f) : __ldg(colp + col);
+    reinterpret_cast<float2*>(dst)[tid] = v;
+  }
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t* cp) const {
     if (row >= M) return;
     if (col >= HQ) {
       float4* dst = reinterpret_cast<float4*>(xp + static_cast<int64_t>(row) * dh + (col - HQ));
@@ -122,13 +166,13 @@ struct EpiProj {
       for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       return;
     }
+    const float2* cpc = reinterpret_cast<const float2*>(cp) + (col & 255);
     if (mode == 1) {
       float4* dst = reinterpret_cast<float4*>(qpre + static_cast<int64_t>(row) * HQ + col);
-      const float4* b4 = reinterpret_cast<const float4*>(bias + col);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float4 b = __ldg(b4 + j);
-        dst[j] = make_float4(v[4 * j] + b.x, v[4 * j + 1] + b.y, v[4 * j + 2] + b.z, v[4 * j + 3] + b.w);
+        dst[j] = make_float4(v[4 * j] + cpc[4 * j].x, v[4 * j + 1] + cpc[4 * j + 1].x,
+                             v[4 * j + 2] + cpc[4 * j + 2].x, v[4 * j + 3] + cpc[4 * j + 3].x);
       }
       return;
     }
@@ -138,11 +182,11 @@ struct EpiProj {
     const int p = e >= half ? 1 : 0;
     const int i0 = e - p * half;
     __nv_bfloat16* base = qs + (static_cast<int64_t>(h * 2 + p) * M + row) * dq;
-    const float4* cp4 = reinterpret_cast<const float4*>(colp + col);
+    const float4* cp4 = reinterpret_cast<const float4*>(cpc);
     uint32_t hi[16], lo[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float4 c = __ldg(cp4 + i);
+      const float4 c = cp4[i];
       const float q0 = fmaf(v[2 * i], c.x, c.y);
       const float q1 = fmaf(v[2 * i + 1], c.z, c.w);
       const __nv_bfloat162 h2 = __floats2bfloat162_rn(q0, q1);
@@ -164,11 +208,11 @@ struct EpiProj {
 // Expert hidden table: out[row][col] = fp16(gelu_erf(v)) for the expert-
 // expansion GEMM E @ W1^T (row = expert id, col = hidden unit; model.py:323
 // evaluated once per expert instead of once per selection).
-struct EpiGeluF16 {
+struct EpiGeluF16 : EpiNoColParams {
   __half* out;
   int64_t ldo;
   int M;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32]) const {
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
     if (row >= M) return;
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ldo + col);
 #pragma unroll
@@ -184,20 +228,73 @@ struct EpiGeluF16 {
   }
 };
 
+// Backward tables: H = fp16(gelu_erf(v)) and G = fp16(gelu_erf'(v)) for the
+// pre-activations v = E @ W1^T of every expert.
+struct EpiGeluBwdF16 : EpiNoColParams {
+  __half* h_out;
+  __half* g_out;
+  int64_t ldo;
+  int M;
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
+    if (row >= M) return;
+    uint4* dh = reinterpret_cast<uint4*>(h_out + static_cast<int64_t>(row) * ldo + col);
+    uint4* dg = reinterpret_cast<uint4*>(g_out + static_cast<int64_t>(row) * ldo + col);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t wh[4], wg[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float a = v[8 * j + 2 * u], b = v[8 * j + 2 * u + 1];
+        const __half2 hh = __floats2half2_rn(gelu_erf(a), gelu_erf(b));
+        const __half2 gg = __floats2half2_rn(gelu_erf_grad(a), gelu_erf_grad(b));
+        wh[u] = *reinterpret_cast<const uint32_t*>(&hh);
+        wg[u] = *reinterpret_cast<const uint32_t*>(&gg);
+      }
+      dh[j] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+      dg[j] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+    }
+  }
+};
+
 // ---------------------------------------------------------------- kernel --
-template <class Epi>
+// Shared-memory descriptor of an MN-major operand in the 128-byte swizzle
+// canonical layout: 64-element MN rows of 128 B per K index, 8 K rows per
+// 1024-B atom (SBO = 1024), consecutive 64-element MN blocks `lbo` bytes
+// apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32_major(int M, int N, bool a_mn, bool b_mn) {
+  return umma_idesc_bf16_f32(M, N) | (a_mn ? (1u << 15) : 0u) | (b_mn ? (1u << 16) : 0u);
+}
+
+template <class Epi, bool kAMN, bool kBMN, int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, Epi epi, int* err) {
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+           int ksplit, Epi epi, int* err) {
+  static_assert(BN == 128 || BN == 256, "N tile is 128 or 256");
+  constexpr int B_BYTES = BN * GEMM_BK * 2;
+  constexpr int STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
+  constexpr int CHUNKS_PER_HALF = BN / 64;  // 32-column chunks per epilogue column half
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
+  uint8_t* colp_s = smem + GEMM_STAGES * GEMM_STAGE_BYTES;
+  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(colp_s + GEMM_COLP_BYTES);
   const int warp = warp_id();
   const int lane = lane_id();
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
-  const int num_n = N / GEMM_BN;
+  const int num_n = N / BN;
   const int num_tiles = num_m * num_n;
-  const int num_k = K / GEMM_BK;
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  const int kpb = (num_kb + ksplit - 1) / ksplit;  // K blocks per split (host guarantees none is empty)
+  const int num_units = num_tiles * ksplit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < GEMM_STAGES; ++s) {
@@ -213,7 +310,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_alloc(&ctl->tmem_base, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -228,18 +325,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tma_prefetch_desc(&tmB);
       RingPos rp;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+        const int tile = u % num_tiles;
+        const int ks = u / num_tiles;
         const int m0 = (tile / num_n) * GEMM_BM;
-        const int n0 = (tile % num_n) * GEMM_BN;
-        for (int kb = 0; kb < num_k; ++kb) {
+        const int n0 = (tile % num_n) * BN;
+        const int kb1 = min(num_kb, (ks + 1) * kpb);
+        for (int kb = ks * kpb; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->empty[rp.stage], rp.phase ^ 1u, abort, err, 1)) {
             ok = false;
             break;
           }
           uint8_t* sa = smem + rp.stage * GEMM_STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[rp.stage], GEMM_STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &ctl->full[rp.stage], kb * GEMM_BK, m0);
-          tma_load_2d(sa + GEMM_A_BYTES, &tmB, &ctl->full[rp.stage], kb * GEMM_BK, n0);
+          uint8_t* sb = sa + GEMM_A_BYTES;
+          mbar_arrive_expect_tx(&ctl->full[rp.stage], STAGE_BYTES);
+          if (kAMN) {
+            tma_load_2d(sa, &tmA, &ctl->full[rp.stage], m0, kb * GEMM_BK);
+            tma_load_2d(sa + 8192, &tmA, &ctl->full[rp.stage], m0 + 64, kb * GEMM_BK);
+          } else {
+            tma_load_2d(sa, &tmA, &ctl->full[rp.stage], kb * GEMM_BK, m0);
+          }
+          if (kBMN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * 8192, &tmB, &ctl->full[rp.stage], n0 + 64 * j, kb * GEMM_BK);
+          } else {
+            tma_load_2d(sb, &tmB, &ctl->full[rp.stage], kb * GEMM_BK, n0);
+          }
           rp.advance(GEMM_STAGES);
         }
       }
@@ -247,12 +359,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16_f32(GEMM_BM, GEMM_BN);
+      const uint32_t idesc = umma_idesc_bf16_f32_major(GEMM_BM, BN, kAMN, kBMN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;  // false once this role gave up (abort or timeout)
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++it) {
+      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x, ++it) {
+        const int ks = u / num_tiles;
+        const int kb0 = ks * kpb, kb1 = min(num_kb, (ks + 1) * kpb);
         const int buf = it & 1;
         const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
         if (!mbar_wait(&ctl->acc_empty[buf], acc_phase ^ 1u, abort, err, 2)) {
@@ -260,8 +374,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(buf * GEMM_BN);
-        for (int kb = 0; kb < num_k; ++kb) {
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->full[stage], phase, abort, err, 3)) {
             ok = false;
             break;
@@ -271,8 +385,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t b_base = a_base + GEMM_A_BYTES;
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
-            umma_bf16(d, umma_desc_sw128(a_base + k * 32), umma_desc_sw128(b_base + k * 32), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
+            const uint64_t ad = kAMN ? umma_desc_sw128_mn(a_base + k * 2048, 8192) : umma_desc_sw128(a_base + k * 32);
+            const uint64_t bd = kBMN ? umma_desc_sw128_mn(b_base + k * 2048, 8192) : umma_desc_sw128(b_base + k * 32);
+            umma_bf16(d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&ctl->empty[stage]);
           if (++stage == GEMM_STAGES) {
@@ -290,23 +405,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
+    // Epilogue warps never leave the unit loop early: after an abort they skip
+    // the work but still take every named barrier, so no partner can block.
     const int q = warp & 3;
     const int ch = (warp - 2) >> 2;  // column half of the tile
     int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+      const int tile = u % num_tiles;
       const int buf = it & 1;
       const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
       const int m0 = (tile / num_n) * GEMM_BM;
-      const int n0 = (tile % num_n) * GEMM_BN;
-      const bool ok = mbar_wait(&ctl->acc_full[buf], acc_phase, abort, err, 4);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      const int n0 = (tile % num_n) * BN;
+      uint8_t* cps = colp_s + buf * 256 * 8;
+      if (Epi::kColParamBytes > 0) {
+        // stage this tile's column data (its previous user, unit it-2, was
+        // released by the barrier of unit it-1)
+        epi.load_col_params(n0, cps, static_cast<int>(threadIdx.x) - 64);
+        named_bar_sync(1, GEMM_EPI_THREADS);
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], acc_phase, abort, err, 4));
+      if (!ok) continue;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-      for (int c = ch * 4; c < ch * 4 + 4; ++c) {
+      for (int c = ch * CHUNKS_PER_HALF; c < (ch + 1) * CHUNKS_PER_HALF; ++c) {
         float v[32];
-        tmem_ld32(tmem_addr(tmem, q * 32, buf * GEMM_BN + c * 32), v);
-        epi(row, n0 + c * 32, v);
+        tmem_ld32(tmem_addr(tmem, q * 32, buf * BN + c * 32), v);
+        epi(row, n0 + c * 32, v, cps);
       }
       tc_fence_before();
       mbar_arrive(&ctl->acc_empty[buf]);
@@ -319,7 +445,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 

@@ -524,10 +524,12 @@ __global__ void k_bn_finalize(const float* __restrict__ qpre, const float* __res
 
 // Eval-mode per-column (scale, offset) from the bias and running statistics:
 // ((v + bias) - rm) * gamma / sqrt(rv + eps) + beta = v * scale + offset.
-__global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, float2* __restrict__ colp) {
+// With on_qpre != 0 the affine applies to qpre = v + bias instead.
+__global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, int on_qpre,
+                               float2* __restrict__ colp) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= C) return;
-  const float bias = bn[col], gamma = bn[1 * C + col], beta = bn[2 * C + col];
+  const float bias = on_qpre ? 0.f : bn[col], gamma = bn[1 * C + col], beta = bn[2 * C + col];
   const float rm = bn[3 * C + col], rv = bn[4 * C + col];
   const float scale = gamma / sqrtf(rv + eps);
   colp[col] = make_float2(scale, beta - (rm - bias) * scale);

@@ -155,6 +155,8 @@ class _EthosLayerFunction(torch.autograd.Function):
             layer.router._write_back_running(pw.bn)
         ctx.layer = layer
         ctx.training_bn = training
+        ctx.x_dtype = x2d.dtype
+        ctx.params = params
         if need_grad:
             ctx.saved = dict(out, x16=x16, pw=pw)
         return out["y"].to(x2d.dtype)

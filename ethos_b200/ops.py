@@ -12,8 +12,8 @@ import torch
 from ._lib import EthosDims, EthosError, check, lib
 
 __all__ = [
-    "make_dims", "gemm_bf16", "product_key_topk", "expert_forward", "router_forward", "layer_forward",
-    "device_error_word", "check_device_error", "PackedWeights",
+    "make_dims", "gemm_bf16", "gemm_ex", "product_key_topk", "expert_forward", "router_forward", "layer_forward",
+    "device_error_word", "check_device_error", "PackedWeights", "layer_backward",
 ]
 
 _ERR_WORDS = {}
@@ -86,6 +86,32 @@ def gemm_bf16(a, b, scale=1.0, out_dtype=torch.float32):
     check(lib().ethos_gemm_bf16(_vp(a), _vp(b), _vp(out), M, N, K, float(scale),
                                 1 if out_dtype == torch.bfloat16 else 0, _vp(err), _stream(a.device)),
           "ethos_gemm_bf16")
+    return out
+
+
+def gemm_ex(a, b, a_mn=False, b_mn=False, out=None, mode="f32", scale=1.0):
+    """General tcgen05 GEMM ``D[m, n] = scale * sum_k A(m, k) B(n, k)``.
+
+    ``a`` is ``[M, K]`` (K-major) or ``[K, M]`` (``a_mn=True``, read in place);
+    ``b`` is ``[N, K]`` or ``[K, N]`` (``b_mn=True``).  ``mode``: "f32" or
+    "bf16" (store) or "acc" (fp32 ``out +=``, split-K atomics)."""
+    _require_cuda(a, "a")
+    _require_cuda(b, "b")
+    if a.stride(-1) != 1 or b.stride(-1) != 1:
+        raise ValueError("operands must have unit stride in their last dimension")
+    K, M = (a.shape[0], a.shape[1]) if a_mn else (a.shape[1], a.shape[0])
+    N = b.shape[1] if b_mn else b.shape[0]
+    Kb = b.shape[0] if b_mn else b.shape[1]
+    if Kb != K:
+        raise ValueError(f"K mismatch {K} vs {Kb}")
+    om = {"f32": 0, "bf16": 1, "acc": 2}[mode]
+    if out is None:
+        dt = torch.bfloat16 if mode == "bf16" else torch.float32
+        out = (torch.zeros if mode == "acc" else torch.empty)((M, N), dtype=dt, device=a.device)
+    err = device_error_word(a.device)
+    check(lib().ethos_gemm_bf16_ex(_vp(a), a.stride(0), int(a_mn), _vp(b), b.stride(0), int(b_mn), _vp(out),
+                                   out.stride(0), M, N, K, float(scale), om, _vp(err), _stream(a.device)),
+          "ethos_gemm_bf16_ex")
     return out
 
 
@@ -196,8 +222,9 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
         out["xp"] = torch.empty((T, dh), dtype=torch.float32, device=dev)
         out["hacc"] = torch.empty((T, dh), dtype=torch.bfloat16, device=dev)
         out["dot"] = torch.empty((T, H * k), dtype=torch.float32, device=dev)
+        out["qpre"] = torch.empty((T, HQ), dtype=torch.float32, device=dev)
+        out["qs"] = torch.empty((H, 2, T, d["d_query"]), dtype=torch.bfloat16, device=dev)
         if bn_training:
-            out["qpre"] = torch.empty((T, HQ), dtype=torch.float32, device=dev)
             out["bn_stats"] = torch.empty((2, HQ), dtype=torch.float32, device=dev)
     g = out.get
     err = device_error_word(dev)
@@ -206,7 +233,48 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
                                 _vp(pw.w1), _vp(pw.wv), int(path), _vp(out["y"]), _vp(out["ids"]),
                                 _vp(out["weights"]),
                                 _vp(g("xp")), _vp(g("hacc")), _vp(g("dot")), _vp(g("qpre")),
-                                _vp(g("bn_stats")), _vp(ws), ws_bytes, _vp(err), _events(stage_events),
+                                _vp(g("bn_stats")), _vp(g("qs")), _vp(ws), ws_bytes, _vp(err), _events(stage_events),
                                 _stream(dev)),
           "ethos_layer_forward")
     return out
+
+
+def layer_backward(dy, x16, pw, saved, bn_training, eps):
+    """Gradients of the layer (see ethos_layer_backward).  ``dy`` [T, d] bf16
+    or fp32; ``saved`` is the dict returned by ``layer_forward(save=True)``.
+    Returns a dict of fp32 tensors: dx, d_latents, d_w1, d_w2, d_wq [H*dq, d],
+    d_bn [3, H*dq] (bias, gamma, beta), d_keys [2, K, dq/2]."""
+    _require_cuda(dy, "dy")
+    d = pw.dims
+    T = dy.shape[0]
+    dev = dy.device
+    dims = make_dims(T, d)
+    L = lib()
+    ws_bytes = L.ethos_backward_workspace_size(ctypes.byref(dims))
+    if ws_bytes == 0:
+        check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    HQ = d["num_heads"] * d["d_query"]
+    f32 = dict(dtype=torch.float32, device=dev)
+    g = dict(
+        dx=torch.empty((T, d["d_model"]), **f32),
+        d_latents=torch.empty((d["num_experts"], d["d_latent"]), **f32),
+        d_w1=torch.empty((d["d_hidden"], d["d_latent"]), **f32),
+        d_w2=torch.empty((2 * d["d_model"], d["d_hidden"]), **f32),
+        d_wq=torch.empty((HQ, d["d_model"]), **f32),
+        d_bn=torch.empty((3, HQ), **f32),
+        d_keys=torch.empty((2, d["num_sub_keys"], d["d_query"] // 2), **f32),
+    )
+    dy = dy.contiguous()
+    if dy.dtype not in (torch.bfloat16, torch.float32):
+        dy = dy.float()
+    err = device_error_word(dev)
+    check(L.ethos_layer_backward(ctypes.byref(dims), 1 if bn_training else 0, float(eps), _vp(dy),
+                                 1 if dy.dtype == torch.float32 else 0, _vp(x16), _vp(pw.w_cat), _vp(pw.bn),
+                                 _vp(pw.key_cat), _vp(pw.latents), _vp(pw.w1), _vp(pw.wv), _vp(saved["ids"]),
+                                 _vp(saved["weights"]), _vp(saved["xp"]), _vp(saved["hacc"]), _vp(saved["dot"]),
+                                 _vp(saved["qpre"]), _vp(saved.get("bn_stats")), _vp(saved["qs"]), _vp(g["dx"]),
+                                 _vp(g["d_latents"]), _vp(g["d_w1"]), _vp(g["d_w2"]), _vp(g["d_wq"]),
+                                 _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws), ws_bytes, _vp(err), _stream(dev)),
+          "ethos_layer_backward")
+    return g

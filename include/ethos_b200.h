@@ -131,15 +131,16 @@ size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path);
  *  save_*    optional (may be NULL) tensors kept for the backward pass:
  *            save_xp fp32 [T, dh] (x @ W_u), save_hacc bf16 [T, dh]
  *            (sum_{h,k} a*h), save_dot fp32 [T, H*k] (h . x_proj),
- *            save_qpre fp32 [T, H*dq] (pre-BatchNorm queries; training only),
- *            save_bn fp32 [2, H*dq] (batch mean, 1/sqrt(var+eps); training only)
+ *            save_qpre fp32 [T, H*dq] (pre-BatchNorm queries, x Wq^T + b),
+ *            save_bn fp32 [2, H*dq] (batch mean, 1/sqrt(var+eps); training only),
+ *            save_qs bf16 [H, 2, T, dq] (normalised queries, split hi | lo)
  */
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
                         const void* w1, const void* wv, int expert_path, void* y, int32_t* ids,
                         float* weights, float* save_xp, void* save_hacc, float* save_dot,
-                        float* save_qpre, float* save_bn, void* workspace, size_t workspace_bytes,
-                        int* dev_err, void* const* stage_events, void* stream);
+                        float* save_qpre, float* save_bn, void* save_qs, void* workspace,
+                        size_t workspace_bytes, int* dev_err, void* const* stage_events, void* stream);
 
 /* Router alone: ProductKeyRouter.forward (model.py:208-254) on x [T, d]
  * (bf16).  Arguments as for ethos_layer_forward; w_cat needs only its first
@@ -172,11 +173,48 @@ int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* la
 int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* keys, int32_t* ids,
                            float* weights, int* dev_err, void* stream);
 
+/* ------------------------------------------------------- backward -- */
+/* Scratch bytes needed by ethos_layer_backward. */
+size_t ethos_backward_workspace_size(const ethos_dims* dims);
+
+/* Backward of ethos_layer_forward: the gradients autograd computes through
+ * SimplifiedHypernetMoE.forward (model.py:288-343) including the router
+ * (model.py:208-254) and its BatchNorm.  Needs num_heads * top_k >= 16.
+ *  dy         [T, d] bf16 (dy_fp32 = 0) or fp32 (dy_fp32 = 1): dL/dy
+ *  x, w_cat, bn, key_cat, latents, w1, wv, ids, weights: as passed to /
+ *             returned by the forward call; bn_training as in the forward
+ *  save_*     the forward's save buffers (all required; save_bn in training)
+ * Outputs (fp32, overwritten):
+ *  dx        [T, d]
+ *  d_latents [N, dl]        expert_latents.weight
+ *  d_w1      [dh, dl]       generation_network.net.0.weight
+ *  d_w2      [2d, dh]       generation_network.net.2.weight
+ *  d_wq      [H*dq, d]      query_projs[h].weight stacked
+ *  d_bn      [3, H*dq]      query_projs bias, query_norms weight, bias
+ *  d_keys    [2, K, dq/2]   sub_keys_1.weight, sub_keys_2.weight */
+int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, const void* dy, int dy_fp32,
+                         const void* x, const void* w_cat, const float* bn, const void* key_cat, const void* latents,
+                         const void* w1, const void* wv, const int32_t* ids, const float* weights,
+                         const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
+                         const float* save_bn, const void* save_qs, float* dx, float* d_latents, float* d_w1,
+                         float* d_w2, float* d_wq, float* d_bn, float* d_keys, void* workspace,
+                         size_t workspace_bytes, int* dev_err, void* stream);
+
 /* Plain bf16 GEMM D[M, N] = A[M, K] B[N, K]^T * scale on the tcgen05 path
  * (fp32 accumulate), used by the layer and exposed for tests.  out_dtype 0 =
- * fp32, 1 = bf16.  M >= 1, N % 256 == 0, K % 64 == 0. */
+ * fp32, 1 = bf16.  M >= 1, N % 128 == 0, K % 8 == 0. */
 int ethos_gemm_bf16(const void* a, const void* b, void* d, int64_t M, int64_t N, int64_t K, float scale,
                     int out_dtype, int* dev_err, void* stream);
+
+/* General form: D[m, n] (=|+=) scale * sum_k A(m, k) B(n, k).
+ *  a_mn_major = 0: A stored [M][K] (row pitch lda); 1: A stored [K][M]
+ *  b_mn_major = 0: B stored [N][K] (row pitch ldb); 1: B stored [K][N]
+ *  out_mode 0: D fp32 = ..., 1: D bf16 = ..., 2: D fp32 += ... (atomic,
+ *  split-K over K when the output has few tiles); D row pitch ldd.
+ * Row pitches and base pointers must be 16-byte aligned. */
+int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb, int b_mn_major,
+                       void* d, int64_t ldd, int64_t M, int64_t N, int64_t K, float scale, int out_mode,
+                       int* dev_err, void* stream);
 
 #ifdef __cplusplus
 }

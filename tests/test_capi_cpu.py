@@ -97,8 +97,12 @@ def test_workspace_size(L):
 def test_null_arguments_rejected_without_gpu(L):
     d = _dims()
     st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None, 0,
-                               None, None, None, None, None, None, None, None, None, 0, None, None, None)
+                               None, None, None, None, None, None, None, None, None, None, 0, None, None, None)
     assert st == 1  # ETHOS_ERR_INVALID_ARG
+    st = L.ethos_layer_backward(ctypes.byref(d), 0, 1e-5, None, 0, *([None] * 15), *([None] * 7), None, 0,
+                                None, None)
+    assert st == 1
+    assert L.ethos_backward_workspace_size(ctypes.byref(d)) > 2 * 512 * 512 * 512 * 2
 
 
 def test_no_cpu_fallback():

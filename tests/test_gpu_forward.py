@@ -75,6 +75,24 @@ def test_gemm_bf16_matches_torch(M, N, K):
     ops.check_device_error("cuda")
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(296, 256, 192), (512, 128, 1000), (136, 384, 4096)])
+def test_gemm_ex_majors_and_split_k(a_mn, b_mn, M, N, K):
+    """MN-major operands (read in place, transposed) and split-K accumulation."""
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    ref = A.double() @ B.double().t()
+    d = ops.gemm_ex(a, b, a_mn=a_mn, b_mn=b_mn)
+    assert rel_err(d, ref) <= 1e-5
+    acc = torch.full((M, N), 1.5, device="cuda")
+    ops.gemm_ex(a, b, a_mn=a_mn, b_mn=b_mn, out=acc, mode="acc", scale=0.25)
+    assert rel_err(acc, ref * 0.25 + 1.5) <= 1e-5
+    ops.check_device_error("cuda")
+
+
 # --------------------------------------------------- product-key top-k --
 @pytest.mark.parametrize("T,K,dq,top_k", [(4096, 512, 256, 16), (65536, 512, 256, 16), (1000, 64, 256, 16),
                                           (777, 512, 256, 8), (300, 128, 256, 4)])
