@@ -15,7 +15,8 @@ __all__ = ["EthosDims", "EthosError", "EthosLibraryError", "lib", "check", "EXPO
 STATUS = {
     0: "ETHOS_OK", 1: "ETHOS_ERR_INVALID_ARG", 2: "ETHOS_ERR_UNSUPPORTED_SHAPE",
     3: "ETHOS_ERR_ALIGNMENT", 4: "ETHOS_ERR_WORKSPACE", 5: "ETHOS_ERR_CUDA",
-    6: "ETHOS_ERR_TENSOR_MAP", 7: "ETHOS_ERR_NO_DEVICE", 16: "ETHOS_ERR_ID_OUT_OF_RANGE",
+    6: "ETHOS_ERR_TENSOR_MAP", 7: "ETHOS_ERR_NO_DEVICE", 8: "ETHOS_ERR_SCRATCH_LIMIT",
+    16: "ETHOS_ERR_ID_OUT_OF_RANGE",
 }
 ETHOS_ERR_TIMEOUT_BASE = 1000
 
@@ -64,6 +65,7 @@ EXPORTS = {
     "ethos_router_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _P, _P, _SZ,
                                   _P, _P]),
     "ethos_expert_forward": (_I, [_DIMS, _I, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "ethos_router_forward_noalloc": (_I, [_DIMS, _P, _P, _P, _F, _P, _P, _P, _P, _P]),
     "ethos_product_key_topk": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _F, _I, _P, _P]),
     "ethos_gemm_bf16_ex": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _F, _I, _P, _P]),

@@ -17,6 +17,12 @@
 
 using namespace ethos;
 
+// Scratch of ethos_router_forward_noalloc: the only device memory that entry
+// point uses besides the caller's inputs and outputs.  In host code this name
+// is a host-side stand-in, not a device address; noalloc_scratch() resolves
+// the device address once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ETHOS_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 constexpr int kAbiVersion = 1;
@@ -504,6 +510,7 @@ const char* ethos_status_string(int status) {
     case ETHOS_ERR_CUDA: return "CUDA runtime error";
     case ETHOS_ERR_TENSOR_MAP: return "tensor map encoding failed";
     case ETHOS_ERR_NO_DEVICE: return "no sm_100 device is current";
+    case ETHOS_ERR_SCRATCH_LIMIT: return "request exceeds the static scratch of the no-allocation entry point";
     case ETHOS_ERR_ID_OUT_OF_RANGE: return "expert id out of range (device)";
     default:
       if (status >= ETHOS_ERR_TIMEOUT_BASE) return "bounded device wait timed out";
@@ -710,6 +717,62 @@ int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b
   e.scale = scale;
   e.accumulate = 0;
   return gemm(oa, ob, m, n, k, 1, e, dev_err, s, *dev);
+}
+
+}  // extern "C"
+
+namespace {
+// Device address of g_noalloc_scratch for the current device, looked up on
+// the first call per device (with that device current) and cached.
+void* noalloc_scratch(int* status) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = ETHOS_ERR_NO_DEVICE;
+    return nullptr;
+  }
+  static std::mutex mu;
+  static void* addr[64];
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *status = ETHOS_ERR_CUDA;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *status = ETHOS_OK;
+  return addr[dev];
+}
+}  // namespace
+
+extern "C" {
+
+int ethos_router_forward_noalloc(const ethos_dims* dims, const void* x, const void* w_cat, const float* bn,
+                                 float bn_eps, const void* key_cat, int32_t* ids, float* weights, int* dev_err,
+                                 void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!x || !w_cat || !bn || !key_cat || !ids || !weights || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(ids) ||
+      !aligned16(weights))
+    return ETHOS_ERR_ALIGNMENT;
+  const ethos_dims& d = *dims;
+  const size_t HQ = static_cast<size_t>(d.num_heads * d.d_query);
+  const size_t colp_bytes = (HQ * sizeof(float2) + 255) & ~static_cast<size_t>(255);
+  const size_t qs_bytes = static_cast<size_t>(d.tokens) * HQ * 2 * sizeof(__nv_bfloat16);
+  if (colp_bytes + qs_bytes > ETHOS_NOALLOC_SCRATCH_BYTES) return ETHOS_ERR_SCRATCH_LIMIT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  char* scratch = static_cast<char*>(noalloc_scratch(&st));
+  if (st != ETHOS_OK) return st;
+  FwdScratch s{};
+  s.colp = reinterpret_cast<float2*>(scratch);
+  s.qs = reinterpret_cast<__nv_bfloat16*>(scratch + colp_bytes);
+  s.slabs = 0;
+  return router_core(d, x, w_cat, const_cast<float*>(bn), bn_eps, 0.f, 0, key_cat, ids, weights, false, nullptr, s,
+                     s.qs, nullptr, false, nullptr, dev_err, static_cast<cudaStream_t>(stream), *dev);
 }
 
 size_t ethos_backward_workspace_size(const ethos_dims* dims) {

@@ -42,6 +42,7 @@ extern "C" {
 #define ETHOS_ERR_CUDA 5              /* a CUDA runtime call failed           */
 #define ETHOS_ERR_TENSOR_MAP 6        /* cuTensorMapEncodeTiled failed        */
 #define ETHOS_ERR_NO_DEVICE 7         /* no sm_100 device current             */
+#define ETHOS_ERR_SCRATCH_LIMIT 8     /* request exceeds the static scratch   */
 /* device-side codes (reported through dev_err) */
 #define ETHOS_ERR_ID_OUT_OF_RANGE 16  /* an expert id outside [0, N)          */
 #define ETHOS_ERR_TIMEOUT_BASE 1000   /* + site: a bounded wait gave up       */
@@ -163,6 +164,35 @@ int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_ca
 int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* latents, const void* w1,
                          const int32_t* ids, const float* weights, const float* xp, void* hacc, float* dot,
                          void* workspace, size_t workspace_bytes, int* dev_err, void* stream);
+
+/* Router forward that allocates nothing (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory per call: a host that runs
+ * under a fixed memory plan reserved at start-up (a serving process that must
+ * not grow or fragment its device heap mid-request), or an embedding runtime
+ * that hands this library its input and output buffers but owns no device
+ * allocator of its own.  Same computation as ethos_router_forward with
+ * BatchNorm in eval mode (running statistics); its scratch -- the split-bf16
+ * scoring operand and the folded per-column BatchNorm affine -- lives in a
+ * file-scope static device array of ETHOS_NOALLOC_SCRATCH_BYTES that every
+ * GPU loading this library holds until process exit.
+ *  - Limit: tokens * num_heads * d_query * 4 + num_heads * d_query * 8 plus
+ *    alignment must fit the array (258 tokens at 8 heads x d_query 512);
+ *    larger requests return ETHOS_ERR_SCRATCH_LIMIT and launch nothing.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array: calls that overlap on the GPU (other
+ *    streams, other host threads) race and must be serialised by the caller.
+ *    Nothing in the array needs to start zeroed: every call fully rewrites
+ *    the parts it reads.
+ * Arguments as for ethos_router_forward (x bf16 [T, d], w_cat first H*dq
+ * rows, bn fp32 [5, H*dq] read only, key_cat bf16 [2, K, dq]); outputs
+ * ids int32 [T, H, k] and fp32 softmax weights [T, H, k]. */
+#define ETHOS_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u + 64u * 1024u)
+int ethos_router_forward_noalloc(const ethos_dims* dims, const void* x, const void* w_cat, const float* bn,
+                                 float bn_eps, const void* key_cat, int32_t* ids, float* weights, int* dev_err,
+                                 void* stream);
 
 /* Product-key top-k from already normalised queries (the scoring, per-half
  * top-k, candidate-grid top-k, softmax and id decode of model.py:217-245).
