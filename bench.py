@@ -204,6 +204,69 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_train(args, rank, world, local, dev):
+    """Config 5: one training step per iteration -- forward (BatchNorm in
+    training mode), backward through all 37 parameters, NCCL all-reduce of
+    the gradients (world > 1) and an SGD update, 16384 tokens per GPU."""
+    import torch.distributed as dist
+    from ethos_b200 import ops
+    from ethos_b200.dist import GradAllReducer
+    from ethos_b200.init import seeded_input, tensor_generator
+    layer = build_layer(dev).train()
+    T = args.tokens
+    x = seeded_input(T, CFG2["d_model"], seed=rank).to(device=dev, dtype=torch.bfloat16)
+    gy = (torch.randn((T, CFG2["d_model"]), generator=tensor_generator(rank, "bench.gy")) * 1e-3).to(
+        device=dev, dtype=torch.bfloat16)
+    opt = torch.optim.SGD(layer.parameters(), lr=1e-3)
+    reducer = GradAllReducer(list(layer.parameters())) if world > 1 else None
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        y = layer(x.view(1, T, -1))
+        y.backward(gy.view(1, T, -1))
+        if reducer is not None:
+            reducer()
+        opt.step()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_device_error(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for s_, e_ in ev:
+        flush.zero_()
+        s_.record(stream)
+        step()
+        e_.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    if rank == 0:
+        line = dict(metric="expert-layer training tokens/s (262K experts, k=16x8 heads)",
+                    value=T * world / (ms / 1e3), unit=UNIT, n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
+                    vs_baseline=None, dtype="bf16", data="synthetic",
+                    config=dict(workload="config 5: ETHOS expert layer training step (forward, backward, "
+                                         "gradient all-reduce, SGD update), BN train mode",
+                                tokens_per_gpu=T, global_batch=T * world, parallelism=f"dp{world}",
+                                l2="flushed between timed steps (256 MiB write)"),
+                    clocks=clocks)
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -213,6 +276,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
+    ap.add_argument("--mode", default="forward", choices=["forward", "train"],
+                    help="forward: config 2 (headline); train: config 5 training step")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -230,6 +295,13 @@ def main():
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    if args.mode == "train":
+        run_train(args, rank, world, local, dev)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     from ethos_b200 import ops
     from ethos_b200.init import seeded_input

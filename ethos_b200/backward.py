@@ -1,8 +1,8 @@
 """Autograd backward of EthosExpertLayer.
 
 Maps the gradients computed by ``ethos_layer_backward`` (one C-ABI call, see
-include/ethos_b200.h) onto the inputs of ``_EthosLayerFunction``: x, then the
-parameters in the order of ``EthosExpertLayer._grad_params`` --
+include/ethos_b200.h) onto the inputs of ``_EthosLayerFunction``: x, the layer
+and the need-grad flag (no gradients), then the parameters in the order of ``EthosExpertLayer._grad_params`` --
 expert_latents, net.0, net.2, query_projs weights, query_projs biases,
 query_norms weights, query_norms biases, sub_keys_1, sub_keys_2.
 """
@@ -26,8 +26,8 @@ def layer_backward(ctx, gy):
     flat += [g["d_bn"][1, h * dq:(h + 1) * dq] for h in range(H)]
     flat += [g["d_bn"][2, h * dq:(h + 1) * dq] for h in range(H)]
     flat += [g["d_keys"][0], g["d_keys"][1]]
-    out = [grads[0], None]  # x, layer (not a tensor)
-    for p, gp, need in zip(params, flat, ctx.needs_input_grad[2:]):
+    out = [grads[0], None, None]  # x, layer, need_grad (not tensors)
+    for p, gp, need in zip(params, flat, ctx.needs_input_grad[3:]):
         out.append(gp.to(p.dtype).view_as(p) if need else None)
     ctx.saved = None
     return tuple(out)

@@ -144,11 +144,12 @@ class _EthosLayerFunction(torch.autograd.Function):
     """Autograd boundary around the fused forward (and backward) kernels."""
 
     @staticmethod
-    def forward(ctx, x2d, layer, *params):
+    def forward(ctx, x2d, layer, need_grad, *params):
+        # need_grad is decided by the caller: inside Function.forward grad
+        # mode is always off and needs_input_grad ignores torch.no_grad()
         pw = layer._packed(x2d.device)
         eps, mom = layer.router._bn_eps_momentum()
         training = layer.router._bn_training()
-        need_grad = any(ctx.needs_input_grad)
         x16 = x2d.to(torch.bfloat16).contiguous()
         out = ops.layer_forward(x16, pw, training, eps, mom, save=need_grad, path=layer.expert_path)
         if training:
@@ -239,7 +240,9 @@ class EthosExpertLayer(nn.Module):
         ops._require_cuda(x, "x")
         batch_size, seq_len, d_model = x.shape
         x2d = x.reshape(-1, d_model)
-        y = _EthosLayerFunction.apply(x2d, self, *self._grad_params())
+        params = self._grad_params()
+        need_grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in params))
+        y = _EthosLayerFunction.apply(x2d, self, need_grad, *params)
         return y.view(batch_size, seq_len, d_model)
 
 
