@@ -7,6 +7,8 @@ expert_latents, net.0, net.2, query_projs weights, query_projs biases,
 query_norms weights, query_norms biases, sub_keys_1, sub_keys_2.
 """
 
+import torch
+
 from . import ops
 
 
@@ -20,6 +22,11 @@ def layer_backward(ctx, gy):
     g = ops.layer_backward(gy.reshape(-1, gy.shape[-1]), sv["x16"], pw, sv, ctx.training_bn, eps)
     params = ctx.params
     grads = [g["dx"].to(ctx.x_dtype)]
+    dtypes = {p.dtype for p in params}
+    if len(dtypes) == 1 and torch.float32 not in dtypes:
+        # one conversion kernel for every parameter gradient
+        conv = g["flat"].to(dtypes.pop())
+        g = dict(g, **{name: conv[o:o + g[name].numel()].view(shp) for name, o, shp in g["layout"]})
     flat = [g["d_latents"], g["d_w1"], g["d_w2"]]
     flat += [g["d_wq"][h * dq:(h + 1) * dq] for h in range(H)]
     flat += [g["d_bn"][0, h * dq:(h + 1) * dq] for h in range(H)]

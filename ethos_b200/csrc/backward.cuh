@@ -28,23 +28,45 @@ namespace ethos {
 // Per-token backward gather: the forward gather kernel's structure with the
 // token vector dhacc in place of xp.  Per selection it writes dw, a and ddot;
 // per token dxp (fp32) and its bf16 copy into the GEMM operand du[:, off:].
+// Warps per block and cp.async ring depth.  The per-token dhacc / xp buffers
+// are double-buffered: token k+2's copies are issued STAGES-1 batches ahead,
+// which is safe while STAGES-1 < 2 * (batches per token); the host picks the
+// 2-stage instance when R / 4 is too small for the default depth.
+// (B200, 16384 tokens x 128 selections, whole backward: 8x5 2.68 ms,
+// 10x3 2.65, 12x2 2.55)
+#ifndef ETHOS_BGATHER_WARPS
+#define ETHOS_BGATHER_WARPS 12
+#endif
+#ifndef ETHOS_BGATHER_STAGES
+#define ETHOS_BGATHER_STAGES 2
+#endif
+constexpr int BGATHER_WARPS = ETHOS_BGATHER_WARPS;
+constexpr int BGATHER_THREADS = BGATHER_WARPS * 32;
+constexpr int BGATHER_STAGES = ETHOS_BGATHER_STAGES;
 constexpr int BGATHER_STAGE_BYTES = GATHER_ROWS * 1024 + 32;  // rows + 4 weights + 4 dots
-constexpr int BGATHER_WARP_BYTES = GATHER_STAGES * BGATHER_STAGE_BYTES + 2 * 2048;
-constexpr int BGATHER_SMEM_BYTES = GATHER_WARPS * BGATHER_WARP_BYTES;
+// + per-token double buffers for dhacc and xp (fp32, 2 KB each)
+__host__ __device__ constexpr int bgather_warp_bytes(int stages) {
+  return stages * BGATHER_STAGE_BYTES + 2 * 2048 + 2 * 2048;
+}
+__host__ __device__ constexpr int bgather_smem_bytes(int stages) { return BGATHER_WARPS * bgather_warp_bytes(stages); }
+static_assert(BGATHER_STAGES >= 2, "ring needs two stages");
+static_assert(bgather_smem_bytes(BGATHER_STAGES) <= 227 * 1024, "backward gather ring exceeds shared memory");
 
-__global__ void __launch_bounds__(GATHER_THREADS, 1)
+template <int STAGES>
+__global__ void __launch_bounds__(BGATHER_THREADS, 1)
     k_expert_bwd_gather(const __half* __restrict__ table, const int32_t* __restrict__ ids,
                         const float* __restrict__ w, const float* __restrict__ dot, const float* __restrict__ dhacc,
                         float* __restrict__ dw_out, float* __restrict__ ca_out, float* __restrict__ cd_out,
-                        float* __restrict__ dxp_out, __nv_bfloat16* __restrict__ du, int64_t ldu, int du_off, int T,
-                        int R, int N, int* err) {
+                        float* __restrict__ dxp_out, __nv_bfloat16* __restrict__ du, int64_t ldu, int du_off,
+                        const float* __restrict__ xp, __nv_bfloat16* __restrict__ gx, int T, int R, int N, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
-  uint8_t* wbase = smem_raw + wib * BGATHER_WARP_BYTES;
-  uint8_t* vbuf = wbase + GATHER_STAGES * BGATHER_STAGE_BYTES;
-  const int gw = blockIdx.x * GATHER_WARPS + wib;
-  const int nw = gridDim.x * GATHER_WARPS;
+  uint8_t* wbase = smem_raw + wib * bgather_warp_bytes(STAGES);
+  uint8_t* vbuf = wbase + STAGES * BGATHER_STAGE_BYTES;
+  uint8_t* xbuf = vbuf + 2 * 2048;
+  const int gw = blockIdx.x * BGATHER_WARPS + wib;
+  const int nw = gridDim.x * BGATHER_WARPS;
   const int nbt = R / GATHER_ROWS;
   const int ntok = T > gw ? (T - 1 - gw) / nw + 1 : 0;
   const int nb = ntok * nbt;
@@ -60,7 +82,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
   auto issue = [&](int b, int4 id4) {
     const int t = gw + (b / nbt) * nw;
     const int r0 = (b % nbt) * GATHER_ROWS;
-    uint8_t* st = wbase + (b % GATHER_STAGES) * BGATHER_STAGE_BYTES;
+    uint8_t* st = wbase + (b % STAGES) * BGATHER_STAGE_BYTES;
     const int idv[4] = {id4.x, id4.y, id4.z, id4.w};
 #pragma unroll
     for (int u = 0; u < GATHER_ROWS; ++u) {
@@ -82,34 +104,41 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
       cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
       cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
       cp_async_16(xd + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
+      const char* ps = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
+      uint8_t* pd = xbuf + ((b / nbt) & 1) * 2048;
+      cp_async_16(pd + 32 * lane, ps + 32 * lane);
+      cp_async_16(pd + 32 * lane + 16, ps + 32 * lane + 16);
+      cp_async_16(pd + 1024 + 32 * lane, ps + 1024 + 32 * lane);
+      cp_async_16(pd + 1024 + 32 * lane + 16, ps + 1024 + 32 * lane + 16);
     }
   };
 
   int4 next_ids = load_ids(0);
 #pragma unroll 1
-  for (int b = 0; b < GATHER_STAGES - 1; ++b) {
+  for (int b = 0; b < STAGES - 1; ++b) {
     const int4 cur = next_ids;
     next_ids = load_ids(b + 1);
     if (b < nb) issue(b, cur);
     cp_async_commit();
   }
   float gv[16];
-  float acc[16];
+  unsigned long long gv2[8];   // dhacc columns as packed pairs
+  unsigned long long acc2[8];  // dxp columns as packed pairs
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  for (int i = 0; i < 8; ++i) acc2[i] = 0ull;
 #pragma unroll 1
   for (int b = 0; b < nb; ++b) {
     {
-      const int bi = b + GATHER_STAGES - 1;
+      const int bi = b + STAGES - 1;
       const int4 cur = next_ids;
       next_ids = load_ids(bi + 1);
       if (bi < nb) issue(bi, cur);
       cp_async_commit();
     }
-    cp_async_wait_group<GATHER_STAGES - 1>();
+    cp_async_wait_group<STAGES - 1>();
     const int t = gw + (b / nbt) * nw;
     const int r0 = (b % nbt) * GATHER_ROWS;
-    const uint8_t* st = wbase + (b % GATHER_STAGES) * BGATHER_STAGE_BYTES;
+    const uint8_t* st = wbase + (b % STAGES) * BGATHER_STAGE_BYTES;
     if (r0 == 0) {
       const float4* x4 = reinterpret_cast<const float4*>(vbuf + ((b / nbt) & 1) * 2048);
       const float4 a0 = x4[2 * lane], a1 = x4[2 * lane + 1], c0 = x4[64 + 2 * lane], c1 = x4[64 + 2 * lane + 1];
@@ -118,23 +147,39 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
       gv[8] = c0.x; gv[9] = c0.y; gv[10] = c0.z; gv[11] = c0.w;
       gv[12] = c1.x; gv[13] = c1.y; gv[14] = c1.z; gv[15] = c1.w;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+      for (int i = 0; i < 8; ++i) {
+        gv2[i] = pk2(gv[2 * i], gv[2 * i + 1]);
+        acc2[i] = 0ull;
+      }
+      // bf16 copy of this token's [dhacc | xp] row for the per-expert pass
+      const float4* p4 = reinterpret_cast<const float4*>(xbuf + ((b / nbt) & 1) * 2048);
+      const float4 e0 = p4[2 * lane], e1 = p4[2 * lane + 1], f0 = p4[64 + 2 * lane], f1 = p4[64 + 2 * lane + 1];
+      __nv_bfloat16* gr = gx + static_cast<int64_t>(t) * 1024;
+      auto pk = [](float a, float b) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&v);
+      };
+      *reinterpret_cast<uint4*>(gr + 8 * lane) = make_uint4(pk(gv[0], gv[1]), pk(gv[2], gv[3]), pk(gv[4], gv[5]),
+                                                            pk(gv[6], gv[7]));
+      *reinterpret_cast<uint4*>(gr + 256 + 8 * lane) = make_uint4(pk(gv[8], gv[9]), pk(gv[10], gv[11]),
+                                                                  pk(gv[12], gv[13]), pk(gv[14], gv[15]));
+      *reinterpret_cast<uint4*>(gr + 512 + 8 * lane) = make_uint4(pk(e0.x, e0.y), pk(e0.z, e0.w), pk(e1.x, e1.y),
+                                                                  pk(e1.z, e1.w));
+      *reinterpret_cast<uint4*>(gr + 768 + 8 * lane) = make_uint4(pk(f0.x, f0.y), pk(f0.z, f0.w), pk(f1.x, f1.y),
+                                                                  pk(f1.z, f1.w));
     }
-    uint4 hv[GATHER_ROWS][2];
+    unsigned long long hf[GATHER_ROWS][8];
     float part[GATHER_ROWS];
 #pragma unroll
     for (int u = 0; u < GATHER_ROWS; ++u) {
-      hv[u][0] = *reinterpret_cast<const uint4*>(st + u * 1024 + 16 * lane);
-      hv[u][1] = *reinterpret_cast<const uint4*>(st + u * 1024 + 512 + 16 * lane);
-      float f[8];
-      float sacc = 0.f;
-      unpack_h8(hv[u][0], f);
+      unpack_h8_x2(*reinterpret_cast<const uint4*>(st + u * 1024 + 16 * lane), hf[u]);
+      unpack_h8_x2(*reinterpret_cast<const uint4*>(st + u * 1024 + 512 + 16 * lane), hf[u] + 4);
+      unsigned long long s2 = 0ull;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sacc = fmaf(f[i], gv[i], sacc);
-      unpack_h8(hv[u][1], f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sacc = fmaf(f[i], gv[8 + i], sacc);
-      part[u] = sacc;
+      for (int i = 0; i < 8; ++i) s2 = ffma2(hf[u][i], gv2[i], s2);
+      float lo, hi;
+      upk2(s2, lo, hi);
+      part[u] = lo + hi;
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -163,15 +208,14 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
 #pragma unroll
     for (int u = 0; u < GATHER_ROWS; ++u) {
       const float c = __shfl_sync(0xffffffffu, ddot, 8 * u);
-      float f[8];
-      unpack_h8(hv[u][0], f);
+      const unsigned long long c2 = pk2(c, c);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(c, f[i], acc[i]);
-      unpack_h8(hv[u][1], f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[8 + i] = fmaf(c, f[i], acc[8 + i]);
+      for (int i = 0; i < 8; ++i) acc2[i] = ffma2(c2, hf[u][i], acc2[i]);
     }
     if (r0 + GATHER_ROWS == R) {
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) upk2(acc2[i], acc[2 * i], acc[2 * i + 1]);
       float* dst = dxp_out + static_cast<int64_t>(t) * 512;
       *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
       *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
@@ -256,16 +300,27 @@ __global__ void k_scatter_experts(const int32_t* __restrict__ ids, int64_t n, in
 }
 
 // ------------------------------------------------------------------------
+__device__ __forceinline__ void unpack_b8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __bfloat1622float2(h[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+
 // Per-expert pre-activation gradient (one warp per expert, lane l owns hidden
 // columns [8l, 8l+8) and [256+8l, 256+8l+8)):
 //   dP[e] = G[e] * sum_{s in seg(e)} (a_s dhacc[t_s] + ddot_s xp[t_s])
-// written as bf16 (operand of the dE / dW1 GEMMs).  Experts without
+// reading the bf16 token rows gx[t] = [dhacc | xp] (2 KB each, L2-resident)
+// and writing bf16 (operand of the dE / dW1 GEMMs).  Experts without
 // selections get zeros.
-__global__ void __launch_bounds__(256) k_expert_dP(const int* __restrict__ offs, const int* __restrict__ perm,
+__global__ void __launch_bounds__(256, 3) k_expert_dP(const int* __restrict__ offs, const int* __restrict__ perm,
                                                     int total, const float* __restrict__ ca,
-                                                    const float* __restrict__ cd, const float* __restrict__ dhacc,
-                                                    const float* __restrict__ xp, const __half* __restrict__ gtab,
-                                                    __nv_bfloat16* __restrict__ dP, int N, int R) {
+                                                    const float* __restrict__ cd, const __nv_bfloat16* __restrict__ gx,
+                                                    const __half* __restrict__ gtab, __nv_bfloat16* __restrict__ dP,
+                                                    int N, int R) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nw = (gridDim.x * blockDim.x) >> 5;
@@ -275,22 +330,52 @@ __global__ void __launch_bounds__(256) k_expert_dP(const int* __restrict__ offs,
     float acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-    for (int sidx = s0; sidx < s1; ++sidx) {
-      const int idx = __ldg(perm + sidx);
-      const int64_t t = idx / R;
-      const float a = __ldg(ca + idx), d = __ldg(cd + idx);
-      const float4* g4 = reinterpret_cast<const float4*>(dhacc + t * 512);
-      const float4* x4 = reinterpret_cast<const float4*>(xp + t * 512);
-      const float4 g0 = __ldg(g4 + 2 * lane), g1 = __ldg(g4 + 2 * lane + 1);
-      const float4 g2 = __ldg(g4 + 64 + 2 * lane), g3 = __ldg(g4 + 64 + 2 * lane + 1);
-      const float4 x0 = __ldg(x4 + 2 * lane), x1 = __ldg(x4 + 2 * lane + 1);
-      const float4 x2 = __ldg(x4 + 64 + 2 * lane), x3 = __ldg(x4 + 64 + 2 * lane + 1);
-      const float gg[16] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w,
-                            g2.x, g2.y, g2.z, g2.w, g3.x, g3.y, g3.z, g3.w};
-      const float xx[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                            x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+    for (int base = s0; base < s1; base += 32) {
+      // lanes fetch up to 32 entries of the segment at once
+      const int n = min(32, s1 - base);
+      int my_t = 0;
+      float my_a = 0.f, my_d = 0.f;
+      if (lane < n) {
+        const int idx = __ldg(perm + base + lane);
+        my_t = idx / R;
+        my_a = __ldg(ca + idx);
+        my_d = __ldg(cd + idx);
+      }
+      for (int u0 = 0; u0 < n; u0 += 2) {
+        uint4 rv[2][4];
+        float av[2], dv[2];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = fmaf(a, gg[i], fmaf(d, xx[i], acc[i]));
+        for (int v = 0; v < 2; ++v) {
+          const int u = u0 + v;
+          const int t = __shfl_sync(0xffffffffu, my_t, u & 31);
+          av[v] = __shfl_sync(0xffffffffu, my_a, u & 31);
+          dv[v] = __shfl_sync(0xffffffffu, my_d, u & 31);
+          if (u < n) {
+            const __nv_bfloat16* row = gx + static_cast<int64_t>(t) * 1024;
+            rv[v][0] = __ldg(reinterpret_cast<const uint4*>(row + 8 * lane));
+            rv[v][1] = __ldg(reinterpret_cast<const uint4*>(row + 256 + 8 * lane));
+            rv[v][2] = __ldg(reinterpret_cast<const uint4*>(row + 512 + 8 * lane));
+            rv[v][3] = __ldg(reinterpret_cast<const uint4*>(row + 768 + 8 * lane));
+          } else {
+            av[v] = 0.f;
+            dv[v] = 0.f;
+            rv[v][0] = rv[v][1] = rv[v][2] = rv[v][3] = make_uint4(0, 0, 0, 0);
+          }
+        }
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+          float g0[8], g1[8], x0[8], x1[8];
+          unpack_b8(rv[v][0], g0);
+          unpack_b8(rv[v][1], g1);
+          unpack_b8(rv[v][2], x0);
+          unpack_b8(rv[v][3], x1);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            acc[i] = fmaf(av[v], g0[i], fmaf(dv[v], x0[i], acc[i]));
+            acc[8 + i] = fmaf(av[v], g1[i], fmaf(dv[v], x1[i], acc[8 + i]));
+          }
+        }
+      }
     }
     const __half* gr = gtab + static_cast<int64_t>(e) * 512;
     float gf[16];
@@ -320,7 +405,7 @@ __global__ void __launch_bounds__(256) k_expert_dP(const int* __restrict__ offs,
 // columns [8l, 8l+8) of each half (dq/2 = 256):
 //   dg_r  = w_r (dw_r - sum_r' w_r' dw_r')                    (softmax)
 //   dq^[t, h, :dq/2] = sum_r dg_r K1[i_r],  dq^[t, h, dq/2:] = sum_r dg_r K2[j_r]
-//   dS_p[h][t][i] = sum_{r: key_p(r) = i} dg_r               (dense, bf16)
+//   dS[p][h][t][i] = sum_{r: key_p(r) = i} dg_r              (dense, bf16)
 // with i_r = id_r / K, j_r = id_r % K.  dS feeds the dK GEMMs; its buffer is
 // zeroed beforehand and every (h, p, t, i) is written by one lane (duplicate
 // keys of a row are combined with __match_any_sync first).
@@ -360,7 +445,7 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
         tot += ku == key ? gu : 0.f;
       }
       if (act && (__ffs(same) - 1) == lane)
-        dS[((static_cast<int64_t>(h) * 2 + p) * T + t) * K + key] = __float2bfloat16_rn(tot);
+        dS[((static_cast<int64_t>(p) * H + h) * T + t) * K + key] = __float2bfloat16_rn(tot);
     }
     // dq^ = sum_r dg_r * key rows
     float acc0[8], acc1[8];
@@ -429,7 +514,8 @@ __global__ void k_bn_bwd_partial(const float* __restrict__ dqh, const float* __r
 }
 
 __global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int C, int T, int training,
-                                  const float* __restrict__ gamma, const float* __restrict__ invstd,
+                                  const float* __restrict__ gamma, const float* __restrict__ mean,
+                                  const float* __restrict__ invstd,
                                   float* __restrict__ dgamma, float* __restrict__ dbeta, float* __restrict__ dbias,
                                   float* __restrict__ coef) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
@@ -442,31 +528,41 @@ __global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int
   dgamma[col] = static_cast<float>(sx);
   dbeta[col] = static_cast<float>(s);
   const float gi = gamma[col] * invstd[col];
-  if (training) {
-    dbias[col] = 0.f;
-    coef[3 * col + 0] = gi;
-    coef[3 * col + 1] = static_cast<float>(s / T);
-    coef[3 * col + 2] = static_cast<float>(sx / T);
-  } else {
-    dbias[col] = static_cast<float>(gi * s);
-    coef[3 * col + 0] = gi;
-    coef[3 * col + 1] = 0.f;
-    coef[3 * col + 2] = 0.f;
-  }
+  // dq = gi * (dq^ - m1 - x^ * m2) with x^ = (qpre - mean) * invstd, folded
+  // into dq = A dq^ + B qpre + C
+  const float m1 = training ? static_cast<float>(s / T) : 0.f;
+  const float m2 = training ? static_cast<float>(sx / T) : 0.f;
+  dbias[col] = training ? 0.f : static_cast<float>(gi * s);
+  const float B = -gi * m2 * invstd[col];
+  reinterpret_cast<float4*>(coef)[col] = make_float4(gi, B, -gi * m1 - B * mean[col], 0.f);
 }
 
+// One thread per 8 consecutive columns of a token (C % 8 == 0);
+// coef[c] = (A, B, C, 0) from k_bn_bwd_finalize.
 __global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __restrict__ qpre,
-                               const float* __restrict__ mean, const float* __restrict__ invstd,
-                               const float* __restrict__ coef, int T, int C, __nv_bfloat16* __restrict__ du,
+                               const float4* __restrict__ coef, int T, int C, __nv_bfloat16* __restrict__ du,
                                int64_t ldu) {
-  const int64_t n = static_cast<int64_t>(T) * C;
+  const int groups = C / 8;
+  const int64_t n = static_cast<int64_t>(T) * groups;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int t = static_cast<int>(i / C);
-    const int c = static_cast<int>(i - static_cast<int64_t>(t) * C);
-    const float xh = (qpre[i] - mean[c]) * invstd[c];
-    const float g = coef[3 * c] * (dqh[i] - coef[3 * c + 1] - xh * coef[3 * c + 2]);
-    du[static_cast<int64_t>(t) * ldu + c] = __float2bfloat16_rn(g);
+    const int t = static_cast<int>(i / groups);
+    const int c0 = static_cast<int>(i - static_cast<int64_t>(t) * groups) * 8;
+    const int64_t o = static_cast<int64_t>(t) * C + c0;
+    const float4 g0 = *reinterpret_cast<const float4*>(dqh + o), g1 = *reinterpret_cast<const float4*>(dqh + o + 4);
+    const float4 q0 = *reinterpret_cast<const float4*>(qpre + o), q1 = *reinterpret_cast<const float4*>(qpre + o + 4);
+    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int u = 0; u < 8; u += 2) {
+      const float4 ka = __ldg(coef + c0 + u), kb = __ldg(coef + c0 + u + 1);
+      const float r0 = fmaf(ka.x, gv[u], fmaf(ka.y, qv[u], ka.z));
+      const float r1 = fmaf(kb.x, gv[u + 1], fmaf(kb.y, qv[u + 1], kb.z));
+      const __nv_bfloat162 b = __floats2bfloat162_rn(r0, r1);
+      out[u >> 1] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(du + static_cast<int64_t>(t) * ldu + c0) = make_uint4(out[0], out[1], out[2], out[3]);
   }
 }
 

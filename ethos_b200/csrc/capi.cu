@@ -353,7 +353,7 @@ int run_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g,
 // Router part shared by ethos_layer_forward and ethos_router_forward:
 // projection GEMM (queries, plus x_proj when with_xp), BatchNorm, scoring and
 // top-k.
-// `qs` is the split-bf16 scoring operand [H][2][T][dq] (scratch, or the
+// `qs` is the split-bf16 scoring operand [2][H][T][dq] (scratch, or the
 // caller's save buffer).  With keep_qpre the projection always writes the
 // pre-BatchNorm queries (fp32) and normalises them in a second pass, so the
 // backward pass has them in both BatchNorm modes.
@@ -414,8 +414,8 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   g.H = static_cast<int>(d.num_heads);
   g.K = static_cast<int>(d.num_sub_keys);
   g.KA = dq;
-  g.a_stride_h = 2 * T;
-  g.a_stride_p = T;
+  g.a_stride_h = T;
+  g.a_stride_p = static_cast<int>(d.num_heads) * T;
   g.a_col_p = 0;
   st = run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, err, stream, dev);
   mark(ev, ETHOS_STAGE_TOPK, stream);
@@ -441,6 +441,7 @@ struct BwdScratch {
   __nv_bfloat16* dP;
   float* dqhat;
   __nv_bfloat16* dS;
+  __nv_bfloat16* gx;
   float* part;
   float* coef;
   float* stats;
@@ -467,9 +468,10 @@ void carve_backward(Carve& c, const ethos_dims& d, BwdScratch* s) {
   s->dP = c.take<__nv_bfloat16>(static_cast<size_t>(N * EX_DH));
   s->dqhat = c.take<float>(static_cast<size_t>(T * HQ));
   s->dS = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.num_sub_keys));
+  s->gx = c.take<__nv_bfloat16>(static_cast<size_t>(T * 2 * EX_DH));
   s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
   s->part = c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2);
-  s->coef = c.take<float>(static_cast<size_t>(3 * HQ));
+  s->coef = c.take<float>(static_cast<size_t>(4 * HQ));
   s->stats = c.take<float>(static_cast<size_t>(2 * HQ));
   s->dy16 = c.take<__nv_bfloat16>(static_cast<size_t>(T * d.d_model));
 }
@@ -864,12 +866,22 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
   }
   // (4) per token: dw, a, ddot per selection; dxp (fp32 + bf16 into du)
   {
-    if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather), BGATHER_SMEM_BYTES)) != ETHOS_OK)
-      return st;
-    int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
+    int blocks = (T + BGATHER_WARPS - 1) / BGATHER_WARPS;
     if (blocks > dev->sm_count) blocks = dev->sm_count;
-    k_expert_bwd_gather<<<blocks, GATHER_THREADS, BGATHER_SMEM_BYTES, sm>>>(
-        s.htab, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du, LDU, HQ, T, R, N, dev_err);
+    if (BGATHER_STAGES - 1 < 2 * (R / GATHER_ROWS)) {
+      constexpr int bytes = bgather_smem_bytes(BGATHER_STAGES);
+      if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather<BGATHER_STAGES>), bytes)) != ETHOS_OK)
+        return st;
+      k_expert_bwd_gather<BGATHER_STAGES><<<blocks, BGATHER_THREADS, bytes, sm>>>(
+          s.htab, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N,
+          dev_err);
+    } else {
+      constexpr int bytes = bgather_smem_bytes(2);
+      if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather<2>), bytes)) != ETHOS_OK) return st;
+      k_expert_bwd_gather<2><<<blocks, BGATHER_THREADS, bytes, sm>>>(s.htab, ids, weights, save_dot, s.dhacc, s.dw,
+                                                                     s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx,
+                                                                     T, R, N, dev_err);
+    }
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   // (5) selections grouped by expert (counting sort)
@@ -885,7 +897,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
-  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.dhacc, save_xp, s.gtab, s.dP, N, R);
+  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.gx, s.gtab, s.dP, N, R);
   if ((st = launch_status()) != ETHOS_OK) return st;
   // (7) dE = dP W1       (W1 read in place, MN-major)
   {
@@ -920,20 +932,20 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                                         s.dqhat, s.dS, sm, *dev); break;
   }
   if (st != ETHOS_OK) return st;
-  // (10) dK_p += dS_{h,p}^T q^_{h,p}  (per head and half; q^ = hi part of qs)
-  for (int h = 0; h < H; ++h) {
-    for (int p = 0; p < 2; ++p) {
-      EpiAtomicF32 e;
-      e.out = d_keys + static_cast<int64_t>(p) * K * half;
-      e.ldo = half;
-      e.M = K;
-      e.scale = 1.0f;
-      const __nv_bfloat16* dSp = s.dS + (static_cast<int64_t>(h) * 2 + p) * T * K;
-      const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(save_qs) + (static_cast<int64_t>(h) * 2 + p) * T * dq;
-      if ((st = gemm(GemmOperand{dSp, K, true}, GemmOperand{qh, dq, true}, K, half, T, auto_ksplit(K, half, T, *dev),
-                     e, dev_err, sm, *dev)) != ETHOS_OK)
-        return st;
-    }
+  // (10) dK_p = dS_p^T q^_p over all heads and tokens (q^ = hi part of qs;
+  //      both [2][H][T][.] so the (h, t) rows of a half are contiguous)
+  for (int p = 0; p < 2; ++p) {
+    EpiAtomicF32 e;
+    e.out = d_keys + static_cast<int64_t>(p) * K * half;
+    e.ldo = half;
+    e.M = K;
+    e.scale = 1.0f;
+    const __nv_bfloat16* dSp = s.dS + static_cast<int64_t>(p) * H * T * K;
+    const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(save_qs) + static_cast<int64_t>(p) * H * T * dq;
+    const int KK = H * T;
+    if ((st = gemm(GemmOperand{dSp, K, true}, GemmOperand{qh, dq, true}, K, half, KK, auto_ksplit(K, half, KK, *dev),
+                   e, dev_err, sm, *dev)) != ETHOS_OK)
+      return st;
   }
   // (11) BatchNorm backward -> dq (bf16 into du[:, :HQ]), dbias, dgamma, dbeta
   {
@@ -946,9 +958,10 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
     }
     dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
     k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, T, HQ, s.part);
-    k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, invstd,
-                                                        d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
-    k_bn_bwd_apply<<<eblocks, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, s.coef, T, HQ, s.du, LDU);
+    k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, mean,
+                                                        invstd, d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
+    k_bn_bwd_apply<<<eblocks, cb, 0, sm>>>(s.dqhat, save_qpre, reinterpret_cast<const float4*>(s.coef), T, HQ,
+                                           s.du, LDU);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   // (12) dx = du @ W_cat          (W_cat read in place, MN-major)

@@ -21,18 +21,59 @@
 
 namespace ethos {
 
-constexpr int GATHER_WARPS = 8;
+// 16 warps x 2 stages: the kernel is bound by load latency per warp, so
+// resident warps matter more than ring depth (measured on B200 at 16384
+// tokens x 128 selections: 8x5 0.47 ms, 12x3 0.40, 14x3 0.36, 16x2 0.31;
+// 18 and more warps spill registers).
+#ifndef ETHOS_GATHER_WARPS
+#define ETHOS_GATHER_WARPS 16
+#endif
+#ifndef ETHOS_GATHER_STAGES
+#define ETHOS_GATHER_STAGES 2
+#endif
+constexpr int GATHER_WARPS = ETHOS_GATHER_WARPS;
 constexpr int GATHER_THREADS = GATHER_WARPS * 32;
-constexpr int GATHER_ROWS = 4;     // table rows per batch
-constexpr int GATHER_STAGES = 5;   // cp.async ring depth per warp (4 batches in flight)
+constexpr int GATHER_ROWS = 4;                     // table rows per batch
+constexpr int GATHER_STAGES = ETHOS_GATHER_STAGES; // cp.async ring depth per warp
 constexpr int GATHER_STAGE_BYTES = GATHER_ROWS * 1024 + 16;          // rows + 4 routing weights
-constexpr int GATHER_WARP_BYTES = GATHER_STAGES * GATHER_STAGE_BYTES + 2 * 2048;  // + 2 x_proj buffers
+// + one x_proj buffer: a token's x_proj moves to registers at its first batch,
+// and the next token's copy is issued at least one batch later (R/4 > STAGES-1)
+// (the table path runs with R >= 16 selections per token, i.e. 4 batches)
+constexpr int GATHER_WARP_BYTES = GATHER_STAGES * GATHER_STAGE_BYTES + 2048;
 constexpr int GATHER_SMEM_BYTES = GATHER_WARPS * GATHER_WARP_BYTES;
+static_assert(GATHER_STAGES >= 2 && GATHER_STAGES <= 4, "single x_proj buffer needs STAGES-1 < 4 batches");
+static_assert(GATHER_SMEM_BYTES <= 227 * 1024, "gather ring exceeds shared memory");
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one 64-bit register pair
+// holds two floats, fma.rn.f32x2 does two FMAs per instruction.
+__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b,
+                                                    unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// 8 fp16 (one uint4) -> 4 packed fp32 pairs
+__device__ __forceinline__ void unpack_h8_x2(const uint4& u, unsigned long long* p) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __half22float2(h[i]);
+    p[i] = pk2(v.x, v.y);
+  }
 }
 
 __device__ __forceinline__ void unpack_h8(const uint4& u, float (&f)[8]) {
@@ -50,8 +91,8 @@ __device__ __forceinline__ void unpack_h8(const uint4& u, float (&f)[8]) {
 // flight while one is reduced.  Lane l copies and later reads only its own
 // slices of each row, hidden columns [8l, 8l + 8) and [256 + 8l, 256 + 8l + 8)
 // (bytes [16l, 16l + 16) and [512 + 16l, ...)), so a cp.async.wait_group
-// alone orders copy and use.  Needs R >= 16 (a token spans >= 4 batches, so
-// the two x_proj buffers are never overwritten while in use).
+// alone orders copy and use.  Needs R / 4 > STAGES - 1 (so a token's x_proj
+// buffer is read into registers before the next token's copy is issued).
 __global__ void __launch_bounds__(GATHER_THREADS, 1)
     k_expert_gather(const __half* __restrict__ table, const int32_t* __restrict__ ids, const float* __restrict__ w,
                     const float* __restrict__ xp, __nv_bfloat16* __restrict__ hacc_out,
@@ -95,7 +136,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
     if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
     if (r0 == 0) {  // first batch of a token also brings this lane's x_proj slices
       const char* xs = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
-      uint8_t* xd = xpbuf + ((b / nbt) & 1) * 2048;
+      uint8_t* xd = xpbuf;
       cp_async_16(xd + 32 * lane, xs + 32 * lane);
       cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
       cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
@@ -111,10 +152,10 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
     if (b < nb) issue(b, cur);
     cp_async_commit();
   }
-  float xv[16];
-  float acc[16];
+  unsigned long long xv2[8];   // this lane's x_proj columns as packed pairs
+  unsigned long long acc2[8];  // hacc columns as packed pairs
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  for (int i = 0; i < 8; ++i) acc2[i] = 0ull;
 #pragma unroll 1
   for (int b = 0; b < nb; ++b) {
     {
@@ -129,31 +170,27 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
     const int r0 = (b % nbt) * GATHER_ROWS;
     const uint8_t* st = wbase + (b % GATHER_STAGES) * GATHER_STAGE_BYTES;
     if (r0 == 0) {
-      const float4* x4 = reinterpret_cast<const float4*>(xpbuf + ((b / nbt) & 1) * 2048);
+      const float4* x4 = reinterpret_cast<const float4*>(xpbuf);
       // this lane's x_proj columns [8l, 8l+8) and [256+8l, 256+8l+8)
       const float4 a0 = x4[2 * lane], a1 = x4[2 * lane + 1], c0 = x4[64 + 2 * lane], c1 = x4[64 + 2 * lane + 1];
-      xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
-      xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
-      xv[8] = c0.x; xv[9] = c0.y; xv[10] = c0.z; xv[11] = c0.w;
-      xv[12] = c1.x; xv[13] = c1.y; xv[14] = c1.z; xv[15] = c1.w;
+      xv2[0] = pk2(a0.x, a0.y); xv2[1] = pk2(a0.z, a0.w); xv2[2] = pk2(a1.x, a1.y); xv2[3] = pk2(a1.z, a1.w);
+      xv2[4] = pk2(c0.x, c0.y); xv2[5] = pk2(c0.z, c0.w); xv2[6] = pk2(c1.x, c1.y); xv2[7] = pk2(c1.z, c1.w);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+      for (int i = 0; i < 8; ++i) acc2[i] = 0ull;
     }
-    uint4 hv[GATHER_ROWS][2];
+    // rows are unpacked to fp32 pairs once and kept for the weighted sum
+    unsigned long long hf[GATHER_ROWS][8];
     float part[GATHER_ROWS];
 #pragma unroll
     for (int u = 0; u < GATHER_ROWS; ++u) {
-      hv[u][0] = *reinterpret_cast<const uint4*>(st + u * 1024 + 16 * lane);
-      hv[u][1] = *reinterpret_cast<const uint4*>(st + u * 1024 + 512 + 16 * lane);
-      float f[8];
-      float sacc = 0.f;
-      unpack_h8(hv[u][0], f);
+      unpack_h8_x2(*reinterpret_cast<const uint4*>(st + u * 1024 + 16 * lane), hf[u]);
+      unpack_h8_x2(*reinterpret_cast<const uint4*>(st + u * 1024 + 512 + 16 * lane), hf[u] + 4);
+      unsigned long long s2 = 0ull;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sacc = fmaf(f[i], xv[i], sacc);
-      unpack_h8(hv[u][1], f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sacc = fmaf(f[i], xv[8 + i], sacc);
-      part[u] = sacc;
+      for (int i = 0; i < 8; ++i) s2 = ffma2(hf[u][i], xv2[i], s2);
+      float lo, hi;
+      upk2(s2, lo, hi);
+      part[u] = lo + hi;
     }
     // transpose-reduce 4 partial dots over 32 lanes (6 shuffles): lanes
     // 8g..8g+7 end up with the full dot of row r0 + g
@@ -177,19 +214,17 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
 #pragma unroll
     for (int u = 0; u < GATHER_ROWS; ++u) {
       const float a = __shfl_sync(0xffffffffu, a_mine, 8 * u);
-      float f[8];
-      unpack_h8(hv[u][0], f);
+      const unsigned long long a2 = pk2(a, a);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(a, f[i], acc[i]);
-      unpack_h8(hv[u][1], f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[8 + i] = fmaf(a, f[i], acc[8 + i]);
+      for (int i = 0; i < 8; ++i) acc2[i] = ffma2(a2, hf[u][i], acc2[i]);
     }
     if (r0 + GATHER_ROWS == R) {
       uint32_t o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const __nv_bfloat162 bb = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        float lo, hi;
+        upk2(acc2[i], lo, hi);
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
         o[i] = *reinterpret_cast<const uint32_t*>(&bb);
       }
       __nv_bfloat16* dst = hacc_out + static_cast<int64_t>(t) * 512;

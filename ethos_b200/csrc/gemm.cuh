@@ -135,7 +135,7 @@ struct EpiAtomicF32 : EpiNoColParams {
 //  mode 0 (BatchNorm eval): q_hat = v * scale + offset, with the bias and the
 //    running statistics folded into (scale, offset) per column, is written as
 //    a bf16 hi/lo pair into the scoring operand
-//    qs[(h*2 + half)][row][0..dq/2) = hi, [dq/2..dq) = lo.
+//    qs[half][h][row][0..dq/2) = hi, [dq/2..dq) = lo.
 //  mode 1 (BatchNorm train): qpre[row][col] = v + bias (fp32) for the batch
 //    statistics pass.
 // x_proj is always written fp32 to xp[row][0..dh).
@@ -181,7 +181,7 @@ struct EpiProj {
     const int half = dq >> 1;
     const int p = e >= half ? 1 : 0;
     const int i0 = e - p * half;
-    __nv_bfloat16* base = qs + (static_cast<int64_t>(h * 2 + p) * M + row) * dq;
+    __nv_bfloat16* base = qs + (static_cast<int64_t>(p * (HQ / dq) + h) * M + row) * dq;
     const float4* cp4 = reinterpret_cast<const float4*>(cpc);
     uint32_t hi[16], lo[16];
 #pragma unroll

@@ -535,8 +535,8 @@ __global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, i
   colp[col] = make_float2(scale, beta - (rm - bias) * scale);
 }
 
-// Normalisation pass of training mode: qpre [T, C] -> split-bf16 scoring
-// operand qs[(h*2 + p)][t][hi | lo].  One thread per 8 consecutive columns.
+// Normalisation pass on qpre [T, C] -> split-bf16 scoring operand
+// qs[p][h][t][hi | lo].  One thread per 8 consecutive columns.
 __global__ void k_bn_apply(const float* __restrict__ qpre, const float2* __restrict__ colp, int T, int H, int dq,
                            __nv_bfloat16* __restrict__ qs) {
   const int C = H * dq;
@@ -568,7 +568,7 @@ __global__ void k_bn_apply(const float* __restrict__ qpre, const float2* __restr
     hi[i >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
     lo[i >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
   }
-  __nv_bfloat16* base = qs + (static_cast<int64_t>(h * 2 + p) * T + t) * dq;
+  __nv_bfloat16* base = qs + (static_cast<int64_t>(p * H + h) * T + t) * dq;
   *reinterpret_cast<uint4*>(base + i0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
   *reinterpret_cast<uint4*>(base + half + i0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }

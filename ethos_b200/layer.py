@@ -68,14 +68,10 @@ class ProductKeyRouter(nn.Module):
     # -- parameter packing ------------------------------------------------
     def _bn_block(self):
         """fp32 [5, H*dq]: bias, gamma, beta, running mean, running var."""
-        rows = [
-            torch.cat([m.bias for m in self.query_projs]),
-            torch.cat([n.weight for n in self.query_norms]),
-            torch.cat([n.bias for n in self.query_norms]),
-            torch.cat([n.running_mean for n in self.query_norms]),
-            torch.cat([n.running_var for n in self.query_norms]),
-        ]
-        return torch.stack([r.detach().to(torch.float32) for r in rows]).contiguous()
+        parts = ([m.bias for m in self.query_projs] + [n.weight for n in self.query_norms]
+                 + [n.bias for n in self.query_norms] + [n.running_mean for n in self.query_norms]
+                 + [n.running_var for n in self.query_norms])
+        return torch.cat([t.detach() for t in parts]).to(torch.float32).view(5, -1).contiguous()
 
     def _bn_eps_momentum(self):
         n0 = self.query_norms[0]
@@ -95,11 +91,12 @@ class ProductKeyRouter(nn.Module):
         """Copy the kernel-updated running statistics back into the buffers
         and count the batch, as BatchNorm1d.forward does in training mode."""
         dq = self.d_query
+        H = self.num_heads
         with torch.no_grad():
-            for h, n in enumerate(self.query_norms):
-                n.running_mean.copy_(bn[3, h * dq:(h + 1) * dq])
-                n.running_var.copy_(bn[4, h * dq:(h + 1) * dq])
-                n.num_batches_tracked.add_(1)
+            dst = [n.running_mean for n in self.query_norms] + [n.running_var for n in self.query_norms]
+            src = [bn[3, h * dq:(h + 1) * dq] for h in range(H)] + [bn[4, h * dq:(h + 1) * dq] for h in range(H)]
+            torch._foreach_copy_(dst, src)
+            torch._foreach_add_([n.num_batches_tracked for n in self.query_norms], 1)
 
     def forward(self, x_flat):
         ops._require_cuda(x_flat, "x_flat")

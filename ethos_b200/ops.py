@@ -223,7 +223,7 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
         out["hacc"] = torch.empty((T, dh), dtype=torch.bfloat16, device=dev)
         out["dot"] = torch.empty((T, H * k), dtype=torch.float32, device=dev)
         out["qpre"] = torch.empty((T, HQ), dtype=torch.float32, device=dev)
-        out["qs"] = torch.empty((H, 2, T, d["d_query"]), dtype=torch.bfloat16, device=dev)
+        out["qs"] = torch.empty((2, H, T, d["d_query"]), dtype=torch.bfloat16, device=dev)
         if bn_training:
             out["bn_stats"] = torch.empty((2, HQ), dtype=torch.float32, device=dev)
     g = out.get
@@ -237,6 +237,13 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
                                 _stream(dev)),
           "ethos_layer_forward")
     return out
+
+
+def _numel(shape):
+    n = 1
+    for s in shape:
+        n *= s
+    return n
 
 
 def layer_backward(dy, x16, pw, saved, bn_training, eps):
@@ -255,16 +262,23 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps):
         check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     HQ = d["num_heads"] * d["d_query"]
-    f32 = dict(dtype=torch.float32, device=dev)
-    g = dict(
-        dx=torch.empty((T, d["d_model"]), **f32),
-        d_latents=torch.empty((d["num_experts"], d["d_latent"]), **f32),
-        d_w1=torch.empty((d["d_hidden"], d["d_latent"]), **f32),
-        d_w2=torch.empty((2 * d["d_model"], d["d_hidden"]), **f32),
-        d_wq=torch.empty((HQ, d["d_model"]), **f32),
-        d_bn=torch.empty((3, HQ), **f32),
-        d_keys=torch.empty((2, d["num_sub_keys"], d["d_query"] // 2), **f32),
-    )
+    # all parameter gradients live in one flat fp32 buffer (256-B aligned
+    # slices), so that a caller can convert them with a single kernel
+    shapes = [("d_latents", (d["num_experts"], d["d_latent"])), ("d_w1", (d["d_hidden"], d["d_latent"])),
+              ("d_w2", (2 * d["d_model"], d["d_hidden"])), ("d_wq", (HQ, d["d_model"])), ("d_bn", (3, HQ)),
+              ("d_keys", (2, d["num_sub_keys"], d["d_query"] // 2))]
+    layout, off = [], 0
+    for name, shp in shapes:
+        n = 1
+        for s_ in shp:
+            n *= s_
+        layout.append((name, off, shp))
+        off += (n + 63) // 64 * 64
+    flat = torch.empty(off, dtype=torch.float32, device=dev)
+    g = {name: flat[o:o + _numel(shp)].view(shp) for name, o, shp in layout}
+    g["dx"] = torch.empty((T, d["d_model"]), dtype=torch.float32, device=dev)
+    g["flat"] = flat
+    g["layout"] = layout
     dy = dy.contiguous()
     if dy.dtype not in (torch.bfloat16, torch.float32):
         dy = dy.float()

@@ -134,7 +134,8 @@ size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path);
  *            (sum_{h,k} a*h), save_dot fp32 [T, H*k] (h . x_proj),
  *            save_qpre fp32 [T, H*dq] (pre-BatchNorm queries, x Wq^T + b),
  *            save_bn fp32 [2, H*dq] (batch mean, 1/sqrt(var+eps); training only),
- *            save_qs bf16 [H, 2, T, dq] (normalised queries, split hi | lo)
+ *            save_qs bf16 [2, H, T, dq] (normalised queries per half and head,
+ *            split hi | lo)
  */
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
