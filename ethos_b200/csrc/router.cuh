@@ -89,22 +89,206 @@ __device__ __forceinline__ float nth_largest_of_union(float (&a)[N], float (&b)[
   return t;
 }
 
+// Sorting networks over (score, id) pairs in registers: fixed, branch-free
+// compare-exchange sequences with eight or more independent exchanges per
+// stage.  ce_desc leaves the larger score at (a, ia); equal scores keep their
+// places.
+__device__ __forceinline__ void ce_desc(float& a, int& ia, float& b, int& ib) {
+  const bool sw = b > a;
+  const float va = sw ? b : a, vb = sw ? a : b;
+  const int ja = sw ? ib : ia, jb = sw ? ia : ib;
+  a = va;
+  b = vb;
+  ia = ja;
+  ib = jb;
+}
+// bitonic sequence -> sorted descending
+template <int N>
+__device__ __forceinline__ void bitonic_merge_desc_kv(float (&v)[N], int (&ix)[N]) {
+#pragma unroll
+  for (int j = N >> 1; j > 0; j >>= 1) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      if ((i & j) == 0) ce_desc(v[i], ix[i], v[i | j], ix[i | j]);
+    }
+  }
+}
+template <int N>
+__device__ __forceinline__ void bitonic_sort_desc_kv(float (&v)[N], int (&ix)[N]) {
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          if ((i & k) == 0)
+            ce_desc(v[i], ix[i], v[l], ix[l]);
+          else
+            ce_desc(v[l], ix[l], v[i], ix[i]);
+        }
+      }
+    }
+  }
+}
+// (a, ia) <- the N largest of a and b (both sorted descending), sorted:
+// max(a[i], b[N-1-i]) is bitonic and holds the top N of the union.
+template <int N>
+__device__ __forceinline__ void top_merge_kv(float (&a)[N], int (&ia)[N], const float (&b)[N], const int (&ib)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const bool tb = b[N - 1 - i] > a[i];
+    a[i] = tb ? b[N - 1 - i] : a[i];
+    ia[i] = tb ? ib[N - 1 - i] : ia[i];
+  }
+  bitonic_merge_desc_kv<N>(a, ia);
+}
+// out <- a ++ b sorted descending (a, b sorted descending)
+template <int N>
+__device__ __forceinline__ void merge_sorted_kv(const float (&a)[N], const int (&ia)[N], const float (&b)[N],
+                                                const int (&ib)[N], float (&out)[2 * N], int (&oi)[2 * N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    out[i] = a[i];
+    oi[i] = ia[i];
+    out[N + i] = b[N - 1 - i];
+    oi[N + i] = ib[N - 1 - i];
+  }
+  bitonic_merge_desc_kv<2 * N>(out, oi);
+}
+// Row i of the candidate grid: a[i] + b[j] for j < n (padded with -inf to P).
+template <int P, int TOPK>
+__device__ __forceinline__ void grid_row(const float (&a)[TOPK], const int (&ia)[TOPK], const float (&b)[TOPK],
+                                         const int (&ib)[TOPK], int i, int n, int K, float (&v)[P], int (&ix)[P]) {
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    v[j] = j < n ? a[i] + b[j] : -INFINITY;
+    ix[j] = j < n ? ia[i] * K + ib[j] : 0;
+  }
+}
+// Top TOPK of the grid a[i] + b[j] (a, b sorted descending), sorted.  Only
+// pairs with (i+1)(j+1) <= TOPK can rank in the top TOPK (every (i', j') with
+// i' <= i, j' <= j scores at least as high), so row i has TOPK/(i+1) entries;
+// the rows are sorted and are merged by networks.
+template <int TOPK>
+__device__ __forceinline__ void grid_topk(const float (&a)[TOPK], const int (&ia)[TOPK], const float (&b)[TOPK],
+                                          const int (&ib)[TOPK], int K, float (&f)[TOPK], int (&fi)[TOPK]) {
+  grid_row<TOPK, TOPK>(a, ia, b, ib, 0, TOPK, K, f, fi);
+  if constexpr (TOPK == 16) {
+    // rows 1 (8 entries) + the singles a[8..15] + b[0]
+    {
+      float r1[8], z[8], w[16];
+      int j1[8], jz[8], jw[16];
+      grid_row<8, 16>(a, ia, b, ib, 1, 8, K, r1, j1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        z[i] = a[8 + i] + b[0];
+        jz[i] = ia[8 + i] * K + ib[0];
+      }
+      merge_sorted_kv<8>(r1, j1, z, jz, w, jw);
+      top_merge_kv<16>(f, fi, w, jw);
+    }
+    // rows 2 (5) and 3 (4)
+    {
+      float r2[8], r3[8], x[16];
+      int j2[8], j3[8], jx[16];
+      grid_row<8, 16>(a, ia, b, ib, 2, 5, K, r2, j2);
+      grid_row<8, 16>(a, ia, b, ib, 3, 4, K, r3, j3);
+      merge_sorted_kv<8>(r2, j2, r3, j3, x, jx);
+      top_merge_kv<16>(f, fi, x, jx);
+    }
+    // rows 4..7 (3, 2, 2, 2)
+    {
+      float r4[4], r5[4], r6[4], r7[4], y1[8], y2[8], y[16];
+      int j4[4], j5[4], j6[4], j7[4], k1[8], k2[8], jy[16];
+      grid_row<4, 16>(a, ia, b, ib, 4, 3, K, r4, j4);
+      grid_row<4, 16>(a, ia, b, ib, 5, 2, K, r5, j5);
+      grid_row<4, 16>(a, ia, b, ib, 6, 2, K, r6, j6);
+      grid_row<4, 16>(a, ia, b, ib, 7, 2, K, r7, j7);
+      merge_sorted_kv<4>(r4, j4, r5, j5, y1, k1);
+      merge_sorted_kv<4>(r6, j6, r7, j7, y2, k2);
+      merge_sorted_kv<8>(y1, k1, y2, k2, y, jy);
+      top_merge_kv<16>(f, fi, y, jy);
+    }
+  } else {
+#pragma unroll
+    for (int i = 1; i < TOPK; ++i) {
+      float r[TOPK];
+      int jr[TOPK];
+      grid_row<TOPK, TOPK>(a, ia, b, ib, i, TOPK / (i + 1), K, r, jr);
+      top_merge_kv<TOPK>(f, fi, r, jr);
+    }
+  }
+}
+
+// The TOPK = 16 grid merge tree in two independent parts: rows 0 and 1 with
+// the singles a[8..15] + b[0], and rows 2..7; the top 16 of the two results
+// is the grid's top 16 (the same rows as grid_topk<16>).
+template <int TOPK>
+__device__ __forceinline__ void grid_rows01(const float (&a)[TOPK], const int (&ia)[TOPK], const float (&b)[TOPK],
+                                            const int (&ib)[TOPK], int K, float (&f)[TOPK], int (&fi)[TOPK]) {
+  static_assert(TOPK == 16, "split tree is for top 16");
+  grid_row<16, 16>(a, ia, b, ib, 0, 16, K, f, fi);
+  float r1[8], z[8], w[16];
+  int j1[8], jz[8], jw[16];
+  grid_row<8, 16>(a, ia, b, ib, 1, 8, K, r1, j1);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    z[i] = a[8 + i] + b[0];
+    jz[i] = ia[8 + i] * K + ib[0];
+  }
+  merge_sorted_kv<8>(r1, j1, z, jz, w, jw);
+  top_merge_kv<16>(f, fi, w, jw);
+}
+template <int TOPK>
+__device__ __forceinline__ void grid_rows27(const float (&a)[TOPK], const int (&ia)[TOPK], const float (&b)[TOPK],
+                                            const int (&ib)[TOPK], int K, float (&f)[TOPK], int (&fi)[TOPK]) {
+  static_assert(TOPK == 16, "split tree is for top 16");
+  float r2[8], r3[8];
+  int j2[8], j3[8];
+  grid_row<8, 16>(a, ia, b, ib, 2, 5, K, r2, j2);
+  grid_row<8, 16>(a, ia, b, ib, 3, 4, K, r3, j3);
+  merge_sorted_kv<8>(r2, j2, r3, j3, f, fi);
+  float r4[4], r5[4], r6[4], r7[4], y1[8], y2[8], y[16];
+  int j4[4], j5[4], j6[4], j7[4], k1[8], k2[8], jy[16];
+  grid_row<4, 16>(a, ia, b, ib, 4, 3, K, r4, j4);
+  grid_row<4, 16>(a, ia, b, ib, 5, 2, K, r5, j5);
+  grid_row<4, 16>(a, ia, b, ib, 6, 2, K, r6, j6);
+  grid_row<4, 16>(a, ia, b, ib, 7, 2, K, r7, j7);
+  merge_sorted_kv<4>(r4, j4, r5, j5, y1, k1);
+  merge_sorted_kv<4>(r6, j6, r7, j7, y2, k2);
+  merge_sorted_kv<8>(y1, k1, y2, k2, y, jy);
+  top_merge_kv<16>(f, fi, y, jy);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ------------------------------------------------------ scoring + top-k --
 // One work item = (head h, tile of 128 tokens); per item two halves p, per
 // half the sub-keys in units of up to 256 (TMEM buffer = unit parity).
 // The MMA warp computes S[t, key] = sum_c A[t, c] * B[key, c] into the
 // unit's 256-column TMEM buffer; 8 epilogue warps (one token row per thread,
 // group kh = 0/1 owning the first/second 256 keys of a half) select the
-// half's top-k per row exactly in three steps:
-//   1. maxima of the 16-key groups of the row (one FMNMX per score);
-//   2. tau = k-th largest of those 32 maxima (a lower bound on the k-th
-//      largest score, since the maxima are k+ distinct scores of the row);
-//   3. fold only scores >= tau into a sorted register list (the threshold
-//      leaves ~20 candidates per 512 keys instead of ~150).
-// Group 1 then hands its list to group 0, which merges the two, and after
-// both halves forms the candidate grid, the fp32 softmax and the ids.  A
-// rows come from the query tensor map at h*a_stride_h + p*a_stride_p + t,
-// column offset p*a_col_p; B rows from the key tensor map at p*K + key.
+// half's top-k per row exactly:
+//   1. maxima of the 8-key groups of the row (three-input FMNMX);
+//   2. tau = k-th largest of the half's 64 maxima (sorted top 16 per group,
+//      exchanged): a lower bound on the k-th largest score, since the maxima
+//      are distinct scores of the row;
+//   3. the scores >= tau (about 9 per 256 keys) are compacted into per-lane
+//      shared-memory slots by predicated stores and sorted by a bitonic
+//      network with their key ids.  A warp where some row has more than
+//      CAND_CAP candidates (ties, or scores far from i.i.d.) folds that unit
+//      from TMEM with the exact insertion path instead.
+// The non-owner group hands its sorted list to the owner group (alternating
+// per item), which merges the two by a network and, after both halves, takes
+// the top k of the candidate grid by merge networks, the fp32 softmax and the
+// ids.  A rows come from the query tensor map at h*a_stride_h + p*a_stride_p
+// + t, column offset p*a_col_p; B rows from the key tensor map at p*K + key.
 // With the split-bf16 layout A = [hi | lo] and B = [keys | keys], so S is the
 // fp32 query . key product to ~2^-16.
 constexpr int ROUTER_THREADS = 320;
@@ -112,9 +296,14 @@ constexpr int ROUTER_STAGES = 3;
 constexpr int ROUTER_A_BYTES = 128 * 64 * 2;
 constexpr int ROUTER_B_BYTES_MAX = 256 * 64 * 2;
 constexpr int ROUTER_STAGE_BYTES = ROUTER_A_BYTES + ROUTER_B_BYTES_MAX;
-// candidate staging: 32 x 32 fp32 scores per epilogue warp, plus 32 x 32 int
-// ids for the 4 warps of group 0 (merges and the candidate grid)
-constexpr int ROUTER_CAND_BYTES = 8 * 32 * 32 * 4 + 4 * 32 * 32 * 4;
+// candidate slots per lane: CAND_CAP plus 4 of headroom (the count saturates
+// once per 4 scores), (score, id) pairs laid out [slot][lane]; the fallback
+// fold's 32 x 32 score staging aliases the same per-warp region
+constexpr int CAND_CAP = 20;
+constexpr int CAND_SLOTS = CAND_CAP + 4;
+constexpr int ROUTER_CAND_WARP_BYTES = CAND_SLOTS * 32 * 8;
+static_assert(ROUTER_CAND_WARP_BYTES >= 32 * 32 * 4, "fallback staging must fit the candidate region");
+constexpr int ROUTER_CAND_BYTES = 8 * ROUTER_CAND_WARP_BYTES;
 constexpr int ROUTER_XMAX_BYTES = 2 * 16 * 128 * 4;     // [group][16 maxima][128 rows]
 constexpr int ROUTER_XLIST_BYTES = 2 * 16 * 128 * 4;    // [value|id][16][128 rows]
 
@@ -170,7 +359,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->acc_full[b], 1);
-      mbar_init(&ctl->acc_empty[b], 128);  // one warp group (4 warps) consumes a unit
+      mbar_init(&ctl->acc_empty[b], 256);  // all 8 epilogue warps consume every unit
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -261,202 +450,281 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    // Every participating warp walks all items and hits every named barrier,
-    // also after an abort (work is skipped, barriers are not).
+    // Both groups work on every unit: group grp takes columns [128 grp,
+    // 128 grp + 128) of it.  All their exchanges go through shared memory
+    // between two syncs of named barrier 1 (256 threads): the first makes
+    // sure the previous readers of the region are done, the second publishes
+    // the writes.  Every warp walks all items and takes every sync in the
+    // same order, also after an abort (work is skipped, syncs are not).
     const int ew = warp - 2;
-    const int q = warp & 3;
-    const int kh = ew >> 2;  // key group: units with nc == kh
-    const bool two = num_chunks == 2;
-    if (!two && kh == 1) {
-      // one unit per half: group 0 alone handles every unit
-    } else {
-      const int row = q * 32 + lane;
-      float* stage = reinterpret_cast<float*>(smem + ROUTER_OFF_CAND) + ew * 32 * 32;
-      int* stage_id = reinterpret_cast<int*>(smem + ROUTER_OFF_CAND + 8 * 32 * 32 * 4) + (ew & 3) * 32 * 32;
-      float* xmax = reinterpret_cast<float*>(smem + ROUTER_OFF_XMAX);   // [2][16][128]
-      float* xlv = reinterpret_cast<float*>(smem + ROUTER_OFF_XLIST);   // [16][128]
-      int* xli = reinterpret_cast<int*>(smem + ROUTER_OFF_XLIST) + 16 * 128;
-      int m = 0;  // units consumed by this group
-      bool ok = true;
-      for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
-        const int h = item / num_mt;
-        const int t = (item - h * num_mt) * 128 + row;
-        float lv[2][TOPK];
-        int li[2][TOPK];
+    const int q = warp & 3;    // TMEM lane quarter = rows of this warp
+    const int grp = ew >> 2;   // column half of every unit
+    const int row = q * 32 + lane;
+    uint8_t* wreg = smem + ROUTER_OFF_CAND + ew * ROUTER_CAND_WARP_BYTES;
+    float2* cand = reinterpret_cast<float2*>(wreg) + lane;  // slot s at cand[32 * s]
+    float* stage = reinterpret_cast<float*>(wreg);           // fallback staging [32][32]
+    float* xmax = reinterpret_cast<float*>(smem + ROUTER_OFF_XMAX);   // [2][16][128] maxima
+    // 16 (score, id) pairs per row: group 0 publishes through the list
+    // region, group 1 through the maxima region (free at that point)
+    float* pub_v = reinterpret_cast<float*>(smem + (grp == 0 ? ROUTER_OFF_XLIST : ROUTER_OFF_XMAX));
+    int* pub_i = reinterpret_cast<int*>(pub_v) + 16 * 128;
+    const float* oth_v = reinterpret_cast<const float*>(smem + (grp == 0 ? ROUTER_OFF_XMAX : ROUTER_OFF_XLIST));
+    const int* oth_i = reinterpret_cast<const int*>(oth_v) + 16 * 128;
+    int m = 0;   // units consumed
+    int it = 0;  // items walked
+    bool ok = true;
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
+      const int h = item / num_mt;
+      const int t = (item - h * num_mt) * 128 + row;
+      float lv[2][TOPK];
+      int li[2][TOPK];
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
+      for (int p = 0; p < 2; ++p) {
 #pragma unroll
-          for (int j = 0; j < TOPK; ++j) {
-            lv[p][j] = -INFINITY;
-            li[p][j] = 0;
-          }
-          for (int nc = (two ? kh : 0); nc < num_chunks; nc += (two ? 2 : 1), ++m) {
-            // unit index within this CTA's sequence: two groups alternate
-            // buffers 0/1 (two == true) or one group walks both buffers
-            const int buf = two ? kh : (m & 1);
-            const uint32_t ph = two ? (static_cast<uint32_t>(m) & 1u) : (static_cast<uint32_t>(m >> 1) & 1u);
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], ph, abort, err, 14));
-            const int valid = min(256, g.K - nc * 256);
-            const int key_base = nc * 256;
-            const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256);
-            if (ok) tc_fence_after();
-            // 1. maxima of 16-key groups
-            float mx[16];
+        for (int j = 0; j < TOPK; ++j) {
+          lv[p][j] = -INFINITY;
+          li[p][j] = 0;
+        }
+        for (int nc = 0; nc < num_chunks; ++nc, ++m) {
+          const int buf = m & 1;
+          const uint32_t ph = static_cast<uint32_t>(m >> 1) & 1u;
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], ph, abort, err, 14));
+          const int valid = min(256, g.K - nc * 256);               // multiple of 32
+          const int vg = min(128, max(0, valid - 128 * grp));        // this group's columns
+          const int key0 = nc * 256 + 128 * grp;
+          const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256 + 128 * grp);
+          if (ok) tc_fence_after();
+          // 1. maxima of the 4-key groups of this group's columns, top 16 sorted
+          float t16[16];
+          {
+            float mx[32];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) mx[i] = -INFINITY;
+            for (int i = 0; i < 32; ++i) mx[i] = -INFINITY;
             if (ok) {
 #pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                if (c * 32 < valid) {
-                  float sc[32];
-                  tmem_ld32(cbase + c * 32, sc);
-                  float m0 = sc[0], m1 = sc[16];
+              for (int c = 0; c < 2; ++c) {
+                if (c * 64 < vg) {  // a 32-column tail reads 32 spare columns
+                  float sc[64];
+                  tmem_ld64(cbase + c * 64, sc);
 #pragma unroll
-                  for (int i = 1; i < 16; ++i) {
-                    m0 = fmaxf(m0, sc[i]);
-                    m1 = fmaxf(m1, sc[16 + i]);
+                  for (int g4 = 0; g4 < 16; ++g4) {
+                    const float* v = sc + 4 * g4;
+                    const float mv = fmaxf(fmax3(v[0], v[1], v[2]), v[3]);
+                    mx[16 * c + g4] = (c * 64 + 4 * g4 < vg) ? mv : -INFINITY;
                   }
-                  mx[2 * c] = m0;
-                  mx[2 * c + 1] = m1;
                 }
               }
             }
-            // 2. tau = TOPK-th largest of the row's 16-key maxima (both groups)
-            float tau;
-            if (two) {
+            float hi[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) xmax[(kh * 16 + i) * 128 + row] = mx[i];
-              named_bar_sync(1, 256);
-              float other[16];
+            for (int i = 0; i < 16; ++i) {
+              t16[i] = mx[i];
+              hi[i] = mx[16 + i];
+            }
+            bitonic_sort_desc<16>(t16);
+            bitonic_sort_desc<16>(hi);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) other[i] = xmax[((kh ^ 1) * 16 + i) * 128 + row];
-              if (TOPK == 16) {
-                tau = nth_largest_of_union<16>(mx, other);
-              } else {
-                bitonic_sort_desc<16>(mx);
-                bitonic_sort_desc<16>(other);
-                float u[2 * TOPK];  // TOPK-th largest of the merged top lists
+            for (int i = 0; i < 16; ++i) t16[i] = fmaxf(t16[i], hi[15 - i]);
 #pragma unroll
-                for (int i = 0; i < TOPK; ++i) {
-                  u[i] = mx[i];
-                  u[TOPK + i] = other[i];
+            for (int j = 8; j > 0; j >>= 1) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if ((i & j) == 0) {
+                  const float x = t16[i], y = t16[i | j];
+                  t16[i] = fmaxf(x, y);
+                  t16[i | j] = fminf(x, y);
                 }
-                float a_[TOPK], b_[TOPK];
-#pragma unroll
-                for (int i = 0; i < TOPK; ++i) {
-                  a_[i] = u[i];
-                  b_[i] = u[TOPK + i];
-                }
-                tau = nth_largest_of_union<TOPK>(a_, b_);
-              }
-            } else {
-              // one unit per half: maxima of this unit only (valid/16 of them)
-              const int nmax = valid / 16;
-              if (nmax >= TOPK) {
-                bitonic_sort_desc<16>(mx);
-                tau = mx[TOPK - 1];
-              } else {
-                tau = -INFINITY;
               }
             }
-            // 3. fold scores >= tau
-            if (ok) {
+          }
+          // 2. tau = TOPK-th largest of the unit's 64 maxima: a lower bound on
+          //    the unit's TOPK-th largest score (the maxima are distinct
+          //    scores), so every score of the half's top TOPK that lies in
+          //    this unit is >= tau
+          named_bar_sync(1, 256);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) xmax[(grp * 16 + i) * 128 + row] = t16[i];
+          named_bar_sync(1, 256);
+          float tau = -INFINITY;
+          if (valid / 4 >= TOPK) {
+            tau = INFINITY;
+#pragma unroll
+            for (int i = 0; i < TOPK; ++i)
+              tau = fminf(tau, fmaxf(t16[i], xmax[((grp ^ 1) * 16 + TOPK - 1 - i) * 128 + row]));
+          }
+          // 3. compact this group's scores >= tau; release the buffer; sort
+          if (ok) {
+            // Predicated and branch-free: a passing score is stored with its
+            // key id into the next free slot (8-byte slots, [slot][lane] rows
+            // of 256 B) and the slot address advances; rejected scores issue
+            // no shared-memory traffic.  The address saturates at CAND_CAP
+            // once per 4 scores (CAND_SLOTS covers the 4 in between); a
+            // saturated row is an overflow.
+            const uint32_t c0 = smem_u32(cand);
+            const uint32_t ccap = c0 + CAND_CAP * 256u;
+            uint32_t ca = c0;
+            bool over = false;
 #pragma unroll 1
-              for (int c = 0; c < 8; ++c) {
-                if (c * 32 >= valid) break;
+            for (int c = 0; c < 2; ++c) {
+              if (c * 64 >= vg) break;
+              float sc[64];
+              tmem_ld64(cbase + c * 64, sc);
+              int id = key0 + c * 64;
+              const int ng = min(16, (vg - c * 64) / 4);
+#pragma unroll
+              for (int g4 = 0; g4 < 16; ++g4) {
+                if (g4 >= ng) break;
+#pragma unroll
+                for (int i = 0; i < 4; ++i, ++id) {
+                  asm volatile(
+                      "{\n\t.reg .pred p;\n\t"
+                      "setp.ge.f32 p, %1, %2;\n\t"
+                      "@p st.shared.v2.b32 [%0], {%1, %3};\n\t"
+                      "@p add.u32 %0, %0, 256;\n\t}"
+                      : "+r"(ca)
+                      : "f"(sc[4 * g4 + i]), "f"(tau), "r"(id)
+                      : "memory");
+                }
+                over |= ca > ccap;
+                ca = ca > ccap ? ccap : ca;
+              }
+            }
+            const int n = static_cast<int>((ca - c0) >> 8);
+            if (!__any_sync(0xffffffffu, over)) {
+              tc_fence_before();
+              mbar_arrive(&ctl->acc_empty[buf]);  // scores no longer needed
+              float v[16], w[16];
+              int ix[16], iw[16];
+#pragma unroll
+              for (int s2 = 0; s2 < 16; ++s2) {
+                const float2 e = cand[32 * s2];
+                v[s2] = s2 < n ? e.x : -INFINITY;
+                ix[s2] = s2 < n ? __float_as_int(e.y) : 0;
+              }
+#pragma unroll
+              for (int s2 = 0; s2 < 16; ++s2) {
+                w[s2] = -INFINITY;
+                iw[s2] = 0;
+              }
+#pragma unroll
+              for (int s2 = 0; s2 < CAND_CAP - 16; ++s2) {
+                const float2 e = cand[32 * (16 + s2)];
+                w[s2] = 16 + s2 < n ? e.x : -INFINITY;
+                iw[s2] = 16 + s2 < n ? __float_as_int(e.y) : 0;
+              }
+              bitonic_sort_desc_kv<16>(v, ix);
+              {
+                float w4[4];
+                int i4[4];
+#pragma unroll
+                for (int s2 = 0; s2 < 4; ++s2) {
+                  w4[s2] = w[s2];
+                  i4[s2] = iw[s2];
+                }
+                bitonic_sort_desc_kv<4>(w4, i4);
+#pragma unroll
+                for (int s2 = 0; s2 < 4; ++s2) {
+                  w[s2] = w4[s2];
+                  iw[s2] = i4[s2];
+                }
+              }
+              top_merge_kv<16>(v, ix, w, iw);
+              // fold the unit's sorted top TOPK into the half's running list
+              float u[TOPK];
+              int iu[TOPK];
+#pragma unroll
+              for (int j = 0; j < TOPK; ++j) {
+                u[j] = v[j];
+                iu[j] = ix[j];
+              }
+              top_merge_kv<TOPK>(lv[p], li[p], u, iu);
+            } else {
+              // exact insertion from TMEM for this warp (rare)
+              __syncwarp();
+#pragma unroll 1
+              for (int c = 0; c < 4; ++c) {
+                if (c * 32 >= vg) break;
                 float sc[32];
                 tmem_ld32(cbase + c * 32, sc);
-                topk_fold_chunk<TOPK, false>(lv[p], li[p], sc, nullptr, key_base + c * 32, tau, stage, stage_id,
-                                             lane);
+                topk_fold_chunk<TOPK, false>(lv[p], li[p], sc, nullptr, key0 + c * 32, tau, stage, nullptr, lane);
               }
               tc_fence_before();
               mbar_arrive(&ctl->acc_empty[buf]);
             }
-          }
-          if (two) {
-            // group 1 hands its half-p list to group 0
-            if (kh == 1) {
-#pragma unroll
-              for (int j = 0; j < TOPK; ++j) {
-                xlv[j * 128 + row] = lv[p][j];
-                xli[j * 128 + row] = li[p][j];
-              }
-              named_bar_sync(2, 256);
-            } else {
-              named_bar_sync(2, 256);
-              float ov[32];
-              int oi[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                ov[j] = j < TOPK ? xlv[j * 128 + row] : -INFINITY;
-                oi[j] = j < TOPK ? xli[j * 128 + row] : 0;
-              }
-              topk_fold_chunk<TOPK, true>(lv[p], li[p], ov, oi, 0, -INFINITY, stage, stage_id, lane);
-            }
+            __syncwarp();
           }
         }
-        if (kh == 0) {
-          // Top-k of the candidate grid lv[0][i] + lv[1][j].  Only pairs with
-          // (i+1)(j+1) <= TOPK can rank in the top TOPK (every (i', j') with
-          // i' <= i, j' <= j scores at least as high); tau_c = max(a_0 +
-          // b_{k-1}, a_{k-1} + b_0) bounds the k-th largest sum from below.
-          constexpr int NC = (TOPK == 16) ? 50 : (TOPK == 8 ? 20 : 8);
-          float cv[64];
-          int ci[64];
-          int n = 0;
+        // 4. the two groups swap their half-p lists and both merge
+        named_bar_sync(1, 256);
 #pragma unroll
-          for (int i = 0; i < TOPK; ++i) {
-#pragma unroll
-            for (int j = 0; (i + 1) * (j + 1) <= TOPK; ++j) {
-              cv[n] = lv[0][i] + lv[1][j];
-              ci[n] = li[0][i] * g.K + li[1][j];
-              ++n;
-            }
-          }
-#pragma unroll
-          for (int j = NC; j < 64; ++j) {
-            cv[j] = -INFINITY;
-            ci[j] = 0;
-          }
-          const float tau_c = fmaxf(lv[0][0] + lv[1][TOPK - 1], lv[0][TOPK - 1] + lv[1][0]);
-          float fv[TOPK];
-          int fid[TOPK];
+        for (int j = 0; j < TOPK; ++j) {
+          pub_v[j * 128 + row] = lv[p][j];
+          pub_i[j * 128 + row] = li[p][j];
+        }
+        named_bar_sync(1, 256);
+        {
+          float ov[TOPK];
+          int oi[TOPK];
 #pragma unroll
           for (int j = 0; j < TOPK; ++j) {
-            fv[j] = -INFINITY;
-            fid[j] = 0;
+            ov[j] = oth_v[j * 128 + row];
+            oi[j] = oth_i[j * 128 + row];
           }
-          {
-            float c0[32], c1[32];
-            int d0[32], d1[32];
+          top_merge_kv<TOPK>(lv[p], li[p], ov, oi);
+        }
+      }
+      // 5. top TOPK of the candidate grid; for TOPK = 16 the merge tree is
+      //    split: the helper group merges rows 2..7 and publishes them, the
+      //    finishing group (alternating per item) merges rows 0, 1 and the
+      //    singles, then the helper's list, and writes the result
+      const int fin = it & 1;
+      float fv[TOPK];
+      int fid[TOPK];
+      if constexpr (TOPK == 16) {
+        if (grp == fin) {
+          grid_rows01<16>(lv[0], li[0], lv[1], li[1], g.K, fv, fid);
+        } else {
+          grid_rows27<16>(lv[0], li[0], lv[1], li[1], g.K, fv, fid);
+        }
+        named_bar_sync(1, 256);
+        if (grp != fin) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              c0[j] = cv[j];
-              d0[j] = ci[j];
-              c1[j] = cv[32 + j];
-              d1[j] = ci[32 + j];
-            }
-            topk_fold_chunk<TOPK, true>(fv, fid, c0, d0, 0, tau_c, stage, stage_id, lane);
-            topk_fold_chunk<TOPK, true>(fv, fid, c1, d1, 0, tau_c, stage, stage_id, lane);
+          for (int j = 0; j < 16; ++j) {
+            pub_v[j * 128 + row] = fv[j];
+            pub_i[j * 128 + row] = fid[j];
           }
-          if (ok && t < g.T) {
-            // fp32 softmax over the selected scores (model.py:234)
-            float e[TOPK];
-            float sum = 0.f;
+        }
+        named_bar_sync(1, 256);
+        if (grp == fin) {
+          float ov[16];
+          int oi[16];
 #pragma unroll
-            for (int j = 0; j < TOPK; ++j) {
-              e[j] = expf(fv[j] - fv[0]);
-              sum += e[j];
-            }
-            const int64_t o = (static_cast<int64_t>(t) * g.H + h) * TOPK;
-            int4* di = reinterpret_cast<int4*>(ids_out + o);
-            float4* dw = reinterpret_cast<float4*>(w_out + o);
-#pragma unroll
-            for (int j = 0; j < TOPK / 4; ++j) {
-              di[j] = make_int4(fid[4 * j], fid[4 * j + 1], fid[4 * j + 2], fid[4 * j + 3]);
-              dw[j] = make_float4(e[4 * j] / sum, e[4 * j + 1] / sum, e[4 * j + 2] / sum, e[4 * j + 3] / sum);
-            }
+          for (int j = 0; j < 16; ++j) {
+            ov[j] = oth_v[j * 128 + row];
+            oi[j] = oth_i[j * 128 + row];
           }
+          top_merge_kv<16>(fv, fid, ov, oi);
+        }
+      } else {
+        if (grp == fin) grid_topk<TOPK>(lv[0], li[0], lv[1], li[1], g.K, fv, fid);
+      }
+      if (grp == fin && ok && t < g.T) {
+        // fp32 softmax over the selected scores (model.py:234)
+        float e[TOPK];
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < TOPK; ++j) {
+          e[j] = expf(fv[j] - fv[0]);
+          sum += e[j];
+        }
+        const float inv = __frcp_rn(sum);  // e / sum to within an ulp
+        const int64_t o = (static_cast<int64_t>(t) * g.H + h) * TOPK;
+        int4* di = reinterpret_cast<int4*>(ids_out + o);
+        float4* dw = reinterpret_cast<float4*>(w_out + o);
+#pragma unroll
+        for (int j = 0; j < TOPK / 4; ++j) {
+          di[j] = make_int4(fid[4 * j], fid[4 * j + 1], fid[4 * j + 2], fid[4 * j + 3]);
+          dw[j] = make_float4(e[4 * j] * inv, e[4 * j + 1] * inv, e[4 * j + 2] * inv, e[4 * j + 3] * inv);
         }
       }
     }

@@ -117,6 +117,35 @@ def test_product_key_topk_config3(T, K, dq, top_k):
     assert (w.cpu() - w_ref).abs().max().item() <= 2e-3
 
 
+@pytest.mark.parametrize("dup", ["adjacent", "all"])
+def test_product_key_topk_tied_scores(dup):
+    """Duplicated sub-keys make every score appear two (or many) times in a
+    256-key unit, so rows overflow the candidate slots and take the exact
+    fallback fold.  Tied ids are interchangeable, so the check is on the
+    selected scores (recomputed from the returned ids) and on the weights."""
+    H, T, K, dq, top_k = 8, 2048, 512, 256, 16
+    gen = torch.Generator().manual_seed(7)
+    q = torch.randn(H, T, dq, generator=gen).to(torch.bfloat16)
+    keys = (torch.randn(2, K, dq // 2, generator=gen) / (dq // 2) ** 0.5).to(torch.bfloat16)
+    if dup == "adjacent":
+        keys[:, 1::2] = keys[:, 0::2]          # each score twice, side by side
+    else:
+        keys[:, 32:] = keys[:, :32].repeat(1, (K - 32) // 32, 1)  # each score 16 times
+    w, ids = ops.product_key_topk(q.cuda(), keys.cuda(), top_k)
+    torch.cuda.synchronize()
+    ops.check_device_error("cuda")
+    qf, k1, k2 = q.float(), keys[0].float(), keys[1].float()
+    s1 = (qf[..., : dq // 2] @ k1.t()).permute(1, 0, 2)   # [T, H, K]
+    s2 = (qf[..., dq // 2:] @ k2.t()).permute(1, 0, 2)
+    ids = ids.cpu().to(torch.int64)
+    got = s1.gather(-1, ids // K) + s2.gather(-1, ids % K)
+    ref = orc.grid_top_scores(qf, k1, k2, top_k)
+    assert (got - ref).abs().max().item() <= 1e-4
+    assert (ids.unsqueeze(-1) == ids.unsqueeze(-2)).sum(-1).eq(1).all(), "an id was selected twice"
+    w_ref, _, _ = orc.topk_from_queries(qf, k1, k2, top_k)
+    assert (w.cpu() - w_ref).abs().max().item() <= 1e-4
+
+
 # ------------------------------------------------------------ router --
 @pytest.mark.parametrize("cfg,T,stats", [(CFG1, 256, False), (CFG1, 200, True), (CFG2, 512, True)])
 def test_router_forward_eval(cfg, T, stats):
