@@ -151,13 +151,13 @@ template <class Epi, bool AMN, bool BMN, int BN>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit, const Epi& epi,
                   int* err, cudaStream_t stream, const DeviceInfo& dev) {
   auto kern = k_gemm<Epi, AMN, BMN, BN>;
-  int st = smem_attr_once(reinterpret_cast<const void*>(kern), GEMM_SMEM_BYTES);
+  int st = smem_attr_once(reinterpret_cast<const void*>(kern), GemmCfg<Epi>::kSmem);
   if (st != ETHOS_OK) return st;
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (N / BN);
   const int units = tiles * ksplit;
   const int grid = units < dev.sm_count ? units : dev.sm_count;
   if (grid <= 0) return ETHOS_OK;
-  kern<<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, stream>>>(ta, tb, M, N, K, ksplit, epi, err);
+  kern<<<grid, GemmCfg<Epi>::kThreads, GemmCfg<Epi>::kSmem, stream>>>(ta, tb, M, N, K, ksplit, epi, err);
   return launch_status();
 }
 

@@ -50,22 +50,6 @@ __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Packed fp32 pairs (sm_100 f32x2 arithmetic): one 64-bit register pair
-// holds two floats, fma.rn.f32x2 does two FMAs per instruction.
-__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void upk2(unsigned long long v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b,
-                                                    unsigned long long c) {
-  unsigned long long d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
 // 8 fp16 (one uint4) -> 4 packed fp32 pairs
 __device__ __forceinline__ void unpack_h8_x2(const uint4& u, unsigned long long* p) {
   const __half2* h = reinterpret_cast<const __half2*>(&u);

@@ -7,9 +7,9 @@
 //   K-major:  one box of 64 K x rows; UMMA steps K by 32 B inside the atom.
 //   MN-major: boxes of 64 M/N x 64 K (8 KB, MN blocks 8 KB apart = LBO),
 //             8-row K groups 1024 B apart (SBO); UMMA steps K by 2 KB.
-// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31;
-// warps 2-5 take the first half of the tile's columns, warps 6-9 the second).
+// Roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, warps
+// 2.. = 8 or 16 epilogue warps (warp w reads TMEM lanes 32*(w%4)..+31; each
+// run of four consecutive warps takes one column group of the tile).
 // Tiles are 128 x BN x 64 (BN = 128 or 256) with a TMA ring and two BN-column
 // TMEM accumulators, so the epilogue of tile i overlaps the main loop of tile
 // i+1.  Split-K: work unit u covers tile u % tiles and K blocks of slice
@@ -29,8 +29,6 @@ constexpr int GEMM_STAGES = 4;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK * 2;
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK * 2;
 constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
-constexpr int GEMM_THREADS = 320;
-constexpr int GEMM_EPI_THREADS = 256;
 
 struct GemmCtl {
   uint64_t full[GEMM_STAGES];
@@ -42,14 +40,61 @@ struct GemmCtl {
   int abort;
 };
 constexpr int GEMM_COLP_BYTES = 2 * 256 * 8;  // double-buffered per-tile column side data
-constexpr int GEMM_SMEM_BYTES =
-    GEMM_STAGES * GEMM_STAGE_BYTES + GEMM_COLP_BYTES + 1024 + static_cast<int>(sizeof(GemmCtl));
+constexpr int GEMM_STG_WARP_BYTES = 32 * 64;   // per epilogue warp: 32 rows x 64 B store staging
+
+// Launch shape of the kernel for an epilogue: Epi::kEpiWarps epilogue warps
+// (8, or 16 for arithmetic-heavy epilogues, which then overlap their
+// arithmetic, TMEM reads and stores across more warps), and the TMA ring
+// depth that fits next to their staging buffers.
+template <class Epi>
+struct GemmCfg {
+  static constexpr int kEpiWarps = Epi::kEpiWarps;
+  static_assert(kEpiWarps == 8 || kEpiWarps == 16, "8 or 16 epilogue warps");
+  static constexpr int kEpiThreads = 32 * kEpiWarps;
+  static constexpr int kThreads = 64 + kEpiThreads;
+  static constexpr int kStages = kEpiWarps == 16 ? 3 : GEMM_STAGES;
+  static constexpr int kSmem = kStages * GEMM_STAGE_BYTES + GEMM_COLP_BYTES + kEpiWarps * GEMM_STG_WARP_BYTES +
+                               1024 + static_cast<int>(sizeof(GemmCtl));
+  static_assert(kSmem <= 227 * 1024, "GEMM shared memory");
+};
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
 }
 
 // ------------------------------------------------------------- epilogues --
+// Per-warp context of an epilogue call: the warp's 32 output rows start at
+// row0 (nrows of them are inside the matrix) and `stg` is its 2 KB staging
+// buffer.  All 32 lanes call the functor together.
+struct EpiCtx {
+  uint8_t* stg;
+  int row0;
+  int nrows;
+  int lane;
+};
+
+// Warp-cooperative store of 32 rows x 64 bytes.  Lane l holds the 64 bytes
+// of row row0 + l in w[0..3]; they pass through the staging buffer (16-byte
+// pieces XOR-swizzled by (row >> 1) & 3, so both phases are free of bank
+// conflicts) and each store instruction then writes 8 rows x 64 contiguous
+// bytes instead of 32 scattered 16-byte pieces.
+__device__ __forceinline__ void warp_store_rows64(const EpiCtx& cx, const uint4 (&w)[4], char* dst_row0,
+                                                  int64_t stride) {
+  const int l = cx.lane;
+  const int sw = (l >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(cx.stg + l * 64 + ((j ^ sw) << 4)) = w[j];
+  __syncwarp();
+  const int piece = l & 3;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (l >> 2);
+    const uint4 u = *reinterpret_cast<const uint4*>(cx.stg + r * 64 + ((piece ^ ((r >> 1) & 3)) << 4));
+    if (r < cx.nrows) *reinterpret_cast<uint4*>(dst_row0 + r * stride + piece * 16) = u;
+  }
+  __syncwarp();
+}
+
 // Each functor is called per warp-chunk: `row` is this lane's output row and
 // v[0..31] the fp32 accumulators of columns col..col+31.  Rows >= M must be
 // ignored by the functor.  A functor with per-column side data declares
@@ -59,6 +104,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // (indexed by column - n0).
 struct EpiNoColParams {
   static constexpr int kColParamBytes = 0;
+  static constexpr int kEpiWarps = 8;
   __device__ __forceinline__ void load_col_params(int, uint8_t*, int) const {}
 };
 
@@ -73,18 +119,16 @@ struct EpiStoreBF16 : EpiNoColParams {
   int64_t ldo;
   int M;
   float scale;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
-    if (row >= M) return;
-    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ldo + col);
+  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
+    uint4 w[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint4 u;
-      u.x = pack_bf16x2(v[8 * j + 0] * scale, v[8 * j + 1] * scale);
-      u.y = pack_bf16x2(v[8 * j + 2] * scale, v[8 * j + 3] * scale);
-      u.z = pack_bf16x2(v[8 * j + 4] * scale, v[8 * j + 5] * scale);
-      u.w = pack_bf16x2(v[8 * j + 6] * scale, v[8 * j + 7] * scale);
-      dst[j] = u;
+      w[j].x = pack_bf16x2(v[8 * j + 0] * scale, v[8 * j + 1] * scale);
+      w[j].y = pack_bf16x2(v[8 * j + 2] * scale, v[8 * j + 3] * scale);
+      w[j].z = pack_bf16x2(v[8 * j + 4] * scale, v[8 * j + 5] * scale);
+      w[j].w = pack_bf16x2(v[8 * j + 6] * scale, v[8 * j + 7] * scale);
     }
+    warp_store_rows64(cx, w, reinterpret_cast<char*>(out + static_cast<int64_t>(cx.row0) * ldo + col), ldo * 2);
   }
 };
 
@@ -95,7 +139,7 @@ struct EpiStoreF32 : EpiNoColParams {
   int M;
   float scale;
   int accumulate;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*, const EpiCtx&) const {
     if (row >= M) return;
     float4* dst = reinterpret_cast<float4*>(out + static_cast<int64_t>(row) * ldo + col);
 #pragma unroll
@@ -117,7 +161,7 @@ struct EpiAtomicF32 : EpiNoColParams {
   int64_t ldo;
   int M;
   float scale;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*, const EpiCtx&) const {
     if (row >= M) return;
     float* dst = out + static_cast<int64_t>(row) * ldo + col;
 #pragma unroll
@@ -141,6 +185,7 @@ struct EpiAtomicF32 : EpiNoColParams {
 // x_proj is always written fp32 to xp[row][0..dh).
 struct EpiProj {
   static constexpr int kColParamBytes = 8;  // float2 (scale, offset) or (bias, -)
+  static constexpr int kEpiWarps = 8;
   int M;   // tokens
   int HQ;  // H * d_query
   int dq;
@@ -158,21 +203,34 @@ struct EpiProj {
     if (col < HQ) v = mode == 1 ? make_float2(__ldg(bias + col), 0.f) : __ldg(colp + col);
     reinterpret_cast<float2*>(dst)[tid] = v;
   }
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t* cp) const {
-    if (row >= M) return;
+  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t* cp,
+                                             const EpiCtx& cx) const {
     if (col >= HQ) {
-      float4* dst = reinterpret_cast<float4*>(xp + static_cast<int64_t>(row) * dh + (col - HQ));
+      char* dst = reinterpret_cast<char*>(xp + static_cast<int64_t>(cx.row0) * dh + (col - HQ));
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint4 w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          w[j] = make_uint4(__float_as_uint(v[16 * hlf + 4 * j]), __float_as_uint(v[16 * hlf + 4 * j + 1]),
+                            __float_as_uint(v[16 * hlf + 4 * j + 2]), __float_as_uint(v[16 * hlf + 4 * j + 3]));
+        warp_store_rows64(cx, w, dst + 64 * hlf, static_cast<int64_t>(dh) * 4);
+      }
       return;
     }
     const float2* cpc = reinterpret_cast<const float2*>(cp) + (col & 255);
     if (mode == 1) {
-      float4* dst = reinterpret_cast<float4*>(qpre + static_cast<int64_t>(row) * HQ + col);
+      char* dst = reinterpret_cast<char*>(qpre + static_cast<int64_t>(cx.row0) * HQ + col);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        dst[j] = make_float4(v[4 * j] + cpc[4 * j].x, v[4 * j + 1] + cpc[4 * j + 1].x,
-                             v[4 * j + 2] + cpc[4 * j + 2].x, v[4 * j + 3] + cpc[4 * j + 3].x);
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint4 w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int b = 16 * hlf + 4 * j;
+          w[j] = make_uint4(__float_as_uint(v[b] + cpc[b].x), __float_as_uint(v[b + 1] + cpc[b + 1].x),
+                            __float_as_uint(v[b + 2] + cpc[b + 2].x), __float_as_uint(v[b + 3] + cpc[b + 3].x));
+        }
+        warp_store_rows64(cx, w, dst + 64 * hlf, static_cast<int64_t>(HQ) * 4);
       }
       return;
     }
@@ -181,7 +239,7 @@ struct EpiProj {
     const int half = dq >> 1;
     const int p = e >= half ? 1 : 0;
     const int i0 = e - p * half;
-    __nv_bfloat16* base = qs + (static_cast<int64_t>(p * (HQ / dq) + h) * M + row) * dq;
+    __nv_bfloat16* base = qs + (static_cast<int64_t>(p * (HQ / dq) + h) * M + cx.row0) * dq;
     const float4* cp4 = reinterpret_cast<const float4*>(cpc);
     uint32_t hi[16], lo[16];
 #pragma unroll
@@ -195,13 +253,14 @@ struct EpiProj {
       hi[i] = *reinterpret_cast<const uint32_t*>(&h2);
       lo[i] = *reinterpret_cast<const uint32_t*>(&l2);
     }
-    uint4* dh_ = reinterpret_cast<uint4*>(base + i0);
-    uint4* dl_ = reinterpret_cast<uint4*>(base + half + i0);
+    uint4 wh[4], wl[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      dh_[j] = make_uint4(hi[4 * j], hi[4 * j + 1], hi[4 * j + 2], hi[4 * j + 3]);
-      dl_[j] = make_uint4(lo[4 * j], lo[4 * j + 1], lo[4 * j + 2], lo[4 * j + 3]);
+      wh[j] = make_uint4(hi[4 * j], hi[4 * j + 1], hi[4 * j + 2], hi[4 * j + 3]);
+      wl[j] = make_uint4(lo[4 * j], lo[4 * j + 1], lo[4 * j + 2], lo[4 * j + 3]);
     }
+    warp_store_rows64(cx, wh, reinterpret_cast<char*>(base + i0), static_cast<int64_t>(dq) * 2);
+    warp_store_rows64(cx, wl, reinterpret_cast<char*>(base + half + i0), static_cast<int64_t>(dq) * 2);
   }
 };
 
@@ -209,21 +268,30 @@ struct EpiProj {
 // expansion GEMM E @ W1^T (row = expert id, col = hidden unit; model.py:323
 // evaluated once per expert instead of once per selection).
 struct EpiGeluF16 : EpiNoColParams {
+  static constexpr int kEpiWarps = 16;  // 0.117 ms vs 0.126 ms with 8 (262144 x 512 table)
   __half* out;
   int64_t ldo;
   int M;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
-    if (row >= M) return;
-    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ldo + col);
+  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
+    uint4 w4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint32_t w[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const __half2 hh = __floats2half2_rn(gelu_erf(v[8 * j + 2 * u]), gelu_erf(v[8 * j + 2 * u + 1]));
+        float g0, g1;
+        gelu_erf2(v[8 * j + 2 * u], v[8 * j + 2 * u + 1], g0, g1);
+        const __half2 hh = __floats2half2_rn(g0, g1);
         w[u] = *reinterpret_cast<const uint32_t*>(&hh);
       }
-      dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+      w4[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    // direct per-row stores: this epilogue is bound by the GELU arithmetic,
+    // where the staged transpose costs more than it saves (measured)
+    if (cx.lane < cx.nrows) {
+      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(cx.row0 + cx.lane) * ldo + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = w4[j];
     }
   }
 };
@@ -231,27 +299,37 @@ struct EpiGeluF16 : EpiNoColParams {
 // Backward tables: H = fp16(gelu_erf(v)) and G = fp16(gelu_erf'(v)) for the
 // pre-activations v = E @ W1^T of every expert.
 struct EpiGeluBwdF16 : EpiNoColParams {
+  static constexpr int kEpiWarps = 8;  // measured faster than 16 for this epilogue
   __half* h_out;
   __half* g_out;
   int64_t ldo;
   int M;
-  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t*) const {
-    if (row >= M) return;
-    uint4* dh = reinterpret_cast<uint4*>(h_out + static_cast<int64_t>(row) * ldo + col);
-    uint4* dg = reinterpret_cast<uint4*>(g_out + static_cast<int64_t>(row) * ldo + col);
+  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
+    uint4 h4[4], g4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint32_t wh[4], wg[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float a = v[8 * j + 2 * u], b = v[8 * j + 2 * u + 1];
-        const __half2 hh = __floats2half2_rn(gelu_erf(a), gelu_erf(b));
-        const __half2 gg = __floats2half2_rn(gelu_erf_grad(a), gelu_erf_grad(b));
+        float ga, gb, da, db;
+        gelu_erf_and_grad2(v[8 * j + 2 * u], v[8 * j + 2 * u + 1], ga, gb, da, db);
+        const __half2 hh = __floats2half2_rn(ga, gb);
+        const __half2 gg = __floats2half2_rn(da, db);
         wh[u] = *reinterpret_cast<const uint32_t*>(&hh);
         wg[u] = *reinterpret_cast<const uint32_t*>(&gg);
       }
-      dh[j] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-      dg[j] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+      h4[j] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+      g4[j] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+    }
+    if (cx.lane < cx.nrows) {  // direct stores, as in EpiGeluF16
+      const int64_t off = static_cast<int64_t>(cx.row0 + cx.lane) * ldo + col;
+      uint4* dh = reinterpret_cast<uint4*>(h_out + off);
+      uint4* dg = reinterpret_cast<uint4*>(g_out + off);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dh[j] = h4[j];
+        dg[j] = g4[j];
+      }
     }
   }
 };
@@ -276,17 +354,20 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32_major(int M, int N, b
 }
 
 template <class Epi, bool kAMN, bool kBMN, int BN>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
            int ksplit, Epi epi, int* err) {
   static_assert(BN == 128 || BN == 256, "N tile is 128 or 256");
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
-  constexpr int CHUNKS_PER_HALF = BN / 64;  // 32-column chunks per epilogue column half
+  using Cfg = GemmCfg<Epi>;
+  constexpr int STAGES = Cfg::kStages;
+  constexpr int CHUNKS = (BN / 32) / (Cfg::kEpiWarps / 4);  // 32-column chunks per epilogue warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* colp_s = smem + GEMM_STAGES * GEMM_STAGE_BYTES;
-  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(colp_s + GEMM_COLP_BYTES);
+  uint8_t* colp_s = smem + STAGES * GEMM_STAGE_BYTES;
+  uint8_t* stg_s = colp_s + GEMM_COLP_BYTES;
+  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(stg_s + Cfg::kEpiWarps * GEMM_STG_WARP_BYTES);
   const int warp = warp_id();
   const int lane = lane_id();
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
@@ -297,13 +378,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int num_units = num_tiles * ksplit;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GEMM_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->acc_full[b], 1);
-      mbar_init(&ctl->acc_empty[b], GEMM_EPI_THREADS);
+      mbar_init(&ctl->acc_empty[b], Cfg::kEpiThreads);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -352,10 +433,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           } else {
             tma_load_2d(sb, &tmB, &ctl->full[rp.stage], kb * GEMM_BK, n0);
           }
-          rp.advance(GEMM_STAGES);
+          rp.advance(STAGES);
         }
       }
-      if (!ok) rp.drain(ctl->full, GEMM_STAGES, err, 5);
+      if (!ok) rp.drain(ctl->full, STAGES, err, 5);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -390,7 +471,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             umma_bf16(d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&ctl->empty[stage]);
-          if (++stage == GEMM_STAGES) {
+          if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -408,7 +489,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // Epilogue warps never leave the unit loop early: after an abort they skip
     // the work but still take every named barrier, so no partner can block.
     const int q = warp & 3;
-    const int ch = (warp - 2) >> 2;  // column half of the tile
+    const int ch = (warp - 2) >> 2;  // column group of the tile (CHUNKS chunks each)
     int it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
@@ -421,18 +502,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (Epi::kColParamBytes > 0) {
         // stage this tile's column data (its previous user, unit it-2, was
         // released by the barrier of unit it-1)
-        epi.load_col_params(n0, cps, static_cast<int>(threadIdx.x) - 64);
-        named_bar_sync(1, GEMM_EPI_THREADS);
+        const int tid = static_cast<int>(threadIdx.x) - 64;
+        if (tid < 256) epi.load_col_params(n0, cps, tid);
+        named_bar_sync(1, Cfg::kEpiThreads);
       }
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], acc_phase, abort, err, 4));
       if (!ok) continue;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
+      const EpiCtx cx{stg_s + (warp - 2) * GEMM_STG_WARP_BYTES, m0 + q * 32, min(32, M - (m0 + q * 32)), lane};
 #pragma unroll 1
-      for (int c = ch * CHUNKS_PER_HALF; c < (ch + 1) * CHUNKS_PER_HALF; ++c) {
+      for (int c = ch * CHUNKS; c < (ch + 1) * CHUNKS; ++c) {
         float v[32];
         tmem_ld32(tmem_addr(tmem, q * 32, buf * BN + c * 32), v);
-        epi(row, n0 + c * 32, v, cps);
+        epi(row, n0 + c * 32, v, cps, cx);
       }
       tc_fence_before();
       mbar_arrive(&ctl->acc_empty[buf]);

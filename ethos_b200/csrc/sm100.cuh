@@ -296,15 +296,115 @@ __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint
 }
 
 // ------------------------------------------------------------------- math --
-// Exact (erf-based) GELU, as torch.nn.functional.gelu(approximate='none').
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one 64-bit register pair
+// holds two floats, fma.rn.f32x2 does two FMAs per instruction.
+__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
 }
-// d/dx GELU(x) = Phi(x) + x * phi(x)
+__device__ __forceinline__ void upk2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b,
+                                                    unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ float ex2_approx(float t) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
+  return r;
+}
+
+// The erf-form GELU, GELU(x) = x Phi(x) (torch.nn.functional.gelu with
+// approximate='none'), with the normal CDF written through the scaled
+// complementary error function:
+//   Phi(x) = 1 - h (x >= 0),  Phi(x) = h (x < 0),
+//   h = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt(2)),
+// erfcx evaluated by a degree-11 least-squares polynomial in
+// s = min(|x| / (4.2 sqrt(2)), 1) (csrc/fit_gelu.py derives the coefficients:
+// |Phi error| <= 1.8e-6, |GELU error| <= 1e-6 with fp32 evaluation) and the
+// exponential by one ex2.  d GELU / dx = Phi(x) + x phi(x) reuses the same
+// exponential: phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
+namespace gelu_detail {
+constexpr float kS = 0.16835875f;      // 1 / (4.2 sqrt(2))
+constexpr float kE = -0.72134752f;     // -log2(e) / 2
+constexpr float kPdf = 0.39894228f;    // 1 / sqrt(2 pi)
+constexpr float C0 = 9.999964237e-01f, C1 = -4.738096237e+00f, C2 = 1.758333588e+01f, C3 = -5.456176758e+01f,
+                C4 = 1.427009735e+02f, C5 = -3.059054565e+02f, C6 = 5.142192993e+02f, C7 = -6.464071045e+02f,
+                C8 = 5.776085815e+02f, C9 = -3.432381897e+02f, C10 = 1.208973465e+02f, C11 = -1.902811050e+01f;
+}  // namespace gelu_detail
+
+// Phi(x) and e = exp(-x^2 / 2)
+__device__ __forceinline__ float gelu_phi(float x, float& e) {
+  using namespace gelu_detail;
+  const float s = fminf(fabsf(x) * kS, 1.0f);
+  float p = C11;
+  p = fmaf(p, s, C10);
+  p = fmaf(p, s, C9);
+  p = fmaf(p, s, C8);
+  p = fmaf(p, s, C7);
+  p = fmaf(p, s, C6);
+  p = fmaf(p, s, C5);
+  p = fmaf(p, s, C4);
+  p = fmaf(p, s, C3);
+  p = fmaf(p, s, C2);
+  p = fmaf(p, s, C1);
+  p = fmaf(p, s, C0);
+  e = ex2_approx(x * x * kE);
+  const float h = 0.5f * e * p;
+  return x >= 0.0f ? 1.0f - h : h;
+}
+// The same for two values, the polynomial on packed pairs.
+__device__ __forceinline__ void gelu_phi2(float x0, float x1, float& phi0, float& phi1, float& e0, float& e1) {
+  using namespace gelu_detail;
+  const unsigned long long s = pk2(fminf(fabsf(x0) * kS, 1.0f), fminf(fabsf(x1) * kS, 1.0f));
+  unsigned long long p = pk2(C11, C11);
+  p = ffma2(p, s, pk2(C10, C10));
+  p = ffma2(p, s, pk2(C9, C9));
+  p = ffma2(p, s, pk2(C8, C8));
+  p = ffma2(p, s, pk2(C7, C7));
+  p = ffma2(p, s, pk2(C6, C6));
+  p = ffma2(p, s, pk2(C5, C5));
+  p = ffma2(p, s, pk2(C4, C4));
+  p = ffma2(p, s, pk2(C3, C3));
+  p = ffma2(p, s, pk2(C2, C2));
+  p = ffma2(p, s, pk2(C1, C1));
+  p = ffma2(p, s, pk2(C0, C0));
+  float p0, p1;
+  upk2(p, p0, p1);
+  e0 = ex2_approx(x0 * x0 * kE);
+  e1 = ex2_approx(x1 * x1 * kE);
+  const float h0 = 0.5f * e0 * p0, h1 = 0.5f * e1 * p1;
+  phi0 = x0 >= 0.0f ? 1.0f - h0 : h0;
+  phi1 = x1 >= 0.0f ? 1.0f - h1 : h1;
+}
+__device__ __forceinline__ float gelu_erf(float x) {
+  float e;
+  return x * gelu_phi(x, e);
+}
 __device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
-  const float pdf = 0.39894228040143267794f * expf(-0.5f * x * x);
-  return cdf + x * pdf;
+  float e;
+  const float phi = gelu_phi(x, e);
+  return fmaf(x * gelu_detail::kPdf, e, phi);
+}
+__device__ __forceinline__ void gelu_erf2(float x0, float x1, float& g0, float& g1) {
+  float p0, p1, e0, e1;
+  gelu_phi2(x0, x1, p0, p1, e0, e1);
+  g0 = x0 * p0;
+  g1 = x1 * p1;
+}
+// GELU and its derivative of two values from one evaluation
+__device__ __forceinline__ void gelu_erf_and_grad2(float x0, float x1, float& g0, float& g1, float& d0, float& d1) {
+  float p0, p1, e0, e1;
+  gelu_phi2(x0, x1, p0, p1, e0, e1);
+  g0 = x0 * p0;
+  g1 = x1 * p1;
+  d0 = fmaf(x0 * gelu_detail::kPdf, e0, p0);
+  d1 = fmaf(x1 * gelu_detail::kPdf, e1, p1);
 }
 
 // Warp transpose-reduce: on entry lane l holds v[0..31] (32 columns of one
