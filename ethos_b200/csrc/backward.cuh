@@ -73,74 +73,70 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
   const int b3 = (lane >> 3) & 1, b4 = (lane >> 4) & 1;
   const int grp = (lane >> 3) & 3;
 
-  auto load_ids = [&](int b) -> int4 {
-    if (b >= nb) return make_int4(0, 0, 0, 0);
-    const int t = gw + (b / nbt) * nw;
-    const int r0 = (b % nbt) * GATHER_ROWS;
-    return __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(t) * R + r0));
-  };
-  auto issue = [&](int b, int4 id4) {
-    const int t = gw + (b / nbt) * nw;
-    const int r0 = (b % nbt) * GATHER_ROWS;
-    uint8_t* st = wbase + (b % STAGES) * BGATHER_STAGE_BYTES;
-    const int idv[4] = {id4.x, id4.y, id4.z, id4.w};
+  // Cursors instead of div/mod by the runtime batch count: the issue cursor
+  // (token it_t, its local index it_k, row it_r) runs STAGES-1 batches ahead
+  // of the consume cursor; the token index parity picks the dhacc / xp
+  // double buffer.
+  int it_t = gw, it_k = 0, it_r = 0, it_n = 0;
+  bool bad_id = false;
+  int4 next_ids = nb > 0 ? __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(gw) * R))
+                         : make_int4(0, 0, 0, 0);
+  auto issue_next = [&]() {
+    if (it_n < nb) {
+      const int t = it_t, r0 = it_r;
+      uint8_t* st = wbase + (it_n % STAGES) * BGATHER_STAGE_BYTES;
+      const int idv[4] = {next_ids.x, next_ids.y, next_ids.z, next_ids.w};
 #pragma unroll
-    for (int u = 0; u < GATHER_ROWS; ++u) {
-      int id = idv[u];
-      if (id < 0 || id >= N) {
-        if (lane == 0) record_error(err, ETHOS_ERR_ID_OUT_OF_RANGE);
-        id = 0;
+      for (int u = 0; u < GATHER_ROWS; ++u) {
+        const bool bad = static_cast<unsigned>(idv[u]) >= static_cast<unsigned>(N);
+        bad_id |= bad;
+        const char* src = reinterpret_cast<const char*>(table + static_cast<int64_t>(bad ? 0 : idv[u]) * 512);
+        cp_async_16(st + u * 1024 + 16 * lane, src + 16 * lane);
+        cp_async_16(st + u * 1024 + 512 + 16 * lane, src + 512 + 16 * lane);
       }
-      const char* src = reinterpret_cast<const char*>(table + static_cast<int64_t>(id) * 512);
-      cp_async_16(st + u * 1024 + 16 * lane, src + 16 * lane);
-      cp_async_16(st + u * 1024 + 512 + 16 * lane, src + 512 + 16 * lane);
+      if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
+      if (lane == 1) cp_async_16(st + GATHER_ROWS * 1024 + 16, dot + static_cast<int64_t>(t) * R + r0);
+      if (r0 == 0) {
+        const char* xs = reinterpret_cast<const char*>(dhacc + static_cast<int64_t>(t) * 512);
+        uint8_t* xd = vbuf + (it_k & 1) * 2048;
+        cp_async_16(xd + 32 * lane, xs + 32 * lane);
+        cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
+        cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
+        cp_async_16(xd + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
+        const char* ps = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
+        uint8_t* pd = xbuf + (it_k & 1) * 2048;
+        cp_async_16(pd + 32 * lane, ps + 32 * lane);
+        cp_async_16(pd + 32 * lane + 16, ps + 32 * lane + 16);
+        cp_async_16(pd + 1024 + 32 * lane, ps + 1024 + 32 * lane);
+        cp_async_16(pd + 1024 + 32 * lane + 16, ps + 1024 + 32 * lane + 16);
+      }
+      ++it_n;
+      it_r += GATHER_ROWS;
+      if (it_r == R) {
+        it_r = 0;
+        it_t += nw;
+        ++it_k;
+      }
+      if (it_n < nb) next_ids = __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(it_t) * R + it_r));
     }
-    if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
-    if (lane == 1) cp_async_16(st + GATHER_ROWS * 1024 + 16, dot + static_cast<int64_t>(t) * R + r0);
-    if (r0 == 0) {
-      const char* xs = reinterpret_cast<const char*>(dhacc + static_cast<int64_t>(t) * 512);
-      uint8_t* xd = vbuf + ((b / nbt) & 1) * 2048;
-      cp_async_16(xd + 32 * lane, xs + 32 * lane);
-      cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
-      cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
-      cp_async_16(xd + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
-      const char* ps = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
-      uint8_t* pd = xbuf + ((b / nbt) & 1) * 2048;
-      cp_async_16(pd + 32 * lane, ps + 32 * lane);
-      cp_async_16(pd + 32 * lane + 16, ps + 32 * lane + 16);
-      cp_async_16(pd + 1024 + 32 * lane, ps + 1024 + 32 * lane);
-      cp_async_16(pd + 1024 + 32 * lane + 16, ps + 1024 + 32 * lane + 16);
-    }
+    cp_async_commit();
   };
 
-  int4 next_ids = load_ids(0);
 #pragma unroll 1
-  for (int b = 0; b < STAGES - 1; ++b) {
-    const int4 cur = next_ids;
-    next_ids = load_ids(b + 1);
-    if (b < nb) issue(b, cur);
-    cp_async_commit();
-  }
+  for (int b = 0; b < STAGES - 1; ++b) issue_next();
   float gv[16];
   unsigned long long gv2[8];   // dhacc columns as packed pairs
   unsigned long long acc2[8];  // dxp columns as packed pairs
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc2[i] = 0ull;
+  int t = gw, tk = 0, r0 = 0;  // consume cursor
 #pragma unroll 1
   for (int b = 0; b < nb; ++b) {
-    {
-      const int bi = b + STAGES - 1;
-      const int4 cur = next_ids;
-      next_ids = load_ids(bi + 1);
-      if (bi < nb) issue(bi, cur);
-      cp_async_commit();
-    }
+    issue_next();
     cp_async_wait_group<STAGES - 1>();
-    const int t = gw + (b / nbt) * nw;
-    const int r0 = (b % nbt) * GATHER_ROWS;
     const uint8_t* st = wbase + (b % STAGES) * BGATHER_STAGE_BYTES;
     if (r0 == 0) {
-      const float4* x4 = reinterpret_cast<const float4*>(vbuf + ((b / nbt) & 1) * 2048);
+      const float4* x4 = reinterpret_cast<const float4*>(vbuf + (tk & 1) * 2048);
       const float4 a0 = x4[2 * lane], a1 = x4[2 * lane + 1], c0 = x4[64 + 2 * lane], c1 = x4[64 + 2 * lane + 1];
       gv[0] = a0.x; gv[1] = a0.y; gv[2] = a0.z; gv[3] = a0.w;
       gv[4] = a1.x; gv[5] = a1.y; gv[6] = a1.z; gv[7] = a1.w;
@@ -152,7 +148,7 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
         acc2[i] = 0ull;
       }
       // bf16 copy of this token's [dhacc | xp] row for the per-expert pass
-      const float4* p4 = reinterpret_cast<const float4*>(xbuf + ((b / nbt) & 1) * 2048);
+      const float4* p4 = reinterpret_cast<const float4*>(xbuf + (tk & 1) * 2048);
       const float4 e0 = p4[2 * lane], e1 = p4[2 * lane + 1], f0 = p4[64 + 2 * lane], f1 = p4[64 + 2 * lane + 1];
       __nv_bfloat16* gr = gx + static_cast<int64_t>(t) * 1024;
       auto pk = [](float a, float b) {
@@ -231,8 +227,15 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
       *reinterpret_cast<uint4*>(ud + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
       *reinterpret_cast<uint4*>(ud + 256 + 8 * lane) = make_uint4(o[4], o[5], o[6], o[7]);
     }
+    r0 += GATHER_ROWS;
+    if (r0 == R) {
+      r0 = 0;
+      t += nw;
+      ++tk;
+    }
   }
   cp_async_wait_group<0>();
+  if (__any_sync(0xffffffffu, bad_id) && lane == 0) record_error(err, ETHOS_ERR_ID_OUT_OF_RANGE);
 }
 
 // ------------------------------------------------------------------------

@@ -94,65 +94,59 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
   const int b3 = (lane >> 3) & 1, b4 = (lane >> 4) & 1;
   const int grp = (lane >> 3) & 3;  // row of the batch whose dot this lane ends up holding
 
-  // ids of the next batch to issue, loaded one issue ahead (int4 broadcast)
-  auto load_ids = [&](int b) -> int4 {
-    if (b >= nb) return make_int4(0, 0, 0, 0);
-    const int t = gw + (b / nbt) * nw;
-    const int r0 = (b % nbt) * GATHER_ROWS;
-    return __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(t) * R + r0));
-  };
-  auto issue = [&](int b, int4 id4) {
-    const int t = gw + (b / nbt) * nw;
-    const int r0 = (b % nbt) * GATHER_ROWS;
-    uint8_t* st = wbase + (b % GATHER_STAGES) * GATHER_STAGE_BYTES;
-    const int idv[4] = {id4.x, id4.y, id4.z, id4.w};
+  // Cursors instead of div/mod by the runtime batch count: the issue cursor
+  // (token it_t, row it_r) runs STAGES-1 batches ahead of the consume cursor.
+  static_assert((GATHER_STAGES & (GATHER_STAGES - 1)) == 0, "ring depth is a power of two");
+  int it_t = gw, it_r = 0, it_n = 0;
+  bool bad_id = false;
+  // ids of the batch at the issue cursor, loaded one issue ahead (int4 broadcast)
+  int4 next_ids = nb > 0 ? __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(gw) * R))
+                         : make_int4(0, 0, 0, 0);
+  auto issue_next = [&]() {
+    if (it_n < nb) {
+      const int t = it_t, r0 = it_r;
+      uint8_t* st = wbase + (it_n & (GATHER_STAGES - 1)) * GATHER_STAGE_BYTES;
+      const int idv[4] = {next_ids.x, next_ids.y, next_ids.z, next_ids.w};
 #pragma unroll
-    for (int u = 0; u < GATHER_ROWS; ++u) {
-      int id = idv[u];
-      if (id < 0 || id >= N) {
-        if (lane == 0) record_error(err, ETHOS_ERR_ID_OUT_OF_RANGE);
-        id = 0;
+      for (int u = 0; u < GATHER_ROWS; ++u) {
+        const bool bad = static_cast<unsigned>(idv[u]) >= static_cast<unsigned>(N);
+        bad_id |= bad;
+        const char* src = reinterpret_cast<const char*>(table + static_cast<int64_t>(bad ? 0 : idv[u]) * 512);
+        cp_async_16(st + u * 1024 + 16 * lane, src + 16 * lane);
+        cp_async_16(st + u * 1024 + 512 + 16 * lane, src + 512 + 16 * lane);
       }
-      const char* src = reinterpret_cast<const char*>(table + static_cast<int64_t>(id) * 512);
-      cp_async_16(st + u * 1024 + 16 * lane, src + 16 * lane);
-      cp_async_16(st + u * 1024 + 512 + 16 * lane, src + 512 + 16 * lane);
+      if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
+      if (r0 == 0) {  // first batch of a token also brings this lane's x_proj slices
+        const char* xs = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
+        cp_async_16(xpbuf + 32 * lane, xs + 32 * lane);
+        cp_async_16(xpbuf + 32 * lane + 16, xs + 32 * lane + 16);
+        cp_async_16(xpbuf + 1024 + 32 * lane, xs + 1024 + 32 * lane);
+        cp_async_16(xpbuf + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
+      }
+      // advance the issue cursor and prefetch its ids
+      ++it_n;
+      it_r += GATHER_ROWS;
+      if (it_r == R) {
+        it_r = 0;
+        it_t += nw;
+      }
+      if (it_n < nb) next_ids = __ldg(reinterpret_cast<const int4*>(ids + static_cast<int64_t>(it_t) * R + it_r));
     }
-    if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
-    if (r0 == 0) {  // first batch of a token also brings this lane's x_proj slices
-      const char* xs = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
-      uint8_t* xd = xpbuf;
-      cp_async_16(xd + 32 * lane, xs + 32 * lane);
-      cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
-      cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
-      cp_async_16(xd + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
-    }
+    cp_async_commit();
   };
 
-  int4 next_ids = load_ids(0);
 #pragma unroll 1
-  for (int b = 0; b < GATHER_STAGES - 1; ++b) {
-    const int4 cur = next_ids;
-    next_ids = load_ids(b + 1);
-    if (b < nb) issue(b, cur);
-    cp_async_commit();
-  }
+  for (int b = 0; b < GATHER_STAGES - 1; ++b) issue_next();
   unsigned long long xv2[8];   // this lane's x_proj columns as packed pairs
   unsigned long long acc2[8];  // hacc columns as packed pairs
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc2[i] = 0ull;
+  int t = gw, r0 = 0;  // consume cursor
 #pragma unroll 1
   for (int b = 0; b < nb; ++b) {
-    {
-      const int bi = b + GATHER_STAGES - 1;
-      const int4 cur = next_ids;
-      next_ids = load_ids(bi + 1);
-      if (bi < nb) issue(bi, cur);
-      cp_async_commit();
-    }
+    issue_next();
     cp_async_wait_group<GATHER_STAGES - 1>();
-    const int t = gw + (b / nbt) * nw;
-    const int r0 = (b % nbt) * GATHER_ROWS;
-    const uint8_t* st = wbase + (b % GATHER_STAGES) * GATHER_STAGE_BYTES;
+    const uint8_t* st = wbase + (b & (GATHER_STAGES - 1)) * GATHER_STAGE_BYTES;
     if (r0 == 0) {
       const float4* x4 = reinterpret_cast<const float4*>(xpbuf);
       // this lane's x_proj columns [8l, 8l+8) and [256+8l, 256+8l+8)
@@ -215,8 +209,14 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
       *reinterpret_cast<uint4*>(dst + 8 * lane) = make_uint4(o[0], o[1], o[2], o[3]);
       *reinterpret_cast<uint4*>(dst + 256 + 8 * lane) = make_uint4(o[4], o[5], o[6], o[7]);
     }
+    r0 += GATHER_ROWS;
+    if (r0 == R) {
+      r0 = 0;
+      t += nw;
+    }
   }
   cp_async_wait_group<0>();
+  if (__any_sync(0xffffffffu, bad_id) && lane == 0) record_error(err, ETHOS_ERR_ID_OUT_OF_RANGE);
 }
 
 }  // namespace ethos
