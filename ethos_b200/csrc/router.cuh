@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
                 iw[s2] = 16 + s2 < n ? __float_as_int(e.y) : 0;
               }
               bitonic_sort_desc_kv<16>(v, ix);
-              {
+              if (__any_sync(0xffffffffu, n > 16)) {  // slots 16..19 in use somewhere in the warp
                 float w4[4];
                 int i4[4];
 #pragma unroll
@@ -627,17 +627,26 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
                   w[s2] = w4[s2];
                   iw[s2] = i4[s2];
                 }
+                top_merge_kv<16>(v, ix, w, iw);
               }
-              top_merge_kv<16>(v, ix, w, iw);
               // fold the unit's sorted top TOPK into the half's running list
-              float u[TOPK];
-              int iu[TOPK];
+              // (the first unit of a half starts it)
+              if (nc == 0) {
 #pragma unroll
-              for (int j = 0; j < TOPK; ++j) {
-                u[j] = v[j];
-                iu[j] = ix[j];
+                for (int j = 0; j < TOPK; ++j) {
+                  lv[p][j] = v[j];
+                  li[p][j] = ix[j];
+                }
+              } else {
+                float u[TOPK];
+                int iu[TOPK];
+#pragma unroll
+                for (int j = 0; j < TOPK; ++j) {
+                  u[j] = v[j];
+                  iu[j] = ix[j];
+                }
+                top_merge_kv<TOPK>(lv[p], li[p], u, iu);
               }
-              top_merge_kv<TOPK>(lv[p], li[p], u, iu);
             } else {
               // exact insertion from TMEM for this warp (rare)
               __syncwarp();
