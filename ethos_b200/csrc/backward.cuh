@@ -540,17 +540,18 @@ __global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int
   reinterpret_cast<float4*>(coef)[col] = make_float4(gi, B, -gi * m1 - B * mean[col], 0.f);
 }
 
-// One thread per 8 consecutive columns of a token (C % 8 == 0);
-// coef[c] = (A, B, C, 0) from k_bn_bwd_finalize.
+// One thread per 8 consecutive columns (C % 8 == 0), grid x over the column
+// groups and y over the token rows (as k_bn_apply); coef[c] = (A, B, C, 0)
+// from k_bn_bwd_finalize.
 __global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __restrict__ qpre,
                                const float4* __restrict__ coef, int T, int C, __nv_bfloat16* __restrict__ du,
                                int64_t ldu) {
-  const int groups = C / 8;
-  const int64_t n = static_cast<int64_t>(T) * groups;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int t = static_cast<int>(i / groups);
-    const int c0 = static_cast<int>(i - static_cast<int64_t>(t) * groups) * 8;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= C) return;
+  float4 k[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) k[u] = __ldg(coef + c0 + u);
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
     const int64_t o = static_cast<int64_t>(t) * C + c0;
     const float4 g0 = *reinterpret_cast<const float4*>(dqh + o), g1 = *reinterpret_cast<const float4*>(dqh + o + 4);
     const float4 q0 = *reinterpret_cast<const float4*>(qpre + o), q1 = *reinterpret_cast<const float4*>(qpre + o + 4);
@@ -559,9 +560,8 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __res
     uint32_t out[4];
 #pragma unroll
     for (int u = 0; u < 8; u += 2) {
-      const float4 ka = __ldg(coef + c0 + u), kb = __ldg(coef + c0 + u + 1);
-      const float r0 = fmaf(ka.x, gv[u], fmaf(ka.y, qv[u], ka.z));
-      const float r1 = fmaf(kb.x, gv[u + 1], fmaf(kb.y, qv[u + 1], kb.z));
+      const float r0 = fmaf(k[u].x, gv[u], fmaf(k[u].y, qv[u], k[u].z));
+      const float r1 = fmaf(k[u + 1].x, gv[u + 1], fmaf(k[u + 1].y, qv[u + 1], k[u + 1].z));
       const __nv_bfloat162 b = __floats2bfloat162_rn(r0, r1);
       out[u >> 1] = *reinterpret_cast<const uint32_t*>(&b);
     }

@@ -271,6 +271,17 @@ int check_dims_impl(const ethos_dims* d) {
   return ETHOS_OK;
 }
 
+// Grid of the row-walking BatchNorm kernels: x covers the C / 8 column groups,
+// y enough token rows to give every SM several blocks.
+dim3 bn_rows_grid(int C, int T, int threads, const DeviceInfo& dev) {
+  const int gx = (C / 8 + threads - 1) / threads;
+  int gy = dev.sm_count * 8 / (gx > 0 ? gx : 1);
+  if (gy < 1) gy = 1;
+  if (gy > T) gy = T;
+  if (gy > 65535) gy = 65535;
+  return dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+}
+
 // ------------------------------------------------------------ experts --
 // Expert execution path: 1 = fused per-token (gather latents, expand on
 // tcgen05, GELU in the epilogue), 2 = expert table (expand + GELU once per
@@ -402,10 +413,8 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
                                                            bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, save_bn,
                                                            s.colp);
     }
-    const int64_t groups = static_cast<int64_t>(T) * (HQ / 8);
-    k_bn_apply<<<static_cast<unsigned>((groups + cb - 1) / cb), cb, 0, stream>>>(qpre, s.colp, T,
-                                                                                static_cast<int>(d.num_heads), dq,
-                                                                                qs);
+    k_bn_apply<<<bn_rows_grid(HQ, T, cb, dev), cb, 0, stream>>>(qpre, s.colp, T, static_cast<int>(d.num_heads),
+                                                                 dq, qs);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   mark(ev, ETHOS_STAGE_BATCHNORM, stream);
@@ -960,8 +969,9 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
     k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, T, HQ, s.part);
     k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, mean,
                                                         invstd, d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
-    k_bn_bwd_apply<<<eblocks, cb, 0, sm>>>(s.dqhat, save_qpre, reinterpret_cast<const float4*>(s.coef), T, HQ,
-                                           s.du, LDU);
+    k_bn_bwd_apply<<<bn_rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(s.dqhat, save_qpre,
+                                                                 reinterpret_cast<const float4*>(s.coef), T, HQ,
+                                                                 s.du, LDU);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   // (12) dx = du @ W_cat          (W_cat read in place, MN-major)

@@ -286,8 +286,8 @@ struct EpiGeluF16 : EpiNoColParams {
       }
       w4[j] = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    // direct per-row stores: this epilogue is bound by the GELU arithmetic,
-    // where the staged transpose costs more than it saves (measured)
+    // direct per-row stores: with one output the staged transpose costs more
+    // than it saves here (0.127 vs 0.117 ms, measured)
     if (cx.lane < cx.nrows) {
       uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(cx.row0 + cx.lane) * ldo + col);
 #pragma unroll
@@ -299,7 +299,7 @@ struct EpiGeluF16 : EpiNoColParams {
 // Backward tables: H = fp16(gelu_erf(v)) and G = fp16(gelu_erf'(v)) for the
 // pre-activations v = E @ W1^T of every expert.
 struct EpiGeluBwdF16 : EpiNoColParams {
-  static constexpr int kEpiWarps = 8;  // measured faster than 16 for this epilogue
+  static constexpr int kEpiWarps = 16;
   __half* h_out;
   __half* g_out;
   int64_t ldo;
@@ -321,16 +321,11 @@ struct EpiGeluBwdF16 : EpiNoColParams {
       h4[j] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
       g4[j] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
     }
-    if (cx.lane < cx.nrows) {  // direct stores, as in EpiGeluF16
-      const int64_t off = static_cast<int64_t>(cx.row0 + cx.lane) * ldo + col;
-      uint4* dh = reinterpret_cast<uint4*>(h_out + off);
-      uint4* dg = reinterpret_cast<uint4*>(g_out + off);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        dh[j] = h4[j];
-        dg[j] = g4[j];
-      }
-    }
+    // two outputs: the staged transpose pays here (whole backward 2.50 ->
+    // 2.38 ms at config 5), unlike in the one-output forward table
+    const int64_t off = static_cast<int64_t>(cx.row0) * ldo + col;
+    warp_store_rows64(cx, h4, reinterpret_cast<char*>(h_out + off), ldo * 2);
+    warp_store_rows64(cx, g4, reinterpret_cast<char*>(g_out + off), ldo * 2);
   }
 };
 

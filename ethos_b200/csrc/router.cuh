@@ -814,40 +814,42 @@ __global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, i
 
 // Normalisation pass on qpre [T, C] -> split-bf16 scoring operand
 // qs[p][h][t][hi | lo].  One thread per 8 consecutive columns.
+// Grid: x covers the column groups of 8 (blockDim.x threads each), y walks the
+// token rows, so the per-thread column math (head, half, offset) is computed
+// once and no thread divides by runtime sizes inside the row loop.
 __global__ void k_bn_apply(const float* __restrict__ qpre, const float2* __restrict__ colp, int T, int H, int dq,
                            __nv_bfloat16* __restrict__ qs) {
   const int C = H * dq;
-  const int groups = C / 8;
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<int64_t>(T) * groups) return;
-  const int t = static_cast<int>(idx / groups);
-  const int col = static_cast<int>(idx - static_cast<int64_t>(t) * groups) * 8;
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (col >= C) return;
   const int h = col / dq;
   const int e = col - h * dq;
   const int half = dq >> 1;
   const int p = e >= half ? 1 : 0;
   const int i0 = e - p * half;
-  const float4* src = reinterpret_cast<const float4*>(qpre + static_cast<int64_t>(t) * C + col);
-  const float4 a = src[0], b = src[1];
-  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  uint32_t hi[4], lo[4];
+  float2 cp[8];
 #pragma unroll
-  for (int i = 0; i < 8; i += 2) {
-    float qn[2];
+  for (int u = 0; u < 8; ++u) cp[u] = colp[col + u];
+  __nv_bfloat16* qbase = qs + static_cast<int64_t>(p * H + h) * T * dq;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
+    const float4* src = reinterpret_cast<const float4*>(qpre + static_cast<int64_t>(t) * C + col);
+    const float4 a = src[0], b = src[1];
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float2 cp = colp[col + i + u];
-      qn[u] = fmaf(v[i + u], cp.x, cp.y);
+    for (int i = 0; i < 8; i += 2) {
+      const float q0 = fmaf(v[i], cp[i].x, cp[i].y);
+      const float q1 = fmaf(v[i + 1], cp[i + 1].x, cp[i + 1].y);
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(q0, q1);
+      const float2 hf = __bfloat1622float2(h2);
+      const __nv_bfloat162 l2 = __floats2bfloat162_rn(q0 - hf.x, q1 - hf.y);
+      hi[i >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+      lo[i >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
     }
-    const __nv_bfloat162 h2 = __floats2bfloat162_rn(qn[0], qn[1]);
-    const float2 hf = __bfloat1622float2(h2);
-    const __nv_bfloat162 l2 = __floats2bfloat162_rn(qn[0] - hf.x, qn[1] - hf.y);
-    hi[i >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
-    lo[i >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
+    __nv_bfloat16* base = qbase + static_cast<int64_t>(t) * dq;
+    *reinterpret_cast<uint4*>(base + i0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(base + half + i0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
-  __nv_bfloat16* base = qs + (static_cast<int64_t>(p * H + h) * T + t) * dq;
-  *reinterpret_cast<uint4*>(base + i0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-  *reinterpret_cast<uint4*>(base + half + i0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 }  // namespace ethos
