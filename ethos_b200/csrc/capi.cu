@@ -426,6 +426,7 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   g.a_stride_h = T;
   g.a_stride_p = static_cast<int>(d.num_heads) * T;
   g.a_col_p = 0;
+  g.split = 1;
   st = run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, err, stream, dev);
   mark(ev, ETHOS_STAGE_TOPK, stream);
   return st;
@@ -681,6 +682,7 @@ int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* ke
   g.a_stride_h = T;
   g.a_stride_p = 0;
   g.a_col_p = half;
+  g.split = 0;
   return run_score(tm_q, tm_k, g, static_cast<int>(d.top_k), ids, weights, dev_err,
                    static_cast<cudaStream_t>(stream), *dev);
 }

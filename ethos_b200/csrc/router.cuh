@@ -289,13 +289,16 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // the top k of the candidate grid by merge networks, the fp32 softmax and the
 // ids.  A rows come from the query tensor map at h*a_stride_h + p*a_stride_p
 // + t, column offset p*a_col_p; B rows from the key tensor map at p*K + key.
-// With the split-bf16 layout A = [hi | lo] and B = [keys | keys], so S is the
-// fp32 query . key product to ~2^-16.
+// With the split-bf16 layout A = [hi | lo] and each key box multiplies both
+// halves, so S is the fp32 query . key product to ~2^-16.
 constexpr int ROUTER_THREADS = 320;
-constexpr int ROUTER_STAGES = 3;
+// A stage holds 64 K-columns of A (hi and, with the split layout, the matching
+// lo columns) and of the keys; with the split layout one key box serves both
+// the hi and the lo MMAs, so the keys cross L2 -> shared memory once.
+constexpr int ROUTER_STAGES = 2;
 constexpr int ROUTER_A_BYTES = 128 * 64 * 2;
 constexpr int ROUTER_B_BYTES_MAX = 256 * 64 * 2;
-constexpr int ROUTER_STAGE_BYTES = ROUTER_A_BYTES + ROUTER_B_BYTES_MAX;
+constexpr int ROUTER_STAGE_BYTES = 2 * ROUTER_A_BYTES + ROUTER_B_BYTES_MAX;
 // candidate slots per lane: CAND_CAP plus 4 of headroom (the count saturates
 // once per 4 scores), (score, id) pairs laid out [slot][lane]; the fallback
 // fold's 32 x 32 score staging aliases the same per-warp region
@@ -330,6 +333,7 @@ struct RouterGeom {
   int a_stride_h; // A row offset per head
   int a_stride_p; // A row offset per half
   int a_col_p;    // A column offset per half
+  int split;      // 1: A = [hi | lo] (KA columns), keys in columns [0, KA / 2)
 };
 
 __device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
@@ -349,8 +353,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
   const int num_items = g.H * num_mt;
   const int box_rows = g.K < 256 ? g.K : 256;   // keys per unit (TMA box rows, MMA N)
   const int num_chunks = (g.K + 255) / 256;     // units per half (1 or 2)
-  const int num_kb = g.KA / 64;
-  const uint32_t stage_tx = ROUTER_A_BYTES + box_rows * 128;
+  const int num_kb = (g.split ? g.KA / 2 : g.KA) / 64;  // stages per unit
+  const uint32_t stage_tx = (g.split ? 2 : 1) * ROUTER_A_BYTES + box_rows * 128;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ROUTER_STAGES; ++s) {
@@ -395,7 +399,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
               uint8_t* sa = smem + rp.stage * ROUTER_STAGE_BYTES;
               mbar_arrive_expect_tx(&ctl->full[rp.stage], stage_tx);
               tma_load_2d(sa, &tmA, &ctl->full[rp.stage], p * g.a_col_p + kb * 64, a_row);
-              tma_load_2d(sa + ROUTER_A_BYTES, &tmB, &ctl->full[rp.stage], kb * 64, p * g.K + nc * 256);
+              if (g.split) tma_load_2d(sa + ROUTER_A_BYTES, &tmA, &ctl->full[rp.stage], g.KA / 2 + kb * 64, a_row);
+              tma_load_2d(sa + 2 * ROUTER_A_BYTES, &tmB, &ctl->full[rp.stage], kb * 64, p * g.K + nc * 256);
               rp.advance(ROUTER_STAGES);
             }
           }
@@ -427,11 +432,17 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
             }
             tc_fence_after();
             const uint32_t a_base = smem_u32(smem + stage * ROUTER_STAGE_BYTES);
-            const uint32_t b_base = a_base + ROUTER_A_BYTES;
+            const uint32_t b_base = a_base + 2 * ROUTER_A_BYTES;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               umma_bf16(d, umma_desc_sw128(a_base + k * 32), umma_desc_sw128(b_base + k * 32), idesc,
                         (kb | k) != 0 ? 1u : 0u);
+            }
+            if (g.split) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma_bf16(d, umma_desc_sw128(a_base + ROUTER_A_BYTES + k * 32), umma_desc_sw128(b_base + k * 32),
+                          idesc, 1u);
             }
             umma_commit(&ctl->empty[stage]);
             if (++stage == ROUTER_STAGES) {
