@@ -207,17 +207,20 @@ def run_reference(args, rank, world):
 def run_train(args, rank, world, local, dev):
     """Config 5: one training step per iteration -- forward (BatchNorm in
     training mode), backward through all 37 parameters, NCCL all-reduce of
-    the gradients (world > 1) and an SGD update, 16384 tokens per GPU."""
+    the gradients (world > 1) and a fused AdamW update, 16384 tokens per GPU."""
     import torch.distributed as dist
     from ethos_b200 import ops
     from ethos_b200.dist import GradAllReducer
     from ethos_b200.init import seeded_input, tensor_generator
+    from ethos_b200.optim import FusedAdamW
     layer = build_layer(dev).train()
     T = args.tokens
     x = seeded_input(T, CFG2["d_model"], seed=rank).to(device=dev, dtype=torch.bfloat16)
     gy = (torch.randn((T, CFG2["d_model"]), generator=tensor_generator(rank, "bench.gy")) * 1e-3).to(
         device=dev, dtype=torch.bfloat16)
-    opt = torch.optim.SGD(layer.parameters(), lr=1e-3)
+    # AdamW as the reference's DeepSpeed config (train.py:74-79), fused over all
+    # of the layer's parameters in one launch, fp32 master weights for bf16
+    opt = FusedAdamW(layer.parameters(), lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
     reducer = GradAllReducer(list(layer.parameters())) if world > 1 else None
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -260,9 +263,67 @@ def run_train(args, rank, world, local, dev):
                     warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
                     vs_baseline=None, dtype="bf16", data="synthetic",
                     config=dict(workload="config 5: ETHOS expert layer training step (forward, backward, "
-                                         "gradient all-reduce, SGD update), BN train mode",
+                                         "gradient all-reduce, fused AdamW update with fp32 master "
+                                         "weights), BN train mode",
                                 tokens_per_gpu=T, global_batch=T * world, parallelism=f"dp{world}",
                                 l2="flushed between timed steps (256 MiB write)"),
+                    clocks=clocks)
+        print(json.dumps(line), flush=True)
+
+
+def run_router(args, rank, world, local, dev):
+    """Config 3: product-key routing micro-benchmark -- 65 536 normalised
+    queries per head for 8 heads (N(0,1), bf16, d_key 256), two 512 x 128
+    sub-key tables, top-16 per half, top-16 of the candidate sums, int32 ids
+    and fp32 softmax weights (ethos_product_key_topk).  Unit: query-heads."""
+    import torch.distributed as dist
+    from ethos_b200 import ops
+    from ethos_b200.init import tensor_generator
+    H, Q, dk, K, k = 8, 65536, 256, 512, 16
+    g = tensor_generator(rank, "bench.router")
+    q = torch.randn((H, Q, dk), generator=g).to(device=dev, dtype=torch.bfloat16)
+    keys = (torch.randn((2, K, dk // 2), generator=g) / (dk // 2) ** 0.5).to(device=dev, dtype=torch.bfloat16)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        ops.product_key_topk(q, keys, k)
+    torch.cuda.synchronize()
+    ops.check_device_error(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for s_, e_ in ev:
+        flush.zero_()
+        s_.record(stream)
+        ops.product_key_topk(q, keys, k)
+        e_.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    peaks = load_peaks()
+    flops = 2.0 * 2 * K * (dk // 2) * H * Q
+    if rank == 0:
+        tf = flops / (ms / 1e3) / 1e12
+        line = dict(metric="product-key routing query-heads/s (2 x 512 sub-keys, d_key 256, top-16)",
+                    value=H * Q * world / (ms / 1e3), unit="query-heads/s", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
+                    vs_baseline=None, dtype="bf16", data="synthetic",
+                    config=dict(workload="config 3: product-key routing microbenchmark, 65536 queries x 8 heads, "
+                                         "bf16 queries, fp32 scores, int32 ids + fp32 weights",
+                                queries_per_head=Q, heads=H, parallelism=f"dp{world}",
+                                l2="flushed between timed steps (256 MiB write)"),
+                    roofline=dict(bound="tensor", kernel="k_score_topk<16>", achieved=tf,
+                                  peak=peaks["bf16_tflops"], unit="TFLOP/s", frac=tf / peaks["bf16_tflops"],
+                                  traffic=None, peak_source=peaks["source"] + " bf16 burst"),
                     clocks=clocks)
         print(json.dumps(line), flush=True)
 
@@ -276,8 +337,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
-    ap.add_argument("--mode", default="forward", choices=["forward", "train"],
-                    help="forward: config 2 (headline); train: config 5 training step")
+    ap.add_argument("--mode", default="forward", choices=["forward", "train", "router"],
+                    help="forward: config 2 (headline); train: config 5 training step; "
+                         "router: config 3 routing microbenchmark")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -296,8 +358,8 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    if args.mode == "train":
-        run_train(args, rank, world, local, dev)
+    if args.mode in ("train", "router"):
+        (run_train if args.mode == "train" else run_router)(args, rank, world, local, dev)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

@@ -69,6 +69,7 @@ EXPORTS = {
     "ethos_product_key_topk": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _F, _I, _P, _P]),
     "ethos_gemm_bf16_ex": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _F, _I, _P, _P]),
+    "ethos_adamw_step": (_I, [_P, _I, _I64, _F, _F, _F, _F, _F, _I64, _P, _P]),
 }
 
 _lock = threading.Lock()

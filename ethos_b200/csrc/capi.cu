@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <mutex>
 
 #include "ethos_b200.h"
@@ -14,6 +15,7 @@
 #include "backward.cuh"
 #include "gemm.cuh"
 #include "router.cuh"
+#include "optim.cuh"
 
 using namespace ethos;
 
@@ -1013,6 +1015,34 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
       return st;
   }
   return ETHOS_OK;
+}
+
+int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t max_n, float lr, float beta1,
+                     float beta2, float eps, float weight_decay, int64_t step, int* dev_err, void* stream) {
+  (void)dev_err;
+  if (num_tensors == 0 || max_n == 0) return ETHOS_OK;
+  if (tensors == nullptr || num_tensors < 0 || num_tensors > 65535 || max_n < 0 || step < 1)
+    return ETHOS_ERR_INVALID_ARG;
+  if (!(beta1 >= 0.f && beta1 < 1.f && beta2 >= 0.f && beta2 < 1.f && eps > 0.f)) return ETHOS_ERR_INVALID_ARG;
+  int st;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  AdamScalars s;
+  s.lr = lr;
+  s.beta1 = beta1;
+  s.beta2 = beta2;
+  s.eps = eps;
+  s.wd = weight_decay;
+  s.step_size = static_cast<float>(lr / (1.0 - std::pow(static_cast<double>(beta1), static_cast<double>(step))));
+  s.bc2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(static_cast<double>(beta2), static_cast<double>(step))));
+  const int threads = 256;
+  int64_t bx = (max_n + threads * 4 - 1) / (threads * 4);
+  const int64_t cap = static_cast<int64_t>(dev->sm_count) * 8;
+  if (bx > cap) bx = cap;
+  if (bx < 1) bx = 1;
+  k_adamw<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(num_tensors)), threads, 0,
+            static_cast<cudaStream_t>(stream)>>>(tensors, s);
+  return launch_status();
 }
 
 }  // extern "C"

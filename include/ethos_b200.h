@@ -247,6 +247,31 @@ int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b
                        void* d, int64_t ldd, int64_t M, int64_t N, int64_t K, float scale, int out_mode,
                        int* dev_err, void* stream);
 
+/* ------------------------------------------------------ optimizer step --
+ * Fused AdamW over many tensors in one launch, the update the reference's
+ * training runs through DeepSpeed (train.py:68-104: AdamW, ZeRO-2 with bf16
+ * weights and fp32 master copies).  Per element, exactly
+ * torch.optim.AdamW(weight_decay=wd) at step `step` (>= 1):
+ *   p <- p (1 - lr wd);  m <- m + (1 - b1)(g - m);  v <- b2 v + (1 - b2) g^2
+ *   p <- p - (lr / (1 - b1^step)) m / (sqrt(v) / sqrt(1 - b2^step) + eps)
+ * `p` is `master` (fp32) when given, whose new value is then also written to
+ * `param` rounded to its dtype; otherwise `param` itself (fp32 or bf16).
+ * `tensors` is a DEVICE array of `num_tensors` descriptors; `max_n` is the
+ * largest `n` among them (sizes the launch).  Grad dtype: fp32 or bf16. */
+typedef struct ethos_adam_tensor {
+  void* param;        /* fp32 or bf16 [n]                                     */
+  const void* grad;   /* fp32 or bf16 [n]                                     */
+  float* exp_avg;     /* fp32 [n]                                             */
+  float* exp_avg_sq;  /* fp32 [n]                                             */
+  float* master;      /* fp32 [n] or NULL                                     */
+  int64_t n;
+  int32_t param_bf16; /* 1 if param is bf16                                   */
+  int32_t grad_bf16;  /* 1 if grad is bf16                                    */
+} ethos_adam_tensor;
+
+int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t max_n, float lr, float beta1,
+                     float beta2, float eps, float weight_decay, int64_t step, int* dev_err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
