@@ -210,7 +210,7 @@ def run_train(args, rank, world, local, dev):
     the gradients (world > 1) and a fused AdamW update, 16384 tokens per GPU."""
     import torch.distributed as dist
     from ethos_b200 import ops
-    from ethos_b200.dist import GradAllReducer
+    from ethos_b200.dist import overlap_grad_allreduce
     from ethos_b200.init import seeded_input, tensor_generator
     from ethos_b200.optim import FusedAdamW
     layer = build_layer(dev).train()
@@ -221,7 +221,8 @@ def run_train(args, rank, world, local, dev):
     # AdamW as the reference's DeepSpeed config (train.py:74-79), fused over all
     # of the layer's parameters in one launch, fp32 master weights for bf16
     opt = FusedAdamW(layer.parameters(), lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
-    reducer = GradAllReducer(list(layer.parameters())) if world > 1 else None
+    if world > 1:
+        overlap_grad_allreduce(layer)  # all-reduce inside the backward, overlapped
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -229,8 +230,6 @@ def run_train(args, rank, world, local, dev):
         opt.zero_grad(set_to_none=True)
         y = layer(x.view(1, T, -1))
         y.backward(gy.view(1, T, -1))
-        if reducer is not None:
-            reducer()
         opt.step()
 
     for _ in range(args.warmup):

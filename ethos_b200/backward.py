@@ -1,4 +1,6 @@
-"""Autograd backward of EthosExpertLayer.
+"""Autograd backward of EthosExpertLayer (and, under
+``ethos_b200.dist.overlap_grad_allreduce``, the data-parallel gradient
+all-reduce overlapped with it).
 
 Maps the gradients computed by ``ethos_layer_backward`` (one C-ABI call, see
 include/ethos_b200.h) onto the inputs of ``_EthosLayerFunction``: x, the layer
@@ -8,8 +10,31 @@ query_norms weights, query_norms biases, sub_keys_1, sub_keys_2.
 """
 
 import torch
+import torch.distributed as dist
 
 from . import ops
+
+
+def _overlapped_allreduce(layer, g, events):
+    """Averages the flat fp32 gradient buffer over the process group set by
+    ``ethos_b200.dist.overlap_grad_allreduce``: the latent and W1 slice as soon
+    as the backward marks them final (ETHOS_BWD_STAGE_EXPERTS), the rest at
+    its end, both on a side stream so the first overlaps the router and
+    BatchNorm gradient kernels; the current stream then waits for both."""
+    comm = layer._grad_comm
+    flat = g["flat"]
+    boundary = g["layout"][2][1]  # d_latents, d_w1 come first; d_w2 starts here
+    if comm.get("stream") is None or comm["stream"].device != flat.device:
+        comm["stream"] = torch.cuda.Stream(flat.device)
+    side = comm["stream"]
+    works = []
+    with torch.cuda.stream(side):
+        side.wait_event(events[0])
+        works.append(dist.all_reduce(flat[:boundary], op=dist.ReduceOp.AVG, group=comm["group"], async_op=True))
+        side.wait_event(events[1])
+        works.append(dist.all_reduce(flat[boundary:], op=dist.ReduceOp.AVG, group=comm["group"], async_op=True))
+    for w in works:
+        w.wait()  # the current stream waits; the host does not block
 
 
 def layer_backward(ctx, gy):
@@ -19,7 +44,14 @@ def layer_backward(ctx, gy):
     H = layer.num_heads
     dq = layer.router.d_query
     eps, _ = layer.router._bn_eps_momentum()
-    g = ops.layer_backward(gy.reshape(-1, gy.shape[-1]), sv["x16"], pw, sv, ctx.training_bn, eps)
+    comm = getattr(layer, "_grad_comm", None)
+    overlap = comm is not None and dist.is_available() and dist.is_initialized() and \
+        dist.get_world_size(comm["group"]) > 1
+    events = [torch.cuda.Event(), torch.cuda.Event()] if overlap else None
+    g = ops.layer_backward(gy.reshape(-1, gy.shape[-1]), sv["x16"], pw, sv, ctx.training_bn, eps,
+                           stage_events=events)
+    if overlap:
+        _overlapped_allreduce(layer, g, events)
     params = ctx.params
     grads = [g["dx"].to(ctx.x_dtype)]
     dtypes = {p.dtype for p in params}

@@ -27,7 +27,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[ETHOS_NOALLOC_S
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 
 // ------------------------------------------------------------ device cache --
 struct DeviceInfo {
@@ -804,7 +804,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
                          const float* save_bn, const void* save_qs, float* dx, float* d_latents, float* d_w1,
                          float* d_w2, float* d_wq, float* d_bn, float* d_keys, void* workspace,
-                         size_t workspace_bytes, int* dev_err, void* stream) {
+                         size_t workspace_bytes, int* dev_err, void* const* stage_events, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (d_latents == nullptr && (dims->num_heads * dims->top_k) < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
@@ -935,6 +935,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                    auto_ksplit(EX_DH, EX_DL, N, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
       return st;
   }
+  mark(stage_events, ETHOS_BWD_STAGE_EXPERTS, sm);  // d_latents, d_w1 final
   // (9) router: softmax backward, dq^ and the dense sub-key score gradient dS
   switch (d.top_k) {
     case 4: st = launch_router_bwd<4>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq, s.dqhat,
@@ -1014,6 +1015,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                    *dev)) != ETHOS_OK)
       return st;
   }
+  mark(stage_events, ETHOS_BWD_STAGE_END, sm);
   return ETHOS_OK;
 }
 

@@ -5,11 +5,12 @@ i.e. data parallelism with the gradients reduced across ranks.  Here:
 
 * the forward needs no communication: every rank runs its own token shard
   against the full (replicated) latent table, hypernetwork and router;
-* after the backward, ``GradAllReducer`` sums the gradients of the latent
-  table, hypernetwork, query projections, BatchNorm affine and sub-keys over
-  the ranks in flat fp32 buckets (NCCL over NVLink on B200; any
-  ``torch.distributed`` backend works, gloo is used by the CPU tests) and
-  divides by the world size;
+* the gradients of the latent table, hypernetwork, query projections,
+  BatchNorm affine and sub-keys are averaged over the ranks in fp32 (NCCL over
+  NVLink on B200): either by ``overlap_grad_allreduce`` inside the layer's
+  backward, overlapped with it, or after the backward by ``GradAllReducer``
+  in flat fp32 buckets (any ``torch.distributed`` backend; gloo in the CPU
+  tests);
 * BatchNorm uses each rank's batch statistics, as the reference does (no
   SyncBN); ``average_running_stats`` optionally averages the running
   statistics so that ranks evaluate identically.
@@ -18,7 +19,7 @@ i.e. data parallelism with the gradients reduced across ranks.  Here:
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_range", "shard_tokens", "GradAllReducer", "average_running_stats"]
+__all__ = ["shard_range", "shard_tokens", "GradAllReducer", "average_running_stats", "overlap_grad_allreduce"]
 
 
 def shard_range(total, rank, world):
@@ -33,6 +34,23 @@ def shard_tokens(x, rank, world, dim=0):
     return x.narrow(dim, start, stop - start)
 
 
+def overlap_grad_allreduce(module, group=None):
+    """Let every EthosExpertLayer in ``module`` average its parameter gradients
+    over ``group`` inside its own backward: the backward's flat fp32 gradient
+    buffer is all-reduced (NCCL ``AVG``) in two slices, the latent table and
+    W1 while the router and BatchNorm gradients are still being computed, the
+    rest at the end, and the parameter gradients are formed from the reduced
+    buffer -- no separate pack / unpack pass.  ``GradAllReducer`` skips these
+    parameters.  Every rank must run the same backward.  Returns the layers."""
+    from .layer import EthosExpertLayer
+    layers = [m for m in module.modules() if isinstance(m, EthosExpertLayer)]
+    for layer in layers:
+        layer._grad_comm = dict(group=group, stream=None)
+        for p in layer.parameters():
+            p._ethos_allreduced = True
+    return layers
+
+
 class GradAllReducer:
     """Sums the ``.grad`` of ``params`` over the process group in flat fp32
     buckets of about ``bucket_bytes`` and divides by the world size.
@@ -42,7 +60,8 @@ class GradAllReducer:
     same order).  A parameter without a gradient contributes zeros."""
 
     def __init__(self, params, group=None, bucket_bytes=64 << 20, average=True):
-        self.params = [p for p in params if p.requires_grad]
+        # parameters whose layer reduces them in its backward are left alone
+        self.params = [p for p in params if p.requires_grad and not getattr(p, "_ethos_allreduced", False)]
         self.group = group
         self.average = average
         self.buckets = []
@@ -58,6 +77,8 @@ class GradAllReducer:
             self.buckets.append(cur)
 
     def __call__(self):
+        if not self.buckets:
+            return
         world = dist.get_world_size(self.group)
         handles = []
         flats = []

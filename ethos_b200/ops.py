@@ -34,6 +34,9 @@ def _events(evs):
         return None
     handles = []
     for e in evs:
+        if e is None:
+            handles.append(None)
+            continue
         if e.cuda_event == 0:
             e.record()
         handles.append(e.cuda_event)
@@ -246,11 +249,19 @@ def _numel(shape):
     return n
 
 
-def layer_backward(dy, x16, pw, saved, bn_training, eps):
+BWD_STAGE_EXPERTS, BWD_STAGE_END = 0, 1  # ETHOS_BWD_STAGE_* (include/ethos_b200.h)
+
+
+def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
     """Gradients of the layer (see ethos_layer_backward).  ``dy`` [T, d] bf16
     or fp32; ``saved`` is the dict returned by ``layer_forward(save=True)``.
     Returns a dict of fp32 tensors: dx, d_latents, d_w1, d_w2, d_wq [H*dq, d],
-    d_bn [3, H*dq] (bias, gamma, beta), d_keys [2, K, dq/2]."""
+    d_bn [3, H*dq] (bias, gamma, beta), d_keys [2, K, dq/2], and the flat fp32
+    buffer holding all parameter gradients (``flat``, ``layout``).
+    ``stage_events``: optional [experts_done, end] ``torch.cuda.Event`` (or
+    None entries), recorded as ETHOS_BWD_STAGE_* describe."""
+    if stage_events is not None and len(stage_events) != 2:
+        raise ValueError("stage_events: one event (or None) per ETHOS_BWD_STAGE_*")
     _require_cuda(dy, "dy")
     d = pw.dims
     T = dy.shape[0]
@@ -289,6 +300,7 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps):
                                  _vp(saved["weights"]), _vp(saved["xp"]), _vp(saved["hacc"]), _vp(saved["dot"]),
                                  _vp(saved["qpre"]), _vp(saved.get("bn_stats")), _vp(saved["qs"]), _vp(g["dx"]),
                                  _vp(g["d_latents"]), _vp(g["d_w1"]), _vp(g["d_w2"]), _vp(g["d_wq"]),
-                                 _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws), ws_bytes, _vp(err), _stream(dev)),
+                                 _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws), ws_bytes, _vp(err),
+                                 _events(stage_events), _stream(dev)),
           "ethos_layer_backward")
     return g

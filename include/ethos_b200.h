@@ -229,7 +229,17 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
                          const float* save_bn, const void* save_qs, float* dx, float* d_latents, float* d_w1,
                          float* d_w2, float* d_wq, float* d_bn, float* d_keys, void* workspace,
-                         size_t workspace_bytes, int* dev_err, void* stream);
+                         size_t workspace_bytes, int* dev_err, void* const* stage_events, void* stream);
+
+/* Backward stage events: with a non-NULL `stage_events` (ETHOS_BWD_STAGE_COUNT
+ * cudaEvent_t, entries may be NULL) the backward records
+ *   ETHOS_BWD_STAGE_EXPERTS  once d_latents and d_w1 are final (their
+ *                            all-reduce can start while the router and
+ *                            BatchNorm gradients are still being computed),
+ *   ETHOS_BWD_STAGE_END      after the last gradient kernel. */
+#define ETHOS_BWD_STAGE_EXPERTS 0
+#define ETHOS_BWD_STAGE_END 1
+#define ETHOS_BWD_STAGE_COUNT 2
 
 /* Plain bf16 GEMM D[M, N] = A[M, K] B[N, K]^T * scale on the tcgen05 path
  * (fp32 accumulate), used by the layer and exposed for tests.  out_dtype 0 =

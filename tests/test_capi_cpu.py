@@ -100,7 +100,7 @@ def test_null_arguments_rejected_without_gpu(L):
                                None, None, None, None, None, None, None, None, None, None, 0, None, None, None)
     assert st == 1  # ETHOS_ERR_INVALID_ARG
     st = L.ethos_layer_backward(ctypes.byref(d), 0, 1e-5, None, 0, *([None] * 15), *([None] * 7), None, 0,
-                                None, None)
+                                None, None, None)
     assert st == 1
     assert L.ethos_backward_workspace_size(ctypes.byref(d)) > 2 * 512 * 512 * 512 * 2
 
