@@ -27,7 +27,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[ETHOS_NOALLOC_S
 
 namespace {
 
-constexpr int kAbiVersion = 2;
+constexpr int kAbiVersion = 3;
 
 // ------------------------------------------------------------ device cache --
 struct DeviceInfo {
@@ -303,7 +303,7 @@ size_t expert_table_bytes(const ethos_dims& d) {
 
 int run_experts(const ethos_dims& d, int path, const void* latents, const void* w1, const int32_t* ids,
                 const float* weights, const float* xp, __nv_bfloat16* hacc, float* dot, __half* table, int* err,
-                cudaStream_t stream, const DeviceInfo& dev, void* const* ev = nullptr) {
+                cudaStream_t stream, const DeviceInfo& dev, void* const* ev = nullptr, __half* gtab = nullptr) {
   const int T = static_cast<int>(d.tokens);
   const int R = static_cast<int>(d.num_heads * d.top_k);
   const int N = static_cast<int>(d.num_experts);
@@ -330,11 +330,20 @@ int run_experts(const ethos_dims& d, int path, const void* latents, const void* 
   CUtensorMap tm_e, tm_w1;
   if ((st = make_tmap_bf16(&tm_e, latents, N, EX_DL, 128)) != ETHOS_OK) return st;
   if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
-  EpiGeluF16 eg;
-  eg.out = table;
-  eg.ldo = EX_DH;
-  eg.M = N;
-  if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
+  if (gtab != nullptr) {  // training: G = gelu'(E W1^T) alongside, for the backward
+    EpiGeluBwdF16 eg;
+    eg.h_out = table;
+    eg.g_out = gtab;
+    eg.ldo = EX_DH;
+    eg.M = N;
+    if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
+  } else {
+    EpiGeluF16 eg;
+    eg.out = table;
+    eg.ldo = EX_DH;
+    eg.M = N;
+    if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
+  }
   mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
   // phase B: per-token gather, dot, activation, weighted sum
   int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
@@ -564,8 +573,8 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
                         const void* w1, const void* wv, int expert_path, void* y, int32_t* ids, float* weights,
                         float* save_xp, void* save_hacc, float* save_dot, float* save_qpre, float* save_bn,
-                        void* save_qs, void* workspace, size_t workspace_bytes, int* dev_err,
-                        void* const* stage_events, void* stream) {
+                        void* save_qs, void* save_htab, void* save_gtab, void* workspace, size_t workspace_bytes,
+                        int* dev_err, void* const* stage_events, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (!x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !y || !ids || !weights || !workspace || !dev_err)
@@ -574,12 +583,15 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
   if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(latents) ||
       !aligned16(w1) || !aligned16(wv) || !aligned16(y) || !aligned16(ids) || !aligned16(weights) ||
       !aligned16(workspace) || (save_xp && !aligned16(save_xp)) || (save_hacc && !aligned16(save_hacc)) ||
-      (save_qpre && !aligned16(save_qpre)) || (save_qs && !aligned16(save_qs)))
+      (save_qpre && !aligned16(save_qpre)) || (save_qs && !aligned16(save_qs)) ||
+      (save_htab && !aligned16(save_htab)) || (save_gtab && !aligned16(save_gtab)))
     return ETHOS_ERR_ALIGNMENT;
+  if ((save_htab == nullptr) != (save_gtab == nullptr)) return ETHOS_ERR_INVALID_ARG;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
   const ethos_dims& d = *dims;
   const int path = resolve_expert_path(d, expert_path);
+  const bool keep_tables = save_htab != nullptr && path == 2;
   if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training, path)) return ETHOS_ERR_WORKSPACE;
   cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
   Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
@@ -597,8 +609,9 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
   if ((st = router_core(d, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, true, xp, s, qs,
                         qpre, save_qpre != nullptr, sbn, dev_err, stream_, *dev, ev)) != ETHOS_OK)
     return st;
-  if ((st = run_experts(d, path, latents, w1, ids, weights, xp, hacc, save_dot, s.table, dev_err, stream_, *dev,
-                        ev)) != ETHOS_OK)
+  if ((st = run_experts(d, path, latents, w1, ids, weights, xp, hacc, save_dot,
+                        keep_tables ? static_cast<__half*>(save_htab) : s.table, dev_err, stream_, *dev, ev,
+                        keep_tables ? static_cast<__half*>(save_gtab) : nullptr)) != ETHOS_OK)
     return st;
   mark(ev, ETHOS_STAGE_EXPERTS, stream_);
 
@@ -802,9 +815,10 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          const void* x, const void* w_cat, const float* bn, const void* key_cat, const void* latents,
                          const void* w1, const void* wv, const int32_t* ids, const float* weights,
                          const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
-                         const float* save_bn, const void* save_qs, float* dx, float* d_latents, float* d_w1,
-                         float* d_w2, float* d_wq, float* d_bn, float* d_keys, void* workspace,
-                         size_t workspace_bytes, int* dev_err, void* const* stage_events, void* stream) {
+                         const float* save_bn, const void* save_qs, const void* htab, const void* gtab,
+                         float* dx, float* d_latents, float* d_w1, float* d_w2, float* d_wq, float* d_bn,
+                         float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
+                         void* const* stage_events, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (d_latents == nullptr && (dims->num_heads * dims->top_k) < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
@@ -813,6 +827,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
       !d_keys || !workspace || !dev_err)
     return ETHOS_ERR_INVALID_ARG;
   if (bn_training && !save_bn) return ETHOS_ERR_INVALID_ARG;
+  if ((htab == nullptr) != (gtab == nullptr)) return ETHOS_ERR_INVALID_ARG;
   if (dims->num_heads * dims->top_k < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
@@ -866,8 +881,11 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                    auto_ksplit(D, EX_DH, T, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
       return st;
   }
-  // (3) per-expert tables H = gelu(E W1^T), G = gelu'(E W1^T)  (fp16)
-  {
+  // (3) per-expert tables H = gelu(E W1^T), G = gelu'(E W1^T)  (fp16), unless
+  // the forward kept them
+  const __half* htab_ = htab ? static_cast<const __half*>(htab) : s.htab;
+  const __half* gtab_ = gtab ? static_cast<const __half*>(gtab) : s.gtab;
+  if (htab == nullptr) {
     EpiGeluBwdF16 e;
     e.h_out = s.htab;
     e.g_out = s.gtab;
@@ -886,12 +904,12 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
       if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather<BGATHER_STAGES>), bytes)) != ETHOS_OK)
         return st;
       k_expert_bwd_gather<BGATHER_STAGES><<<blocks, BGATHER_THREADS, bytes, sm>>>(
-          s.htab, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N,
+          htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N,
           dev_err);
     } else {
       constexpr int bytes = bgather_smem_bytes(2);
       if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather<2>), bytes)) != ETHOS_OK) return st;
-      k_expert_bwd_gather<2><<<blocks, BGATHER_THREADS, bytes, sm>>>(s.htab, ids, weights, save_dot, s.dhacc, s.dw,
+      k_expert_bwd_gather<2><<<blocks, BGATHER_THREADS, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw,
                                                                      s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx,
                                                                      T, R, N, dev_err);
     }
@@ -910,7 +928,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
-  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.gx, s.gtab, s.dP, N, R);
+  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.gx, gtab_, s.dP, N, R);
   if ((st = launch_status()) != ETHOS_OK) return st;
   // (7) dE = dP W1       (W1 read in place, MN-major)
   {
@@ -1003,16 +1021,16 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
         ETHOS_OK)
       return st;
   }
-  // (14) dW_u = x^T dxp -> d_w2[:d]   [d, dh]
+  // (14) dW_u = x^T dxp -> d_w2[:d]   [d, dh]: 8 output tiles, so split K
+  // (the tokens) over the GPU and reduce into the zeroed d_w2 with atomics
   {
-    EpiStoreF32 e;
+    EpiAtomicF32 e;
     e.out = d_w2;
     e.ldo = EX_DH;
     e.M = D;
     e.scale = 1.0f;
-    e.accumulate = 0;
-    if ((st = gemm(GemmOperand{x, D, true}, GemmOperand{s.du + HQ, LDU, true}, D, EX_DH, T, 1, e, dev_err, sm,
-                   *dev)) != ETHOS_OK)
+    if ((st = gemm(GemmOperand{x, D, true}, GemmOperand{s.du + HQ, LDU, true}, D, EX_DH, T,
+                   auto_ksplit(D, EX_DH, T, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
       return st;
   }
   mark(stage_events, ETHOS_BWD_STAGE_END, sm);

@@ -200,6 +200,18 @@ def router_forward(x2d, pw, bn_training, eps, momentum, save_qpre=None, save_bn=
 STAGES = ("start", "projection", "batchnorm", "topk", "expert_table", "experts", "end")
 
 
+def resolve_expert_path(tokens, dims, path=EXPERT_AUTO):
+    """The expert path the library runs (its resolve rule, include/ethos_b200.h):
+    the table once the step makes at least one selection per expert and
+    H * k >= 16, otherwise the fused per-token kernel."""
+    R = dims["num_heads"] * dims["top_k"]
+    if path == EXPERT_FUSED:
+        return EXPERT_FUSED
+    if path == EXPERT_TABLE:
+        return EXPERT_TABLE if R >= 16 else EXPERT_FUSED
+    return EXPERT_TABLE if (tokens * R >= dims["num_experts"] and R >= 16) else EXPERT_FUSED
+
+
 def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_AUTO, stage_events=None):
     """Router + experts.  Returns a dict with ``y`` (bf16 [T, d]), ``ids``,
     ``weights`` and, when ``save``, the tensors the backward pass needs.
@@ -229,6 +241,10 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
         out["qs"] = torch.empty((2, H, T, d["d_query"]), dtype=torch.bfloat16, device=dev)
         if bn_training:
             out["bn_stats"] = torch.empty((2, HQ), dtype=torch.float32, device=dev)
+        if resolve_expert_path(T, d, path) == EXPERT_TABLE:
+            # the expert table and its GELU derivative, kept for the backward
+            out["htab"] = torch.empty((d["num_experts"], dh), dtype=torch.float16, device=dev)
+            out["gtab"] = torch.empty((d["num_experts"], dh), dtype=torch.float16, device=dev)
     g = out.get
     err = device_error_word(dev)
     check(L.ethos_layer_forward(ctypes.byref(dims), _vp(x2d), _vp(pw.w_cat), _vp(pw.bn), float(eps),
@@ -236,8 +252,8 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
                                 _vp(pw.w1), _vp(pw.wv), int(path), _vp(out["y"]), _vp(out["ids"]),
                                 _vp(out["weights"]),
                                 _vp(g("xp")), _vp(g("hacc")), _vp(g("dot")), _vp(g("qpre")),
-                                _vp(g("bn_stats")), _vp(g("qs")), _vp(ws), ws_bytes, _vp(err), _events(stage_events),
-                                _stream(dev)),
+                                _vp(g("bn_stats")), _vp(g("qs")), _vp(g("htab")), _vp(g("gtab")), _vp(ws), ws_bytes,
+                                _vp(err), _events(stage_events), _stream(dev)),
           "ethos_layer_forward")
     return out
 
@@ -298,7 +314,8 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
                                  1 if dy.dtype == torch.float32 else 0, _vp(x16), _vp(pw.w_cat), _vp(pw.bn),
                                  _vp(pw.key_cat), _vp(pw.latents), _vp(pw.w1), _vp(pw.wv), _vp(saved["ids"]),
                                  _vp(saved["weights"]), _vp(saved["xp"]), _vp(saved["hacc"]), _vp(saved["dot"]),
-                                 _vp(saved["qpre"]), _vp(saved.get("bn_stats")), _vp(saved["qs"]), _vp(g["dx"]),
+                                 _vp(saved["qpre"]), _vp(saved.get("bn_stats")), _vp(saved["qs"]),
+                                 _vp(saved.get("htab")), _vp(saved.get("gtab")), _vp(g["dx"]),
                                  _vp(g["d_latents"]), _vp(g["d_w1"]), _vp(g["d_w2"]), _vp(g["d_wq"]),
                                  _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws), ws_bytes, _vp(err),
                                  _events(stage_events), _stream(dev)),

@@ -135,14 +135,19 @@ size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path);
  *            save_qpre fp32 [T, H*dq] (pre-BatchNorm queries, x Wq^T + b),
  *            save_bn fp32 [2, H*dq] (batch mean, 1/sqrt(var+eps); training only),
  *            save_qs bf16 [2, H, T, dq] (normalised queries per half and head,
- *            split hi | lo)
+ *            split hi | lo),
+ *            save_htab, save_gtab fp16 [N, dh] (both or neither; used only
+ *            when the table path runs): the expert table H = gelu(E W1^T) is
+ *            built there instead of in the workspace, together with
+ *            G = gelu'(E W1^T), so that the backward need not rebuild them
  */
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
                         const void* w1, const void* wv, int expert_path, void* y, int32_t* ids,
                         float* weights, float* save_xp, void* save_hacc, float* save_dot,
-                        float* save_qpre, float* save_bn, void* save_qs, void* workspace,
-                        size_t workspace_bytes, int* dev_err, void* const* stage_events, void* stream);
+                        float* save_qpre, float* save_bn, void* save_qs, void* save_htab, void* save_gtab,
+                        void* workspace, size_t workspace_bytes, int* dev_err, void* const* stage_events,
+                        void* stream);
 
 /* Router alone: ProductKeyRouter.forward (model.py:208-254) on x [T, d]
  * (bf16).  Arguments as for ethos_layer_forward; w_cat needs only its first
@@ -215,6 +220,8 @@ size_t ethos_backward_workspace_size(const ethos_dims* dims);
  *  x, w_cat, bn, key_cat, latents, w1, wv, ids, weights: as passed to /
  *             returned by the forward call; bn_training as in the forward
  *  save_*     the forward's save buffers (all required; save_bn in training)
+ *  htab, gtab the forward's save_htab / save_gtab when it filled them (table
+ *             path), else NULL: the backward then builds both itself
  * Outputs (fp32, overwritten):
  *  dx        [T, d]
  *  d_latents [N, dl]        expert_latents.weight
@@ -227,9 +234,10 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          const void* x, const void* w_cat, const float* bn, const void* key_cat, const void* latents,
                          const void* w1, const void* wv, const int32_t* ids, const float* weights,
                          const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
-                         const float* save_bn, const void* save_qs, float* dx, float* d_latents, float* d_w1,
-                         float* d_w2, float* d_wq, float* d_bn, float* d_keys, void* workspace,
-                         size_t workspace_bytes, int* dev_err, void* const* stage_events, void* stream);
+                         const float* save_bn, const void* save_qs, const void* htab, const void* gtab,
+                         float* dx, float* d_latents, float* d_w1, float* d_w2, float* d_wq, float* d_bn,
+                         float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
+                         void* const* stage_events, void* stream);
 
 /* Backward stage events: with a non-NULL `stage_events` (ETHOS_BWD_STAGE_COUNT
  * cudaEvent_t, entries may be NULL) the backward records

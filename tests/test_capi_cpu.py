@@ -96,10 +96,10 @@ def test_workspace_size(L):
 
 def test_null_arguments_rejected_without_gpu(L):
     d = _dims()
-    st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None, 0,
+    st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None, 0, None, None,
                                None, None, None, None, None, None, None, None, None, None, 0, None, None, None)
     assert st == 1  # ETHOS_ERR_INVALID_ARG
-    st = L.ethos_layer_backward(ctypes.byref(d), 0, 1e-5, None, 0, *([None] * 15), *([None] * 7), None, 0,
+    st = L.ethos_layer_backward(ctypes.byref(d), 0, 1e-5, None, 0, *([None] * 17), *([None] * 7), None, 0,
                                 None, None, None)
     assert st == 1
     assert L.ethos_backward_workspace_size(ctypes.byref(d)) > 2 * 512 * 512 * 512 * 2
@@ -111,3 +111,22 @@ def test_no_cpu_fallback():
     from ethos_b200 import ops
     with pytest.raises(RuntimeError, match="no CPU path"):
         ops.gemm_bf16(torch.zeros(128, 64, dtype=torch.bfloat16), torch.zeros(256, 64, dtype=torch.bfloat16))
+
+
+def test_python_path_rule_matches_library(L):
+    """ops.resolve_expert_path (which decides whether the forward keeps the
+    expert tables for the backward) agrees with the library's own choice, as
+    seen in the workspace it asks for (the table path needs N x dh fp16)."""
+    from ethos_b200 import ops
+    base = dict(d_model=1024, num_experts=512 * 512, num_sub_keys=512, d_query=512, d_latent=128, d_hidden=512)
+    for H, k in ((8, 16), (1, 4), (2, 8), (4, 4)):
+        for T in (1, 64, 2047, 2048, 16384, 65536):
+            for path in (ops.EXPERT_AUTO, ops.EXPERT_FUSED, ops.EXPERT_TABLE):
+                d = _dims(tokens=T, num_heads=H, top_k=k)
+                if L.ethos_check_dims(ctypes.byref(d)) != 0:
+                    continue
+                ws = L.ethos_forward_workspace_size(ctypes.byref(d), 0, path)
+                ws_fused = L.ethos_forward_workspace_size(ctypes.byref(d), 0, ops.EXPERT_FUSED)
+                lib_table = ws >= ws_fused + d.num_experts * d.d_hidden * 2
+                py = ops.resolve_expert_path(T, dict(base, num_heads=H, top_k=k), path)
+                assert (py == ops.EXPERT_TABLE) == lib_table, (H, k, T, path)
