@@ -1,5 +1,5 @@
-"""Fused AdamW for the expert layer's parameters (SURVEY row f2 of the hot
-path: the optimizer step the reference runs through DeepSpeed, train.py:68-104).
+"""Fused AdamW for the expert layer's parameters: the optimizer step the
+reference runs through DeepSpeed (train.py:68-104).
 
 ``FusedAdamW`` follows ``torch.optim.AdamW`` exactly (decoupled weight decay,
 bias-corrected moments, the same per-element order of operations) and updates

@@ -88,7 +88,7 @@ def max_rel(a, b):
 
 def margin_mask(x, p, top_k, training=False, margin=1e-3):
     """Which (t, h, j) positions are decided by more than `margin` in the fp32
-    oracle (SURVEY parity rule for ids)."""
+    oracle (the id parity rule: positions decided by a margin above 1e-3)."""
     qn, _ = orc.router_queries(x, p, training)
     v = orc.grid_top_scores(qn, p.K1, p.K2, top_k + 1)
     return orc.id_match_mask(v, top_k, margin)
