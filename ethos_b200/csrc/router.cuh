@@ -5,6 +5,8 @@
 // Reference: ProductKeyRouter.forward, model.py:208-254.
 #pragma once
 
+#include <cfloat>
+
 #include "gemm.cuh"
 
 namespace ethos {
@@ -604,41 +606,62 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
             if (!__any_sync(0xffffffffu, over)) {
               tc_fence_before();
               mbar_arrive(&ctl->acc_empty[buf]);  // scores no longer needed
-              float v[16], w[16];
-              int ix[16], iw[16];
+              // Sort keys, not (score, id) pairs: each candidate's slot number
+              // rides in the 5 low mantissa bits of its score, so a min/max
+              // network (2 instructions per exchange instead of 5) orders them,
+              // and the exact score and id are fetched back by slot.  A key
+              // differs from its score by < 32 ulps, which can only reorder
+              // candidates that close; unused slots get finite -FLT_MAX keys
+              // carrying their own slot (>= n), never NaN.
+              static_assert(CAND_CAP <= 32, "slot numbers use 5 key bits");
+              float key[16];
 #pragma unroll
               for (int s2 = 0; s2 < 16; ++s2) {
-                const float2 e = cand[32 * s2];
-                v[s2] = s2 < n ? e.x : -INFINITY;
-                ix[s2] = s2 < n ? __float_as_int(e.y) : 0;
+                const float sc = s2 < n ? cand[32 * s2].x : -FLT_MAX;
+                key[s2] = __uint_as_float((__float_as_uint(sc) & ~31u) | static_cast<uint32_t>(s2));
               }
-#pragma unroll
-              for (int s2 = 0; s2 < 16; ++s2) {
-                w[s2] = -INFINITY;
-                iw[s2] = 0;
-              }
-#pragma unroll
-              for (int s2 = 0; s2 < CAND_CAP - 16; ++s2) {
-                const float2 e = cand[32 * (16 + s2)];
-                w[s2] = 16 + s2 < n ? e.x : -INFINITY;
-                iw[s2] = 16 + s2 < n ? __float_as_int(e.y) : 0;
-              }
-              bitonic_sort_desc_kv<16>(v, ix);
+              bitonic_sort_desc<16>(key);
               if (__any_sync(0xffffffffu, n > 16)) {  // slots 16..19 in use somewhere in the warp
-                float w4[4];
-                int i4[4];
+                float k4[16];
 #pragma unroll
-                for (int s2 = 0; s2 < 4; ++s2) {
-                  w4[s2] = w[s2];
-                  i4[s2] = iw[s2];
-                }
-                bitonic_sort_desc_kv<4>(w4, i4);
+                for (int s2 = 0; s2 < 16; ++s2) k4[s2] = -FLT_MAX;
 #pragma unroll
-                for (int s2 = 0; s2 < 4; ++s2) {
-                  w[s2] = w4[s2];
-                  iw[s2] = i4[s2];
+                for (int s2 = 0; s2 < CAND_CAP - 16; ++s2) {
+                  const float sc = 16 + s2 < n ? cand[32 * (16 + s2)].x : -FLT_MAX;
+                  k4[s2] = __uint_as_float((__float_as_uint(sc) & ~31u) | static_cast<uint32_t>(16 + s2));
                 }
-                top_merge_kv<16>(v, ix, w, iw);
+                {
+                  float t4[4];
+#pragma unroll
+                  for (int s2 = 0; s2 < 4; ++s2) t4[s2] = k4[s2];
+                  bitonic_sort_desc<4>(t4);
+#pragma unroll
+                  for (int s2 = 0; s2 < 4; ++s2) k4[s2] = t4[s2];
+                }
+                // top 16 of the two sorted key lists (max(a_i, b_15-i) is
+                // bitonic), then the half-cleaner merge
+#pragma unroll
+                for (int i = 0; i < 16; ++i) key[i] = fmaxf(key[i], k4[15 - i]);
+#pragma unroll
+                for (int j = 8; j > 0; j >>= 1) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                    if ((i & j) == 0) {
+                      const float x = key[i], y = key[i | j];
+                      key[i] = fmaxf(x, y);
+                      key[i | j] = fminf(x, y);
+                    }
+                  }
+                }
+              }
+              float v[16];
+              int ix[16];
+#pragma unroll
+              for (int j = 0; j < TOPK; ++j) {
+                const int slot = static_cast<int>(__float_as_uint(key[j]) & 31u);
+                const float2 e = cand[32 * slot];
+                v[j] = slot < n ? e.x : -INFINITY;
+                ix[j] = slot < n ? __float_as_int(e.y) : 0;
               }
               // fold the unit's sorted top TOPK into the half's running list
               // (the first unit of a half starts it)
