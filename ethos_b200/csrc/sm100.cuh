@@ -338,28 +338,12 @@ constexpr float C0 = 9.999964237e-01f, C1 = -4.738096237e+00f, C2 = 1.758333588e
                 C8 = 5.776085815e+02f, C9 = -3.432381897e+02f, C10 = 1.208973465e+02f, C11 = -1.902811050e+01f;
 }  // namespace gelu_detail
 
-// Phi(x) and e = exp(-x^2 / 2)
-__device__ __forceinline__ float gelu_phi(float x, float& e) {
-  using namespace gelu_detail;
-  const float s = fminf(fabsf(x) * kS, 1.0f);
-  float p = C11;
-  p = fmaf(p, s, C10);
-  p = fmaf(p, s, C9);
-  p = fmaf(p, s, C8);
-  p = fmaf(p, s, C7);
-  p = fmaf(p, s, C6);
-  p = fmaf(p, s, C5);
-  p = fmaf(p, s, C4);
-  p = fmaf(p, s, C3);
-  p = fmaf(p, s, C2);
-  p = fmaf(p, s, C1);
-  p = fmaf(p, s, C0);
-  e = ex2_approx(x * x * kE);
-  const float h = 0.5f * e * p;
-  return x >= 0.0f ? 1.0f - h : h;
-}
-// The same for two values, the polynomial on packed pairs.
-__device__ __forceinline__ void gelu_phi2(float x0, float x1, float& phi0, float& phi1, float& e0, float& e1) {
+// h = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt 2) -- the tail mass 1 - Phi(|x|) --
+// for two values, the polynomial on packed pairs; the 0.5 rides in the ex2
+// argument (log2 0.5 = -1) and the half-exponential e = 0.5 exp(-x^2 / 2) is
+// returned too.  Then Phi(x) = x >= 0 ? 1 - h : h and
+// GELU(x) = x Phi(x) = max(x, 0) - |x| h for either sign.
+__device__ __forceinline__ void gelu_tail2(float x0, float x1, float& h0, float& h1, float& e0, float& e1) {
   using namespace gelu_detail;
   const unsigned long long s = pk2(fminf(fabsf(x0) * kS, 1.0f), fminf(fabsf(x1) * kS, 1.0f));
   unsigned long long p = pk2(C11, C11);
@@ -376,35 +360,56 @@ __device__ __forceinline__ void gelu_phi2(float x0, float x1, float& phi0, float
   p = ffma2(p, s, pk2(C0, C0));
   float p0, p1;
   upk2(p, p0, p1);
-  e0 = ex2_approx(x0 * x0 * kE);
-  e1 = ex2_approx(x1 * x1 * kE);
-  const float h0 = 0.5f * e0 * p0, h1 = 0.5f * e1 * p1;
-  phi0 = x0 >= 0.0f ? 1.0f - h0 : h0;
-  phi1 = x1 >= 0.0f ? 1.0f - h1 : h1;
+  e0 = ex2_approx(fmaf(x0 * kE, x0, -1.0f));  // 0.5 exp(-x^2 / 2)
+  e1 = ex2_approx(fmaf(x1 * kE, x1, -1.0f));
+  h0 = e0 * p0;
+  h1 = e1 * p1;
+}
+__device__ __forceinline__ float gelu_tail(float x, float& e) {
+  using namespace gelu_detail;
+  const float s = fminf(fabsf(x) * kS, 1.0f);
+  float p = C11;
+  p = fmaf(p, s, C10);
+  p = fmaf(p, s, C9);
+  p = fmaf(p, s, C8);
+  p = fmaf(p, s, C7);
+  p = fmaf(p, s, C6);
+  p = fmaf(p, s, C5);
+  p = fmaf(p, s, C4);
+  p = fmaf(p, s, C3);
+  p = fmaf(p, s, C2);
+  p = fmaf(p, s, C1);
+  p = fmaf(p, s, C0);
+  e = ex2_approx(fmaf(x * kE, x, -1.0f));  // 0.5 exp(-x^2 / 2)
+  return e * p;
 }
 __device__ __forceinline__ float gelu_erf(float x) {
   float e;
-  return x * gelu_phi(x, e);
+  return fmaf(-fabsf(x), gelu_tail(x, e), fmaxf(x, 0.0f));
 }
+// d GELU / dx = Phi(x) + x phi(x), phi(x) = exp(-x^2/2) / sqrt(2 pi) =
+// 2 e / sqrt(2 pi) with e the half-exponential of the tail
 __device__ __forceinline__ float gelu_erf_grad(float x) {
   float e;
-  const float phi = gelu_phi(x, e);
-  return fmaf(x * gelu_detail::kPdf, e, phi);
+  const float h = gelu_tail(x, e);
+  const float phi = x >= 0.0f ? 1.0f - h : h;
+  return fmaf(x * (2.0f * gelu_detail::kPdf), e, phi);
 }
 __device__ __forceinline__ void gelu_erf2(float x0, float x1, float& g0, float& g1) {
-  float p0, p1, e0, e1;
-  gelu_phi2(x0, x1, p0, p1, e0, e1);
-  g0 = x0 * p0;
-  g1 = x1 * p1;
+  float h0, h1, e0, e1;
+  gelu_tail2(x0, x1, h0, h1, e0, e1);
+  g0 = fmaf(-fabsf(x0), h0, fmaxf(x0, 0.0f));
+  g1 = fmaf(-fabsf(x1), h1, fmaxf(x1, 0.0f));
 }
 // GELU and its derivative of two values from one evaluation
 __device__ __forceinline__ void gelu_erf_and_grad2(float x0, float x1, float& g0, float& g1, float& d0, float& d1) {
-  float p0, p1, e0, e1;
-  gelu_phi2(x0, x1, p0, p1, e0, e1);
-  g0 = x0 * p0;
-  g1 = x1 * p1;
-  d0 = fmaf(x0 * gelu_detail::kPdf, e0, p0);
-  d1 = fmaf(x1 * gelu_detail::kPdf, e1, p1);
+  float h0, h1, e0, e1;
+  gelu_tail2(x0, x1, h0, h1, e0, e1);
+  g0 = fmaf(-fabsf(x0), h0, fmaxf(x0, 0.0f));
+  g1 = fmaf(-fabsf(x1), h1, fmaxf(x1, 0.0f));
+  const float p0 = x0 >= 0.0f ? 1.0f - h0 : h0, p1 = x1 >= 0.0f ? 1.0f - h1 : h1;
+  d0 = fmaf(x0 * (2.0f * gelu_detail::kPdf), e0, p0);
+  d1 = fmaf(x1 * (2.0f * gelu_detail::kPdf), e1, p1);
 }
 
 // Warp transpose-reduce: on entry lane l holds v[0..31] (32 columns of one

@@ -48,6 +48,9 @@ def test_gelu_error_bounds():
     gelu = xs * phi
     gelu_ref = 0.5 * xs * (1 + scipy_special.erf(xs / np.sqrt(2)))
     assert np.abs(gelu - gelu_ref).max() <= 1.5e-6
+    # the form the kernels assemble: max(x, 0) - |x| h with h = 1 - Phi(|x|)
+    h = np.where(xs >= 0, 1 - phi, phi)
+    assert np.abs(np.maximum(xs, 0) - np.abs(xs) * h - gelu_ref).max() <= 1.5e-6
     # derivative Phi + x phi, as the backward tables compute it
     d = phi + xs * np.exp(-0.5 * xs ** 2) / np.sqrt(2 * np.pi)
     d_ref = ref + xs * np.exp(-0.5 * xs ** 2) / np.sqrt(2 * np.pi)
