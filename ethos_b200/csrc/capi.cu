@@ -106,17 +106,23 @@ EncodeTiledFn encode_fn() {
 // Row-major bf16 matrix [rows, cols] (row pitch ld >= cols elements) read in
 // boxes of 64 columns x box_rows rows with the 128-byte swizzle that the UMMA
 // descriptors expect.
-int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows, int64_t ld = 0) {
+// box_cols 64 (128-byte rows, 128-byte swizzle) or 32 (64-byte rows, 64-byte
+// swizzle); the UMMA descriptor of the consuming kernel must use the same one.
+int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows, int64_t ld = 0,
+                   int box_cols = 64) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return ETHOS_ERR_TENSOR_MAP;
   if (ld == 0) ld = cols;
   if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || (ld * 2) % 16 != 0) return ETHOS_ERR_ALIGNMENT;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  if (box_cols != 64 && box_cols != 32) return ETHOS_ERR_TENSOR_MAP;
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ETHOS_OK : ETHOS_ERR_TENSOR_MAP;
 }
@@ -393,9 +399,10 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   int st;
   if ((st = make_tmap_bf16(&tm_x, x, T, d.d_model, 128)) != ETHOS_OK) return st;
   if ((st = make_tmap_bf16(&tm_w, w_cat, ncat, d.d_model, 256)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tm_q, qs, static_cast<int64_t>(d.num_heads) * 2 * T, dq, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_q, qs, static_cast<int64_t>(d.num_heads) * 2 * T, dq, 128, 0, ROUTER_KB)) != ETHOS_OK)
+    return st;
   const int box_keys = d.num_sub_keys < 256 ? static_cast<int>(d.num_sub_keys) : 256;
-  if ((st = make_tmap_bf16(&tm_k, key_cat, 2 * d.num_sub_keys, dq, box_keys)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_k, key_cat, 2 * d.num_sub_keys, dq, box_keys, 0, ROUTER_KB)) != ETHOS_OK) return st;
 
   const int cb = 256;
   if (!bn_training) {
@@ -686,9 +693,9 @@ int ethos_product_key_topk(const ethos_dims* dims, const void* q, const void* ke
   const int T = static_cast<int>(d.tokens);
   const int half = static_cast<int>(d.d_query / 2);
   CUtensorMap tm_q, tm_k;
-  if ((st = make_tmap_bf16(&tm_q, q, d.num_heads * T, d.d_query, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_q, q, d.num_heads * T, d.d_query, 128, 0, ROUTER_KB)) != ETHOS_OK) return st;
   const int box_keys = d.num_sub_keys < 256 ? static_cast<int>(d.num_sub_keys) : 256;
-  if ((st = make_tmap_bf16(&tm_k, keys, 2 * d.num_sub_keys, half, box_keys)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_k, keys, 2 * d.num_sub_keys, half, box_keys, 0, ROUTER_KB)) != ETHOS_OK) return st;
   RouterGeom g;
   g.T = T;
   g.H = static_cast<int>(d.num_heads);

@@ -272,34 +272,43 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 // ------------------------------------------------------ scoring + top-k --
 // One work item = (head h, tile of 128 tokens); per item two halves p, per
-// half the sub-keys in units of up to 256 (TMEM buffer = unit parity).
+// half the sub-keys in units of up to 256 (TMEM buffer = unit parity, so the
+// two units of a 512-key half fill all 512 columns).
 // The MMA warp computes S[t, key] = sum_c A[t, c] * B[key, c] into the
-// unit's 256-column TMEM buffer; 8 epilogue warps (one token row per thread,
-// group kh = 0/1 owning the first/second 256 keys of a half) select the
-// half's top-k per row exactly:
-//   1. maxima of the 8-key groups of the row (three-input FMNMX);
-//   2. tau = k-th largest of the half's 64 maxima (sorted top 16 per group,
-//      exchanged): a lower bound on the k-th largest score, since the maxima
-//      are distinct scores of the row;
-//   3. the scores >= tau (about 9 per 256 keys) are compacted into per-lane
-//      shared-memory slots by predicated stores and sorted by a bitonic
-//      network with their key ids.  A warp where some row has more than
-//      CAND_CAP candidates (ties, or scores far from i.i.d.) folds that unit
-//      from TMEM with the exact insertion path instead.
-// The non-owner group hands its sorted list to the owner group (alternating
-// per item), which merges the two by a network and, after both halves, takes
-// the top k of the candidate grid by merge networks, the fp32 softmax and the
-// ids.  A rows come from the query tensor map at h*a_stride_h + p*a_stride_p
-// + t, column offset p*a_col_p; B rows from the key tensor map at p*K + key.
+// unit's 256-column TMEM buffer; 8 epilogue warps (one token row per thread)
+// in two groups, group g taking columns [128 g, 128 g + 128) of every unit,
+// select the half's top-k per row exactly:
+//   1. maxima of the 8-key groups (three-input max), top 16 per group;
+//   2. tau = k-th largest of the half's 64 maxima (the groups' sorted lists
+//      exchanged through shared memory): a lower bound on the half's k-th
+//      largest score, since the maxima are distinct scores of the row;
+//   3. the scores >= tau (about 9 per group and half) are compacted into
+//      per-lane shared-memory slots by predicated stores, the TMEM buffers
+//      are released and the slots sorted by a network on packed keys.  A
+//      warp where some row has more than CAND_CAP candidates (ties, or
+//      scores far from i.i.d.) folds the half from TMEM by exact insertion.
+// The two groups swap their sorted lists and both merge them; after both
+// halves the top k of the candidate grid is taken by merge networks split
+// between the groups, then the fp32 softmax and the ids.  A rows come from
+// the query tensor map at h*a_stride_h + p*a_stride_p + t, column offset
+// p*a_col_p; B rows from the key tensor map at p*K + key.
 // With the split-bf16 layout A = [hi | lo] and each key box multiplies both
 // halves, so S is the fp32 query . key product to ~2^-16.
 constexpr int ROUTER_THREADS = 320;
-// A stage holds 64 K-columns of A (hi and, with the split layout, the matching
-// lo columns) and of the keys; with the split layout one key box serves both
-// the hi and the lo MMAs, so the keys cross L2 -> shared memory once.
-constexpr int ROUTER_STAGES = 2;
-constexpr int ROUTER_A_BYTES = 128 * 64 * 2;
-constexpr int ROUTER_B_BYTES_MAX = 256 * 64 * 2;
+// A stage holds ROUTER_KB K-columns of A (hi and, with the split layout, the
+// matching lo columns) and of the keys; with the split layout one key box
+// serves both the hi and the lo MMAs, so the keys cross L2 -> shared memory
+// once.  The feed is bound by copy latency, not bandwidth, so the same 128 KB
+// of ring is cut into more, narrower stages: 32 columns (64-byte rows, the
+// 64-byte swizzle) x 4 stages keep 96 KB in flight where 64 x 2 kept 64 KB.
+#ifndef ETHOS_ROUTER_KB
+#define ETHOS_ROUTER_KB 32
+#endif
+constexpr int ROUTER_KB = ETHOS_ROUTER_KB;
+static_assert(ROUTER_KB == 32 || ROUTER_KB == 64, "stage width is one 64- or 128-byte swizzle row");
+constexpr int ROUTER_STAGES = 128 / ROUTER_KB;
+constexpr int ROUTER_A_BYTES = 128 * ROUTER_KB * 2;
+constexpr int ROUTER_B_BYTES_MAX = 256 * ROUTER_KB * 2;
 constexpr int ROUTER_STAGE_BYTES = 2 * ROUTER_A_BYTES + ROUTER_B_BYTES_MAX;
 // candidate slots per lane: CAND_CAP plus 4 of headroom (the count saturates
 // once per 4 scores), (score, id) pairs laid out [slot][lane]; the fallback
@@ -311,6 +320,10 @@ static_assert(ROUTER_CAND_WARP_BYTES >= 32 * 32 * 4, "fallback staging must fit 
 constexpr int ROUTER_CAND_BYTES = 8 * ROUTER_CAND_WARP_BYTES;
 constexpr int ROUTER_XMAX_BYTES = 2 * 16 * 128 * 4;     // [group][16 maxima][128 rows]
 constexpr int ROUTER_XLIST_BYTES = 2 * 16 * 128 * 4;    // [value|id][16][128 rows]
+
+__device__ __forceinline__ uint64_t router_desc(uint32_t smem_addr) {
+  return ROUTER_KB == 64 ? umma_desc_sw128(smem_addr) : umma_desc_sw64(smem_addr);
+}
 
 struct RouterCtl {
   uint64_t full[ROUTER_STAGES];
@@ -355,8 +368,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
   const int num_items = g.H * num_mt;
   const int box_rows = g.K < 256 ? g.K : 256;   // keys per unit (TMA box rows, MMA N)
   const int num_chunks = (g.K + 255) / 256;     // units per half (1 or 2)
-  const int num_kb = (g.split ? g.KA / 2 : g.KA) / 64;  // stages per unit
-  const uint32_t stage_tx = (g.split ? 2 : 1) * ROUTER_A_BYTES + box_rows * 128;
+  const int num_kb = (g.split ? g.KA / 2 : g.KA) / ROUTER_KB;  // stages per unit
+  const uint32_t stage_tx = (g.split ? 2 : 1) * ROUTER_A_BYTES + box_rows * ROUTER_KB * 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ROUTER_STAGES; ++s) {
@@ -400,9 +413,10 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
               }
               uint8_t* sa = smem + rp.stage * ROUTER_STAGE_BYTES;
               mbar_arrive_expect_tx(&ctl->full[rp.stage], stage_tx);
-              tma_load_2d(sa, &tmA, &ctl->full[rp.stage], p * g.a_col_p + kb * 64, a_row);
-              if (g.split) tma_load_2d(sa + ROUTER_A_BYTES, &tmA, &ctl->full[rp.stage], g.KA / 2 + kb * 64, a_row);
-              tma_load_2d(sa + 2 * ROUTER_A_BYTES, &tmB, &ctl->full[rp.stage], kb * 64, p * g.K + nc * 256);
+              const int kc = kb * ROUTER_KB;
+              tma_load_2d(sa, &tmA, &ctl->full[rp.stage], p * g.a_col_p + kc, a_row);
+              if (g.split) tma_load_2d(sa + ROUTER_A_BYTES, &tmA, &ctl->full[rp.stage], g.KA / 2 + kc, a_row);
+              tma_load_2d(sa + 2 * ROUTER_A_BYTES, &tmB, &ctl->full[rp.stage], kc, p * g.K + nc * 256);
               rp.advance(ROUTER_STAGES);
             }
           }
@@ -436,15 +450,14 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
             const uint32_t a_base = smem_u32(smem + stage * ROUTER_STAGE_BYTES);
             const uint32_t b_base = a_base + 2 * ROUTER_A_BYTES;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              umma_bf16(d, umma_desc_sw128(a_base + k * 32), umma_desc_sw128(b_base + k * 32), idesc,
+            for (int k = 0; k < ROUTER_KB / 16; ++k) {
+              umma_bf16(d, router_desc(a_base + k * 32), router_desc(b_base + k * 32), idesc,
                         (kb | k) != 0 ? 1u : 0u);
             }
             if (g.split) {
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
-                umma_bf16(d, umma_desc_sw128(a_base + ROUTER_A_BYTES + k * 32), umma_desc_sw128(b_base + k * 32),
-                          idesc, 1u);
+              for (int k = 0; k < ROUTER_KB / 16; ++k)
+                umma_bf16(d, router_desc(a_base + ROUTER_A_BYTES + k * 32), router_desc(b_base + k * 32), idesc, 1u);
             }
             umma_commit(&ctl->empty[stage]);
             if (++stage == ROUTER_STAGES) {
@@ -498,46 +511,57 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
           lv[p][j] = -INFINITY;
           li[p][j] = 0;
         }
-        for (int nc = 0; nc < num_chunks; ++nc, ++m) {
-          const int buf = m & 1;
-          const uint32_t ph = static_cast<uint32_t>(m >> 1) & 1u;
+        // The half's units stay in TMEM until its candidates are compacted:
+        // 1. per unit, the maxima of this group's 8-key groups, sorted and
+        //    merged into the top 16 over the half's units;
+        // 2. tau = TOPK-th largest of the half's 8-key maxima (both groups,
+        //    exchanged): a lower bound on the half's TOPK-th largest score,
+        //    since the maxima are distinct scores of the row, so every score
+        //    of the half's top TOPK is >= tau (about 9 of this group's 256
+        //    scores pass);
+        // 3. the scores >= tau of all the half's units are compacted into
+        //    this lane's shared-memory slots, the buffers are released and
+        //    the slots are sorted into this group's list for the half.
+        const int m0 = m;
+        m += num_chunks;
+        float t16[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t16[i] = -INFINITY;
+        for (int nc = 0; nc < num_chunks; ++nc) {
+          const int buf = (m0 + nc) & 1;
+          const uint32_t ph = static_cast<uint32_t>((m0 + nc) >> 1) & 1u;
           if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&ctl->acc_full[buf], ph, abort, err, 14));
-          const int valid = min(256, g.K - nc * 256);               // multiple of 32
-          const int vg = min(128, max(0, valid - 128 * grp));        // this group's columns
-          const int key0 = nc * 256 + 128 * grp;
-          const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256 + 128 * grp);
           if (ok) tc_fence_after();
-          // 1. maxima of the 4-key groups of this group's columns, top 16 sorted
-          float t16[16];
-          {
-            float mx[32];
+          const int valid = min(256, g.K - nc * 256);                // multiple of 32
+          const int vg = min(128, max(0, valid - 128 * grp));        // this group's columns
+          const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256 + 128 * grp);
+          float mx[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx[i] = -INFINITY;
-            if (ok) {
+          for (int i = 0; i < 16; ++i) mx[i] = -INFINITY;
+          if (ok) {
 #pragma unroll
-              for (int c = 0; c < 2; ++c) {
-                if (c * 64 < vg) {  // a 32-column tail reads 32 spare columns
-                  float sc[64];
-                  tmem_ld64(cbase + c * 64, sc);
+            for (int c = 0; c < 2; ++c) {
+              if (c * 64 < vg) {  // a 32-column tail reads 32 spare columns
+                float sc[64];
+                tmem_ld64(cbase + c * 64, sc);
 #pragma unroll
-                  for (int g4 = 0; g4 < 16; ++g4) {
-                    const float* v = sc + 4 * g4;
-                    const float mv = fmaxf(fmax3(v[0], v[1], v[2]), v[3]);
-                    mx[16 * c + g4] = (c * 64 + 4 * g4 < vg) ? mv : -INFINITY;
-                  }
+                for (int g8 = 0; g8 < 8; ++g8) {
+                  const float* v = sc + 8 * g8;
+                  const float mv = fmax3(fmax3(v[0], v[1], v[2]), fmax3(v[3], v[4], v[5]), fmaxf(v[6], v[7]));
+                  mx[8 * c + g8] = (c * 64 + 8 * g8 < vg) ? mv : -INFINITY;
                 }
               }
             }
-            float hi[16];
+          }
+          bitonic_sort_desc<16>(mx);
+          if (nc == 0) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              t16[i] = mx[i];
-              hi[i] = mx[16 + i];
-            }
-            bitonic_sort_desc<16>(t16);
-            bitonic_sort_desc<16>(hi);
+            for (int i = 0; i < 16; ++i) t16[i] = mx[i];
+          } else {
+            // top 16 of two sorted lists: max(a_i, b_15-i) is bitonic, then
+            // the half-cleaner merge
 #pragma unroll
-            for (int i = 0; i < 16; ++i) t16[i] = fmaxf(t16[i], hi[15 - i]);
+            for (int i = 0; i < 16; ++i) t16[i] = fmaxf(t16[i], mx[15 - i]);
 #pragma unroll
             for (int j = 8; j > 0; j >>= 1) {
 #pragma unroll
@@ -550,32 +574,37 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
               }
             }
           }
-          // 2. tau = TOPK-th largest of the unit's 64 maxima: a lower bound on
-          //    the unit's TOPK-th largest score (the maxima are distinct
-          //    scores), so every score of the half's top TOPK that lies in
-          //    this unit is >= tau
-          named_bar_sync(1, 256);
+        }
+        named_bar_sync(1, 256);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) xmax[(grp * 16 + i) * 128 + row] = t16[i];
-          named_bar_sync(1, 256);
-          float tau = -INFINITY;
-          if (valid / 4 >= TOPK) {
-            tau = INFINITY;
+        for (int i = 0; i < 16; ++i) xmax[(grp * 16 + i) * 128 + row] = t16[i];
+        named_bar_sync(1, 256);
+        float tau = -INFINITY;
+        if (g.K / 8 >= TOPK) {
+          tau = INFINITY;
 #pragma unroll
-            for (int i = 0; i < TOPK; ++i)
-              tau = fminf(tau, fmaxf(t16[i], xmax[((grp ^ 1) * 16 + TOPK - 1 - i) * 128 + row]));
-          }
-          // 3. compact this group's scores >= tau; release the buffer; sort
-          if (ok) {
-            // Predicated and branch-free: a passing score is stored with its
-            // key id into the next free slot (8-byte slots, [slot][lane] rows
-            // of 256 B) and the slot address advances; rejected scores issue
-            // no shared-memory traffic.  The address saturates at CAND_CAP
-            // once per 4 scores (CAND_SLOTS covers the 4 in between); a
-            // saturated row is an overflow.
-            const uint32_t c0 = smem_u32(cand);
-            const uint32_t ccap = c0 + CAND_CAP * 256u;
-            uint32_t ca = c0;
+          for (int i = 0; i < TOPK; ++i)
+            tau = fminf(tau, fmaxf(t16[i], xmax[((grp ^ 1) * 16 + TOPK - 1 - i) * 128 + row]));
+        }
+        if (ok) {
+          // Predicated and branch-free: a passing score is stored with its
+          // key id into the next free slot (8-byte slots, [slot][lane] rows
+          // of 256 B) and the slot address advances; rejected scores issue
+          // no shared-memory traffic.  The address saturates at CAND_CAP
+          // once per 4 scores (CAND_SLOTS covers the 4 in between); a
+          // saturated row is an overflow.
+          const uint32_t c0 = smem_u32(cand);
+          const uint32_t ccap = c0 + CAND_CAP * 256u;
+          uint32_t ca = c0;
+          int fold_from = num_chunks;  // first unit that overflowed (num_chunks: none)
+#pragma unroll 1
+          for (int nc = 0; nc < num_chunks; ++nc) {
+            const int buf = (m0 + nc) & 1;
+            const int valid = min(256, g.K - nc * 256);
+            const int vg = min(128, max(0, valid - 128 * grp));
+            const int key0 = nc * 256 + 128 * grp;
+            const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256 + 128 * grp);
+            const uint32_t ca_unit = ca;
             bool over = false;
 #pragma unroll 1
             for (int c = 0; c < 2; ++c) {
@@ -602,88 +631,91 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
                 ca = ca > ccap ? ccap : ca;
               }
             }
-            const int n = static_cast<int>((ca - c0) >> 8);
-            if (!__any_sync(0xffffffffu, over)) {
-              tc_fence_before();
-              mbar_arrive(&ctl->acc_empty[buf]);  // scores no longer needed
-              // Sort keys, not (score, id) pairs: each candidate's slot number
-              // rides in the 5 low mantissa bits of its score, so a min/max
-              // network (2 instructions per exchange instead of 5) orders them,
-              // and the exact score and id are fetched back by slot.  A key
-              // differs from its score by < 32 ulps, which can only reorder
-              // candidates that close; unused slots get finite -FLT_MAX keys
-              // carrying their own slot (>= n), never NaN.
-              static_assert(CAND_CAP <= 32, "slot numbers use 5 key bits");
-              float key[16];
+            if (__any_sync(0xffffffffu, over)) {
+              ca = ca_unit;  // this unit and the later ones are folded from TMEM
+              fold_from = nc;
+              break;
+            }
+            tc_fence_before();
+            mbar_arrive(&ctl->acc_empty[buf]);  // the unit's scores are no longer needed
+          }
+          const int n = static_cast<int>((ca - c0) >> 8);
+          if (fold_from == num_chunks) {
+            // Sort keys, not (score, id) pairs: each candidate's slot number
+            // rides in the 5 low mantissa bits of its score, so a min/max
+            // network (2 instructions per exchange instead of 5) orders them,
+            // and the exact score and id are fetched back by slot.  A key
+            // differs from its score by < 32 ulps, which can only reorder
+            // candidates that close; unused slots get finite -FLT_MAX keys
+            // carrying their own slot (>= n), never NaN.
+            static_assert(CAND_CAP <= 32, "slot numbers use 5 key bits");
+            float key[16];
 #pragma unroll
-              for (int s2 = 0; s2 < 16; ++s2) {
-                const float sc = s2 < n ? cand[32 * s2].x : -FLT_MAX;
-                key[s2] = __uint_as_float((__float_as_uint(sc) & ~31u) | static_cast<uint32_t>(s2));
+            for (int s2 = 0; s2 < 16; ++s2) {
+              const float sc = s2 < n ? cand[32 * s2].x : -FLT_MAX;
+              key[s2] = __uint_as_float((__float_as_uint(sc) & ~31u) | static_cast<uint32_t>(s2));
+            }
+            bitonic_sort_desc<16>(key);
+            if (__any_sync(0xffffffffu, n > 16)) {  // slots 16..19 in use somewhere in the warp
+              float k4[16];
+#pragma unroll
+              for (int s2 = 0; s2 < 16; ++s2) k4[s2] = -FLT_MAX;
+#pragma unroll
+              for (int s2 = 0; s2 < CAND_CAP - 16; ++s2) {
+                const float sc = 16 + s2 < n ? cand[32 * (16 + s2)].x : -FLT_MAX;
+                k4[s2] = __uint_as_float((__float_as_uint(sc) & ~31u) | static_cast<uint32_t>(16 + s2));
               }
-              bitonic_sort_desc<16>(key);
-              if (__any_sync(0xffffffffu, n > 16)) {  // slots 16..19 in use somewhere in the warp
-                float k4[16];
+              {
+                float t4[4];
 #pragma unroll
-                for (int s2 = 0; s2 < 16; ++s2) k4[s2] = -FLT_MAX;
+                for (int s2 = 0; s2 < 4; ++s2) t4[s2] = k4[s2];
+                bitonic_sort_desc<4>(t4);
 #pragma unroll
-                for (int s2 = 0; s2 < CAND_CAP - 16; ++s2) {
-                  const float sc = 16 + s2 < n ? cand[32 * (16 + s2)].x : -FLT_MAX;
-                  k4[s2] = __uint_as_float((__float_as_uint(sc) & ~31u) | static_cast<uint32_t>(16 + s2));
-                }
-                {
-                  float t4[4];
+                for (int s2 = 0; s2 < 4; ++s2) k4[s2] = t4[s2];
+              }
+              // top 16 of the two sorted key lists (max(a_i, b_15-i) is
+              // bitonic), then the half-cleaner merge
 #pragma unroll
-                  for (int s2 = 0; s2 < 4; ++s2) t4[s2] = k4[s2];
-                  bitonic_sort_desc<4>(t4);
+              for (int i = 0; i < 16; ++i) key[i] = fmaxf(key[i], k4[15 - i]);
 #pragma unroll
-                  for (int s2 = 0; s2 < 4; ++s2) k4[s2] = t4[s2];
-                }
-                // top 16 of the two sorted key lists (max(a_i, b_15-i) is
-                // bitonic), then the half-cleaner merge
+              for (int j = 8; j > 0; j >>= 1) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) key[i] = fmaxf(key[i], k4[15 - i]);
-#pragma unroll
-                for (int j = 8; j > 0; j >>= 1) {
-#pragma unroll
-                  for (int i = 0; i < 16; ++i) {
-                    if ((i & j) == 0) {
-                      const float x = key[i], y = key[i | j];
-                      key[i] = fmaxf(x, y);
-                      key[i | j] = fminf(x, y);
-                    }
+                for (int i = 0; i < 16; ++i) {
+                  if ((i & j) == 0) {
+                    const float x = key[i], y = key[i | j];
+                    key[i] = fmaxf(x, y);
+                    key[i | j] = fminf(x, y);
                   }
                 }
               }
-              float v[16];
-              int ix[16];
+            }
 #pragma unroll
-              for (int j = 0; j < TOPK; ++j) {
-                const int slot = static_cast<int>(__float_as_uint(key[j]) & 31u);
-                const float2 e = cand[32 * slot];
-                v[j] = slot < n ? e.x : -INFINITY;
-                ix[j] = slot < n ? __float_as_int(e.y) : 0;
-              }
-              // fold the unit's sorted top TOPK into the half's running list
-              // (the first unit of a half starts it)
-              if (nc == 0) {
-#pragma unroll
-                for (int j = 0; j < TOPK; ++j) {
-                  lv[p][j] = v[j];
-                  li[p][j] = ix[j];
-                }
-              } else {
-                float u[TOPK];
-                int iu[TOPK];
-#pragma unroll
-                for (int j = 0; j < TOPK; ++j) {
-                  u[j] = v[j];
-                  iu[j] = ix[j];
-                }
-                top_merge_kv<TOPK>(lv[p], li[p], u, iu);
-              }
-            } else {
-              // exact insertion from TMEM for this warp (rare)
-              __syncwarp();
+            for (int j = 0; j < TOPK; ++j) {
+              const int slot = static_cast<int>(__float_as_uint(key[j]) & 31u);
+              const float2 e = cand[32 * slot];
+              lv[p][j] = slot < n ? e.x : -INFINITY;
+              li[p][j] = slot < n ? __float_as_int(e.y) : 0;
+            }
+          } else {
+            // Rare: some row of the warp has more than CAND_CAP candidates.
+            // The candidates of the units already compacted are inserted
+            // from their slots, the rest of the half is folded from TMEM by
+            // exact insertion, and those units are released.
+            __syncwarp();
+            const int nmax = __reduce_max_sync(0xffffffffu, n);
+#pragma unroll 1
+            for (int s2 = 0; s2 < nmax; ++s2) {
+              const float2 e = cand[32 * s2];
+              topk_insert<TOPK>(lv[p], li[p], s2 < n ? e.x : -INFINITY, s2 < n ? __float_as_int(e.y) : 0);
+            }
+            __syncwarp();
+#pragma unroll 1
+            for (int nc = fold_from; nc < num_chunks; ++nc) {
+              const int buf = (m0 + nc) & 1;
+              const int valid = min(256, g.K - nc * 256);
+              const int vg = min(128, max(0, valid - 128 * grp));
+              const int key0 = nc * 256 + 128 * grp;
+              const uint32_t cbase = tmem_addr(tmem, q * 32, buf * 256 + 128 * grp);
 #pragma unroll 1
               for (int c = 0; c < 4; ++c) {
                 if (c * 32 >= vg) break;
@@ -694,10 +726,13 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
               tc_fence_before();
               mbar_arrive(&ctl->acc_empty[buf]);
             }
-            __syncwarp();
           }
+          __syncwarp();
         }
-        // 4. the two groups swap their half-p lists and both merge
+        // 4. the two groups swap their half-p lists and both merge them,
+        //    both with group 0's list as the first operand: with tied scores
+        //    the merge order decides which of the tied entries lands where,
+        //    and the split grid step needs the same list in both groups
         named_bar_sync(1, 256);
 #pragma unroll
         for (int j = 0; j < TOPK; ++j) {
@@ -713,7 +748,16 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
             ov[j] = oth_v[j * 128 + row];
             oi[j] = oth_i[j * 128 + row];
           }
-          top_merge_kv<TOPK>(lv[p], li[p], ov, oi);
+          if (grp == 0) {
+            top_merge_kv<TOPK>(lv[p], li[p], ov, oi);
+          } else {
+            top_merge_kv<TOPK>(ov, oi, lv[p], li[p]);
+#pragma unroll
+            for (int j = 0; j < TOPK; ++j) {
+              lv[p][j] = ov[j];
+              li[p][j] = oi[j];
+            }
+          }
         }
       }
       // 5. top TOPK of the candidate grid; for TOPK = 16 the merge tree is

@@ -173,6 +173,20 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// The same for the 64-byte swizzle: rows of 64 B (32 bf16), 8-row groups 512 B
+// apart, 16-byte chunks XOR-permuted by (row / 2) % 4; layout = 4
+// (SWIZZLE_64B), tile base 512-B aligned, K steps inside the 64-B atom again
+// add (k_bytes >> 4) to the start field.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major.
 // Bits: [4,6) D format (1 = f32), [7,10) A format (1 = bf16), [10,13) B format
 // (1 = bf16), bit 15/16 A/B major (0 = K), [17,23) N>>3, [24,29) M>>4.

@@ -117,20 +117,25 @@ def test_product_key_topk_config3(T, K, dq, top_k):
     assert (w.cpu() - w_ref).abs().max().item() <= 2e-3
 
 
-@pytest.mark.parametrize("dup", ["adjacent", "all"])
+@pytest.mark.parametrize("dup", ["adjacent", "all", "second_unit"])
 def test_product_key_topk_tied_scores(dup):
     """Duplicated sub-keys make every score appear two (or many) times in a
     256-key unit, so rows overflow the candidate slots and take the exact
-    fallback fold.  Tied ids are interchangeable, so the check is on the
-    selected scores (recomputed from the returned ids) and on the weights."""
+    fallback fold ("second_unit": only the second 256 keys of each half are
+    duplicated, so the first unit's candidates come from the slots and the
+    second unit is folded).  Tied ids are interchangeable, so the check is on
+    the selected scores (recomputed from the returned ids) and on the
+    weights."""
     H, T, K, dq, top_k = 8, 2048, 512, 256, 16
     gen = torch.Generator().manual_seed(7)
     q = torch.randn(H, T, dq, generator=gen).to(torch.bfloat16)
     keys = (torch.randn(2, K, dq // 2, generator=gen) / (dq // 2) ** 0.5).to(torch.bfloat16)
     if dup == "adjacent":
         keys[:, 1::2] = keys[:, 0::2]          # each score twice, side by side
-    else:
+    elif dup == "all":
         keys[:, 32:] = keys[:, :32].repeat(1, (K - 32) // 32, 1)  # each score 16 times
+    else:
+        keys[:, 256:] = keys[:, 256:288].repeat(1, 8, 1)          # second unit: each score 8 times
     w, ids = ops.product_key_topk(q.cuda(), keys.cuda(), top_k)
     torch.cuda.synchronize()
     ops.check_device_error("cuda")
