@@ -503,6 +503,22 @@ def main():
         torch.cuda.synchronize()
         serial_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in sev2) / len(sev2))
 
+        # serving with frozen parameters: the expert table cached across
+        # forwards (built once, outside the timed steps), L2 flushed per step
+        layer.cache_expert_table = True
+        for _ in range(2):
+            layer(x_dev.view(1, T, -1))
+        cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
+        for s, e in cev:
+            flush.zero_()
+            s.record(stream)
+            layer(x_dev.view(1, T, -1))
+            e.record(stream)
+        torch.cuda.synchronize()
+        layer.cache_expert_table = False
+        cached_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in cev) / len(cev))
+        ops.check_device_error(dev)
+
     peaks = load_peaks()
     total_tokens = T * world
     value = total_tokens / (ms / 1e3)
@@ -538,6 +554,8 @@ def main():
                       peak_source=peaks["source"] + (" bf16 burst" if kind == "tensor" else " HBM copy")),
         stages=stage_report,
         fused_expert_path_ms=fused_ms,
+        cached_table_serving=dict(value=total_tokens / (cached_ms / 1e3), unit=UNIT, ms_per_step=cached_ms,
+                                  note="frozen parameters: expert table built once and reused, not the headline"),
         e2e=dict(value=total_tokens / (ems / 1e3), unit=UNIT, h2d_bytes_per_step=x_host.numel() * 2,
                  d2h_bytes_per_step=y_host.numel() * 2, ms_per_step=ems, steps=e2e_steps,
                  pipeline="upload / layer / download on three streams, L2 flush per step inside the span",

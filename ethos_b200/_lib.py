@@ -65,6 +65,7 @@ EXPORTS = {
     "ethos_router_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _P, _P, _SZ,
                                   _P, _P]),
     "ethos_expert_forward": (_I, [_DIMS, _I, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "ethos_expert_table_build": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_router_forward_noalloc": (_I, [_DIMS, _P, _P, _P, _F, _P, _P, _P, _P, _P]),
     "ethos_product_key_topk": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _F, _I, _P, _P]),

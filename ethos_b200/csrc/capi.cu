@@ -27,7 +27,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[ETHOS_NOALLOC_S
 
 namespace {
 
-constexpr int kAbiVersion = 3;
+constexpr int kAbiVersion = 4;
 
 // ------------------------------------------------------------ device cache --
 struct DeviceInfo {
@@ -106,8 +106,8 @@ EncodeTiledFn encode_fn() {
 // Row-major bf16 matrix [rows, cols] (row pitch ld >= cols elements) read in
 // boxes of 64 columns x box_rows rows with the 128-byte swizzle that the UMMA
 // descriptors expect.
-// box_cols 64 (128-byte rows, 128-byte swizzle) or 32 (64-byte rows, 64-byte
-// swizzle); the UMMA descriptor of the consuming kernel must use the same one.
+// box_cols 64, 32 or 16 (rows of 128, 64 or 32 bytes, with the swizzle of
+// that width); the UMMA descriptor of the consuming kernel must match it.
 int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows, int64_t ld = 0,
                    int box_cols = 64) {
   EncodeTiledFn fn = encode_fn();
@@ -116,12 +116,13 @@ int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, 
   if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || (ld * 2) % 16 != 0) return ETHOS_ERR_ALIGNMENT;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  if (box_cols != 64 && box_cols != 32) return ETHOS_ERR_TENSOR_MAP;
+  if (box_cols != 64 && box_cols != 32 && box_cols != 16) return ETHOS_ERR_TENSOR_MAP;
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : (box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B),
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ETHOS_OK : ETHOS_ERR_TENSOR_MAP;
@@ -293,10 +294,12 @@ dim3 bn_rows_grid(int C, int T, int threads, const DeviceInfo& dev) {
 // ------------------------------------------------------------ experts --
 // Expert execution path: 1 = fused per-token (gather latents, expand on
 // tcgen05, GELU in the epilogue), 2 = expert table (expand + GELU once per
-// expert, then gather hidden rows per token).  0 picks the table once the
-// step makes at least one selection per expert on average.
+// expert, then gather hidden rows per token), 3 = the table path on a table
+// the caller built earlier (no expansion).  0 picks the table once the step
+// makes at least one selection per expert on average.
 int resolve_expert_path(const ethos_dims& d, int path) {
   if (path == 1) return 1;
+  if (path == 3) return 3;
   if (path == 2) return d.num_heads * d.top_k >= 16 ? 2 : 1;
   const int64_t R = d.num_heads * d.top_k;
   const int64_t sel = d.tokens * R;
@@ -305,6 +308,41 @@ int resolve_expert_path(const ethos_dims& d, int path) {
 
 size_t expert_table_bytes(const ethos_dims& d) {
   return static_cast<size_t>(d.num_experts) * EX_DH * sizeof(__half);
+}
+
+// phase A: H = fp16(gelu(E @ W1^T)) [N, 512] (and, for training, G =
+// fp16(gelu'(E @ W1^T)) alongside, for the backward)
+int build_table(const ethos_dims& d, const void* latents, const void* w1, __half* table, __half* gtab, int* err,
+                cudaStream_t stream, const DeviceInfo& dev) {
+  const int N = static_cast<int>(d.num_experts);
+  int st;
+  CUtensorMap tm_e, tm_w1;
+  if ((st = make_tmap_bf16(&tm_e, latents, N, EX_DL, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
+  if (gtab != nullptr) {  // training: G = gelu'(E W1^T) alongside, for the backward
+    EpiGeluBwdF16 eg;
+    eg.h_out = table;
+    eg.g_out = gtab;
+    eg.ldo = EX_DH;
+    eg.M = N;
+    return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev);
+  }
+  EpiGeluF16 eg;
+  eg.out = table;
+  eg.ldo = EX_DH;
+  eg.M = N;
+  return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev);
+}
+
+// phase B: per-token gather, dot, activation, weighted sum
+int launch_gather(const __half* table, const int32_t* ids, const float* weights, const float* xp,
+                  __nv_bfloat16* hacc, float* dot, int T, int R, int N, int* err, cudaStream_t stream,
+                  const DeviceInfo& dev) {
+  int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
+  if (blocks > dev.sm_count) blocks = dev.sm_count;
+  k_expert_gather<<<blocks, GATHER_THREADS, GATHER_SMEM_BYTES, stream>>>(table, ids, weights, xp, hacc, dot, T, R,
+                                                                         N, err);
+  return launch_status();
 }
 
 int run_experts(const ethos_dims& d, int path, const void* latents, const void* w1, const int32_t* ids,
@@ -332,31 +370,13 @@ int run_experts(const ethos_dims& d, int path, const void* latents, const void* 
     k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, stream>>>(tm_w1, ea, err);
     return launch_status();
   }
-  // phase A: H = fp16(gelu(E @ W1^T))   [N, 512]
-  CUtensorMap tm_e, tm_w1;
-  if ((st = make_tmap_bf16(&tm_e, latents, N, EX_DL, 128)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
-  if (gtab != nullptr) {  // training: G = gelu'(E W1^T) alongside, for the backward
-    EpiGeluBwdF16 eg;
-    eg.h_out = table;
-    eg.g_out = gtab;
-    eg.ldo = EX_DH;
-    eg.M = N;
-    if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
-  } else {
-    EpiGeluF16 eg;
-    eg.out = table;
-    eg.ldo = EX_DH;
-    eg.M = N;
-    if ((st = launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev)) != ETHOS_OK) return st;
+  if (path == 3) {  // the caller's table: phase A is skipped
+    mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
+    return launch_gather(table, ids, weights, xp, hacc, dot, T, R, N, err, stream, dev);
   }
+  if ((st = build_table(d, latents, w1, table, gtab, err, stream, dev)) != ETHOS_OK) return st;
   mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
-  // phase B: per-token gather, dot, activation, weighted sum
-  int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
-  if (blocks > dev.sm_count) blocks = dev.sm_count;
-  k_expert_gather<<<blocks, GATHER_THREADS, GATHER_SMEM_BYTES, stream>>>(table, ids, weights, xp, hacc, dot, T, R,
-                                                                         N, err);
-  return launch_status();
+  return launch_gather(table, ids, weights, xp, hacc, dot, T, R, N, err, stream, dev);
 }
 
 template <int TOPK>
@@ -573,7 +593,20 @@ size_t ethos_forward_workspace_size(const ethos_dims* dims, int bn_training, int
 
 size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path) {
   if (check_dims_impl(dims) != ETHOS_OK) return 0;
-  return resolve_expert_path(*dims, expert_path) == 2 ? expert_table_bytes(*dims) + 256 : 256;
+  return resolve_expert_path(*dims, expert_path) >= 2 ? expert_table_bytes(*dims) + 256 : 256;
+}
+
+int ethos_expert_table_build(const ethos_dims* dims, const void* latents, const void* w1, void* htab, void* gtab,
+                             int* dev_err, void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!latents || !w1 || !htab || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(latents) || !aligned16(w1) || !aligned16(htab) || (gtab && !aligned16(gtab)))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  return build_table(*dims, latents, w1, static_cast<__half*>(htab), static_cast<__half*>(gtab), dev_err,
+                     static_cast<cudaStream_t>(stream), *dev);
 }
 
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
@@ -586,19 +619,24 @@ int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat
   if (st != ETHOS_OK) return st;
   if (!x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !y || !ids || !weights || !workspace || !dev_err)
     return ETHOS_ERR_INVALID_ARG;
-  if (expert_path < 0 || expert_path > 2) return ETHOS_ERR_INVALID_ARG;
+  if (expert_path < 0 || expert_path > 3) return ETHOS_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(w_cat) || !aligned16(bn) || !aligned16(key_cat) || !aligned16(latents) ||
       !aligned16(w1) || !aligned16(wv) || !aligned16(y) || !aligned16(ids) || !aligned16(weights) ||
       !aligned16(workspace) || (save_xp && !aligned16(save_xp)) || (save_hacc && !aligned16(save_hacc)) ||
       (save_qpre && !aligned16(save_qpre)) || (save_qs && !aligned16(save_qs)) ||
       (save_htab && !aligned16(save_htab)) || (save_gtab && !aligned16(save_gtab)))
     return ETHOS_ERR_ALIGNMENT;
-  if ((save_htab == nullptr) != (save_gtab == nullptr)) return ETHOS_ERR_INVALID_ARG;
+  if (expert_path == 3) {  // save_htab is the caller's table, read only
+    if (save_htab == nullptr || save_gtab != nullptr) return ETHOS_ERR_INVALID_ARG;
+    if (dims->num_heads * dims->top_k < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  } else if ((save_htab == nullptr) != (save_gtab == nullptr)) {
+    return ETHOS_ERR_INVALID_ARG;
+  }
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
   const ethos_dims& d = *dims;
   const int path = resolve_expert_path(d, expert_path);
-  const bool keep_tables = save_htab != nullptr && path == 2;
+  const bool keep_tables = save_htab != nullptr && path >= 2;
   if (workspace_bytes < ethos_forward_workspace_size(dims, bn_training, path)) return ETHOS_ERR_WORKSPACE;
   cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
   Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
@@ -664,14 +702,15 @@ int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* la
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
   if (!latents || !w1 || !ids || !weights || !xp || !hacc || !dev_err) return ETHOS_ERR_INVALID_ARG;
-  if (expert_path < 0 || expert_path > 2) return ETHOS_ERR_INVALID_ARG;
+  if (expert_path < 0 || expert_path > 3) return ETHOS_ERR_INVALID_ARG;
+  if (expert_path == 3 && dims->num_heads * dims->top_k < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
   if (!aligned16(latents) || !aligned16(w1) || !aligned16(ids) || !aligned16(weights) || !aligned16(xp) ||
       !aligned16(hacc) || (workspace && !aligned16(workspace)))
     return ETHOS_ERR_ALIGNMENT;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
   const int path = resolve_expert_path(*dims, expert_path);
-  if (path == 2 && (workspace == nullptr || workspace_bytes < expert_table_bytes(*dims)))
+  if (path >= 2 && (workspace == nullptr || workspace_bytes < expert_table_bytes(*dims)))
     return ETHOS_ERR_WORKSPACE;
   return run_experts(*dims, path, latents, w1, ids, weights, xp, static_cast<__nv_bfloat16*>(hacc), dot,
                      static_cast<__half*>(workspace), dev_err, static_cast<cudaStream_t>(stream), *dev);

@@ -305,7 +305,7 @@ constexpr int ROUTER_THREADS = 320;
 #define ETHOS_ROUTER_KB 32
 #endif
 constexpr int ROUTER_KB = ETHOS_ROUTER_KB;
-static_assert(ROUTER_KB == 32 || ROUTER_KB == 64, "stage width is one 64- or 128-byte swizzle row");
+static_assert(ROUTER_KB == 16 || ROUTER_KB == 32 || ROUTER_KB == 64, "stage width is one swizzle row");
 constexpr int ROUTER_STAGES = 128 / ROUTER_KB;
 constexpr int ROUTER_A_BYTES = 128 * ROUTER_KB * 2;
 constexpr int ROUTER_B_BYTES_MAX = 256 * ROUTER_KB * 2;
@@ -322,7 +322,8 @@ constexpr int ROUTER_XMAX_BYTES = 2 * 16 * 128 * 4;     // [group][16 maxima][12
 constexpr int ROUTER_XLIST_BYTES = 2 * 16 * 128 * 4;    // [value|id][16][128 rows]
 
 __device__ __forceinline__ uint64_t router_desc(uint32_t smem_addr) {
-  return ROUTER_KB == 64 ? umma_desc_sw128(smem_addr) : umma_desc_sw64(smem_addr);
+  return ROUTER_KB == 64 ? umma_desc_sw128(smem_addr)
+                         : (ROUTER_KB == 32 ? umma_desc_sw64(smem_addr) : umma_desc_sw32(smem_addr));
 }
 
 struct RouterCtl {

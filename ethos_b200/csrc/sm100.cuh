@@ -187,6 +187,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t smem_addr) {
   return d;
 }
 
+// And for the 32-byte swizzle: rows of 32 B (16 bf16, one K step), 8-row
+// groups 256 B apart, layout = 6 (SWIZZLE_32B), tile base 256-B aligned.
+__device__ __forceinline__ uint64_t umma_desc_sw32(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(256u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(6u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major.
 // Bits: [4,6) D format (1 = f32), [7,10) A format (1 = bf16), [10,13) B format
 // (1 = bf16), bit 15/16 A/B major (0 = K), [17,23) N>>3, [24,29) M>>4.

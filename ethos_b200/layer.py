@@ -148,7 +148,8 @@ class _EthosLayerFunction(torch.autograd.Function):
         eps, mom = layer.router._bn_eps_momentum()
         training = layer.router._bn_training()
         x16 = x2d.to(torch.bfloat16).contiguous()
-        out = ops.layer_forward(x16, pw, training, eps, mom, save=need_grad, path=layer.expert_path)
+        htab = layer._expert_table() if (layer.cache_expert_table and not need_grad) else None
+        out = ops.layer_forward(x16, pw, training, eps, mom, save=need_grad, path=layer.expert_path, htab=htab)
         if training:
             layer.router._write_back_running(pw.bn)
         ctx.layer = layer
@@ -187,6 +188,11 @@ class EthosExpertLayer(nn.Module):
         # AUTO evaluates gelu(E @ W1^T) once per expert when a step makes at
         # least one selection per expert on average, else per selection
         self.expert_path = ops.EXPERT_AUTO
+        # inference with frozen parameters: keep the expert table H =
+        # gelu(E @ W1^T) (N x dh fp16, 256 MiB at 262 144 experts) across
+        # forwards and gather from it; rebuilt whenever a weight changes
+        # (storage or version counter), never used when gradients are needed
+        self.cache_expert_table = False
         self._cache_key = None
         self._cache = None
 
@@ -223,6 +229,14 @@ class EthosExpertLayer(nn.Module):
             c["bn_key"] = None if r.training else bn_key
         return ops.PackedWeights(w_cat=c["w_cat"], key_cat=c["key_cat"], latents=c["latents"], w1=c["w1"],
                                  wv=c["wv"], bn=c["bn"], dims=self.dims)
+
+    def _expert_table(self):
+        """The cached expert table for the weights ``_packed`` last saw (its
+        cache entry is replaced, and the table with it, when they change)."""
+        c = self._cache
+        if c.get("htab") is None:
+            c["htab"], _ = ops.expert_table_build(c["latents"], c["w1"], self.dims)
+        return c["htab"]
 
     def _grad_params(self):
         r = self.router

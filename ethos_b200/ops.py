@@ -137,7 +137,7 @@ def product_key_topk(q, keys, top_k):
     return w, ids
 
 
-EXPERT_AUTO, EXPERT_FUSED, EXPERT_TABLE = 0, 1, 2
+EXPERT_AUTO, EXPERT_FUSED, EXPERT_TABLE, EXPERT_TABLE_CACHED = 0, 1, 2, 3
 
 
 def expert_forward(latents, w1, ids, weights, xp, dims, save_dot=False, path=EXPERT_AUTO):
@@ -159,6 +159,23 @@ def expert_forward(latents, w1, ids, weights, xp, dims, save_dot=False, path=EXP
                                  _vp(weights.contiguous()), _vp(xp.contiguous()), _vp(hacc), _vp(dot), _vp(ws),
                                  ws_bytes, _vp(err), _stream(ids.device)), "ethos_expert_forward")
     return hacc, dot
+
+
+def expert_table_build(latents, w1, dims, with_grad=False):
+    """The expert table ``H = fp16(gelu(latents @ w1^T))`` [N, dh] (and, with
+    ``with_grad``, ``G = fp16(gelu'(latents @ w1^T))``) that
+    ``EXPERT_TABLE_CACHED`` gathers from.  ``latents`` bf16 [N, dl], ``w1``
+    bf16 [dh, dl].  Returns ``(htab, gtab or None)``."""
+    _require_cuda(latents, "latents")
+    N, dh = dims["num_experts"], dims["d_hidden"]
+    htab = torch.empty((N, dh), dtype=torch.float16, device=latents.device)
+    gtab = torch.empty_like(htab) if with_grad else None
+    ed = make_dims(1, dims)
+    err = device_error_word(latents.device)
+    check(lib().ethos_expert_table_build(ctypes.byref(ed), _vp(latents.contiguous()), _vp(w1.contiguous()),
+                                         _vp(htab), _vp(gtab), _vp(err), _stream(latents.device)),
+          "ethos_expert_table_build")
+    return htab, gtab
 
 
 class PackedWeights:
@@ -205,6 +222,8 @@ def resolve_expert_path(tokens, dims, path=EXPERT_AUTO):
     the table once the step makes at least one selection per expert and
     H * k >= 16, otherwise the fused per-token kernel."""
     R = dims["num_heads"] * dims["top_k"]
+    if path == EXPERT_TABLE_CACHED:
+        return EXPERT_TABLE_CACHED
     if path == EXPERT_FUSED:
         return EXPERT_FUSED
     if path == EXPERT_TABLE:
@@ -212,12 +231,20 @@ def resolve_expert_path(tokens, dims, path=EXPERT_AUTO):
     return EXPERT_TABLE if (tokens * R >= dims["num_experts"] and R >= 16) else EXPERT_FUSED
 
 
-def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_AUTO, stage_events=None):
+def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_AUTO, stage_events=None,
+                  htab=None):
     """Router + experts.  Returns a dict with ``y`` (bf16 [T, d]), ``ids``,
     ``weights`` and, when ``save``, the tensors the backward pass needs.
     ``stage_events``: optional list of len(STAGES) ``torch.cuda.Event`` that
-    the library records at each stage boundary (per-kernel timing)."""
+    the library records at each stage boundary (per-kernel timing).
+    ``htab``: a prebuilt expert table (``expert_table_build``) for the
+    current latents and W1; the experts then gather from it and skip the
+    expansion (inference only: not with ``save``)."""
     _require_cuda(x2d, "x")
+    if htab is not None:
+        if save:
+            raise ValueError("a cached expert table serves inference only (save=False)")
+        path = EXPERT_TABLE_CACHED
     d = pw.dims
     T = x2d.shape[0]
     dev = x2d.device
@@ -246,6 +273,8 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
             out["htab"] = torch.empty((d["num_experts"], dh), dtype=torch.float16, device=dev)
             out["gtab"] = torch.empty((d["num_experts"], dh), dtype=torch.float16, device=dev)
     g = out.get
+    if htab is not None:
+        out["htab"] = htab
     err = device_error_word(dev)
     check(L.ethos_layer_forward(ctypes.byref(dims), _vp(x2d), _vp(pw.w_cat), _vp(pw.bn), float(eps),
                                 float(momentum), 1 if bn_training else 0, _vp(pw.key_cat), _vp(pw.latents),
@@ -255,6 +284,8 @@ def layer_forward(x2d, pw, bn_training, eps, momentum, save=False, path=EXPERT_A
                                 _vp(g("bn_stats")), _vp(g("qs")), _vp(g("htab")), _vp(g("gtab")), _vp(ws), ws_bytes,
                                 _vp(err), _events(stage_events), _stream(dev)),
           "ethos_layer_forward")
+    if htab is not None:
+        del out["htab"]
     return out
 
 

@@ -81,10 +81,15 @@ int ethos_check_dims(const ethos_dims* dims);
  *      tcgen05 and apply GELU in the epilogue (no scratch);
  *  2 = expert table: expand + GELU once per expert into an fp16 [N, dh]
  *      table (scratch), then gather hidden rows per token;
+ *  3 = cached expert table: path 2 without the expansion, gathering from a
+ *      table the caller built with ethos_expert_table_build (serving with
+ *      frozen parameters; the caller rebuilds it whenever expert_latents or
+ *      net.0.weight change).  Needs num_heads * top_k >= 16;
  *  0 = automatic: the table once tokens*heads*top_k >= num_experts. */
 #define ETHOS_EXPERT_AUTO 0
 #define ETHOS_EXPERT_FUSED 1
 #define ETHOS_EXPERT_TABLE 2
+#define ETHOS_EXPERT_TABLE_CACHED 3
 
 /* Stage boundaries of ethos_layer_forward (indices into stage_events). */
 #define ETHOS_STAGE_START 0
@@ -139,7 +144,9 @@ size_t ethos_expert_workspace_size(const ethos_dims* dims, int expert_path);
  *            save_htab, save_gtab fp16 [N, dh] (both or neither; used only
  *            when the table path runs): the expert table H = gelu(E W1^T) is
  *            built there instead of in the workspace, together with
- *            G = gelu'(E W1^T), so that the backward need not rebuild them
+ *            G = gelu'(E W1^T), so that the backward need not rebuild them.
+ *            With expert_path ETHOS_EXPERT_TABLE_CACHED, save_htab is instead
+ *            the caller's prebuilt table (read only) and save_gtab is NULL.
  */
 int ethos_layer_forward(const ethos_dims* dims, const void* x, const void* w_cat, float* bn, float bn_eps,
                         float bn_momentum, int bn_training, const void* key_cat, const void* latents,
@@ -164,12 +171,21 @@ int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_ca
  *  hacc   bf16 [T, dh] out: sum_{h,k} gelu(h.xp)*w*h;  dot fp32 [T, H*k] out
  *         (optional, may be NULL)
  *  workspace: ethos_expert_workspace_size() bytes (the fp16 expert table for
- *         the table path; may be NULL for the fused path)
+ *         the table path; may be NULL for the fused path; for
+ *         ETHOS_EXPERT_TABLE_CACHED it holds the prebuilt table)
  * Ids outside [0, N) are not dereferenced: they set ETHOS_ERR_ID_OUT_OF_RANGE
  * in dev_err and read row 0 instead. */
 int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* latents, const void* w1,
                          const int32_t* ids, const float* weights, const float* xp, void* hacc, float* dot,
                          void* workspace, size_t workspace_bytes, int* dev_err, void* stream);
+
+/* The expert table alone (no counterpart in the reference, whose experts
+ * expand every selection, model.py:320-323): htab fp16 [N, dh] =
+ * gelu_erf(latents @ w1^T), and when gtab (fp16 [N, dh], may be NULL) is
+ * given also gelu_erf'(latents @ w1^T).  latents bf16 [N, dl], w1 bf16
+ * [dh, dl].  The table that ETHOS_EXPERT_TABLE_CACHED gathers from. */
+int ethos_expert_table_build(const ethos_dims* dims, const void* latents, const void* w1, void* htab, void* gtab,
+                             int* dev_err, void* stream);
 
 /* Router forward that allocates nothing (no counterpart in the reference).
  *

@@ -326,3 +326,38 @@ def test_stage_events_time_every_kernel():
     times = [ev[i].elapsed_time(ev[i + 1]) for i in range(len(ev) - 1)]
     assert all(t >= 0 for t in times)
     assert times[0] > 0 and times[2] > 0 and times[3] > 0 and times[4] > 0 and times[5] > 0
+
+
+def test_cached_expert_table_matches_and_tracks_weights():
+    """Serving with frozen parameters: the cached table gives the table path's
+    output bit for bit (the same gather on the same table), at any batch size,
+    and is rebuilt after an in-place weight update."""
+    cfg = CFG1
+    layer = EthosExpertLayer(EthosConfig(**cfg))
+    layer.load_state_dict(seeded_state_dict(layer, seed=5))
+    layer = layer.to("cuda", torch.bfloat16).eval()
+    layer.expert_path = ops.EXPERT_TABLE
+    for T in (512, 24):  # 24 tokens: fewer selections than experts
+        x = seeded_input(T, cfg["d_model"], seed=13).to("cuda", torch.bfloat16).view(1, T, -1)
+        with torch.no_grad():
+            layer.cache_expert_table = False
+            ref = layer(x)
+            layer.cache_expert_table = True
+            first = layer(x)
+            again = layer(x)
+        torch.cuda.synchronize()
+        ops.check_device_error("cuda")
+        assert torch.equal(first, ref) and torch.equal(again, ref)
+    with torch.no_grad():
+        layer.expert_latents.weight.mul_(1.5)   # bumps the version counter
+        cached = layer(x)
+        layer.cache_expert_table = False
+        fresh = layer(x)
+    torch.cuda.synchronize()
+    assert torch.equal(cached, fresh) and not torch.equal(cached, ref)
+    # with gradients the table is rebuilt (and kept for the backward) every call
+    layer.cache_expert_table = True
+    xg = x.detach().clone().requires_grad_(True)
+    y = layer(xg)
+    y.float().sum().backward()
+    assert rel_err(y.detach().float(), fresh.float()) <= 1e-3 and xg.grad is not None
