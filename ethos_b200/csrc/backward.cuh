@@ -434,56 +434,65 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
     const float dg = act ? wr * (dwr - s) : 0.f;
     const int id = act ? ids[o + lane] : 0;
     const int i1 = id / K, i2 = id - i1 * K;
-    // dS scatter: lanes with the same key combine (uniform loop over the
-    // TOPK selections), the lowest such lane stores
+    // dS scatter: lanes with the same key combine (each lane walks the lanes
+    // of its key group, the warp as long as the largest group), the lowest
+    // lane of a group stores
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int key = act ? (p == 0 ? i1 : i2) : -1 - lane;
-      const unsigned same = __match_any_sync(0xffffffffu, key);
+      unsigned m = __match_any_sync(0xffffffffu, key);
+      const int leader = __ffs(m) - 1;
+      const int rounds = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(__popc(m)));
       float tot = 0.f;
-#pragma unroll
-      for (int u = 0; u < TOPK; ++u) {
-        const float gu = __shfl_sync(0xffffffffu, dg, u);
-        const int ku = __shfl_sync(0xffffffffu, key, u);
-        tot += ku == key ? gu : 0.f;
+      for (int it = 0; it < rounds; ++it) {
+        const int src = m ? __ffs(m) - 1 : lane;
+        const float gu = __shfl_sync(0xffffffffu, dg, src);
+        tot += m ? gu : 0.f;
+        m &= m - 1u;
       }
-      if (act && (__ffs(same) - 1) == lane)
+      if (act && leader == lane)
         dS[((static_cast<int64_t>(p) * H + h) * T + t) * K + key] = __float2bfloat16_rn(tot);
     }
-    // dq^ = sum_r dg_r * key rows
-    float acc0[8], acc1[8];
+    // dq^ = sum_r dg_r * key rows: the selection's sub-key indices come from
+    // the lane that decoded them; bf16 pairs widen to fp32 pairs by shifts
+    unsigned long long acc0[4], acc1[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      acc0[i] = 0.f;
-      acc1[i] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+      acc0[i] = 0ull;
+      acc1[i] = 0ull;
     }
 #pragma unroll 4
     for (int u = 0; u < TOPK; ++u) {
       const float g = __shfl_sync(0xffffffffu, dg, u);
-      const int ku = __shfl_sync(0xffffffffu, id, u);
-      const int k1 = ku / K, k2 = ku - (ku / K) * K;
+      const int k1 = __shfl_sync(0xffffffffu, i1, u);
+      const int k2 = __shfl_sync(0xffffffffu, i2, u);
       if (lane < nl) {
         const uint4 a = *reinterpret_cast<const uint4*>(keys + static_cast<int64_t>(k1) * key_ld + 8 * lane);
         const uint4 b = *reinterpret_cast<const uint4*>(keys + (static_cast<int64_t>(K) + k2) * key_ld + 8 * lane);
-        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+        const unsigned long long g2 = pk2(g, g);
+        const uint32_t av[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 fa = __bfloat1622float2(a2[i]);
-          const float2 fb = __bfloat1622float2(b2[i]);
-          acc0[2 * i] = fmaf(g, fa.x, acc0[2 * i]);
-          acc0[2 * i + 1] = fmaf(g, fa.y, acc0[2 * i + 1]);
-          acc1[2 * i] = fmaf(g, fb.x, acc1[2 * i]);
-          acc1[2 * i + 1] = fmaf(g, fb.y, acc1[2 * i + 1]);
+          const unsigned long long fa = pk2(__uint_as_float(av[i] << 16), __uint_as_float(av[i] & 0xffff0000u));
+          const unsigned long long fb = pk2(__uint_as_float(bv[i] << 16), __uint_as_float(bv[i] & 0xffff0000u));
+          acc0[i] = ffma2(g2, fa, acc0[i]);
+          acc1[i] = ffma2(g2, fb, acc1[i]);
         }
       }
     }
     if (lane < nl) {
       float* dst = dqhat + static_cast<int64_t>(t) * (H * 2 * half) + static_cast<int64_t>(h) * 2 * half;
-      *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(acc0[0], acc0[1], acc0[2], acc0[3]);
-      *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(acc0[4], acc0[5], acc0[6], acc0[7]);
-      *reinterpret_cast<float4*>(dst + half + 8 * lane) = make_float4(acc1[0], acc1[1], acc1[2], acc1[3]);
-      *reinterpret_cast<float4*>(dst + half + 8 * lane + 4) = make_float4(acc1[4], acc1[5], acc1[6], acc1[7]);
+      float c0[8], c1[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        upk2(acc0[i], c0[2 * i], c0[2 * i + 1]);
+        upk2(acc1[i], c1[2 * i], c1[2 * i + 1]);
+      }
+      *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(c0[0], c0[1], c0[2], c0[3]);
+      *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(c0[4], c0[5], c0[6], c0[7]);
+      *reinterpret_cast<float4*>(dst + half + 8 * lane) = make_float4(c1[0], c1[1], c1[2], c1[3]);
+      *reinterpret_cast<float4*>(dst + half + 8 * lane + 4) = make_float4(c1[4], c1[5], c1[6], c1[7]);
     }
   }
 }
