@@ -28,32 +28,38 @@ namespace ethos {
 // Per-token backward gather: the forward gather kernel's structure with the
 // token vector dhacc in place of xp.  Per selection it writes dw, a and ddot;
 // per token dxp (fp32) and its bf16 copy into the GEMM operand du[:, off:].
-// Warps per block and cp.async ring depth.  The per-token dhacc / xp buffers
-// are double-buffered: token k+2's copies are issued STAGES-1 batches ahead,
-// which is safe while STAGES-1 < 2 * (batches per token); the host picks the
-// 2-stage instance when R / 4 is too small for the default depth.
+// Warps per block, cp.async ring depth and per-token buffers.  A token's
+// dhacc / xp vectors move to registers at its first batch and the next
+// token's copies are issued STAGES-1 batches ahead, so one buffer each is
+// enough while STAGES-1 < batches per token (R / 4); for R = 4 the host
+// launches a double-buffered instance (safe while STAGES-1 < 2 R / 4).
 // (B200, 16384 tokens x 128 selections, whole backward: 8x5 2.68 ms,
-// 10x3 2.65, 12x2 2.55)
+// 10x3 2.65, 12x2 2.55 with double buffers; 16x2 single-buffered below)
 #ifndef ETHOS_BGATHER_WARPS
-#define ETHOS_BGATHER_WARPS 12
+#define ETHOS_BGATHER_WARPS 16
 #endif
 #ifndef ETHOS_BGATHER_STAGES
 #define ETHOS_BGATHER_STAGES 2
 #endif
 constexpr int BGATHER_WARPS = ETHOS_BGATHER_WARPS;
-constexpr int BGATHER_THREADS = BGATHER_WARPS * 32;
 constexpr int BGATHER_STAGES = ETHOS_BGATHER_STAGES;
+constexpr int BGATHER_SMALL_R_WARPS = 12;  // the double-buffered instance
 constexpr int BGATHER_STAGE_BYTES = GATHER_ROWS * 1024 + 32;  // rows + 4 weights + 4 dots
-// + per-token double buffers for dhacc and xp (fp32, 2 KB each)
-__host__ __device__ constexpr int bgather_warp_bytes(int stages) {
-  return stages * BGATHER_STAGE_BYTES + 2 * 2048 + 2 * 2048;
+// + per-token buffers for dhacc and xp (fp32, 2 KB each), nbuf deep
+__host__ __device__ constexpr int bgather_warp_bytes(int stages, int nbuf) {
+  return stages * BGATHER_STAGE_BYTES + nbuf * 2048 + nbuf * 2048;
 }
-__host__ __device__ constexpr int bgather_smem_bytes(int stages) { return BGATHER_WARPS * bgather_warp_bytes(stages); }
+__host__ __device__ constexpr int bgather_smem_bytes(int warps, int stages, int nbuf) {
+  return warps * bgather_warp_bytes(stages, nbuf);
+}
 static_assert(BGATHER_STAGES >= 2, "ring needs two stages");
-static_assert(bgather_smem_bytes(BGATHER_STAGES) <= 227 * 1024, "backward gather ring exceeds shared memory");
+static_assert(bgather_smem_bytes(BGATHER_WARPS, BGATHER_STAGES, 1) <= 227 * 1024,
+              "backward gather ring exceeds shared memory");
+static_assert(bgather_smem_bytes(BGATHER_SMALL_R_WARPS, 2, 2) <= 227 * 1024,
+              "backward gather ring exceeds shared memory");
 
-template <int STAGES>
-__global__ void __launch_bounds__(BGATHER_THREADS, 1)
+template <int WARPS, int STAGES, int NBUF>
+__global__ void __launch_bounds__(WARPS * 32, 1)
     k_expert_bwd_gather(const __half* __restrict__ table, const int32_t* __restrict__ ids,
                         const float* __restrict__ w, const float* __restrict__ dot, const float* __restrict__ dhacc,
                         float* __restrict__ dw_out, float* __restrict__ ca_out, float* __restrict__ cd_out,
@@ -62,11 +68,11 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
-  uint8_t* wbase = smem_raw + wib * bgather_warp_bytes(STAGES);
+  uint8_t* wbase = smem_raw + wib * bgather_warp_bytes(STAGES, NBUF);
   uint8_t* vbuf = wbase + STAGES * BGATHER_STAGE_BYTES;
-  uint8_t* xbuf = vbuf + 2 * 2048;
-  const int gw = blockIdx.x * BGATHER_WARPS + wib;
-  const int nw = gridDim.x * BGATHER_WARPS;
+  uint8_t* xbuf = vbuf + NBUF * 2048;
+  const int gw = blockIdx.x * WARPS + wib;
+  const int nw = gridDim.x * WARPS;
   const int nbt = R / GATHER_ROWS;
   const int ntok = T > gw ? (T - 1 - gw) / nw + 1 : 0;
   const int nb = ntok * nbt;
@@ -98,13 +104,13 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
       if (lane == 1) cp_async_16(st + GATHER_ROWS * 1024 + 16, dot + static_cast<int64_t>(t) * R + r0);
       if (r0 == 0) {
         const char* xs = reinterpret_cast<const char*>(dhacc + static_cast<int64_t>(t) * 512);
-        uint8_t* xd = vbuf + (it_k & 1) * 2048;
+        uint8_t* xd = vbuf + (it_k % NBUF) * 2048;
         cp_async_16(xd + 32 * lane, xs + 32 * lane);
         cp_async_16(xd + 32 * lane + 16, xs + 32 * lane + 16);
         cp_async_16(xd + 1024 + 32 * lane, xs + 1024 + 32 * lane);
         cp_async_16(xd + 1024 + 32 * lane + 16, xs + 1024 + 32 * lane + 16);
         const char* ps = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
-        uint8_t* pd = xbuf + (it_k & 1) * 2048;
+        uint8_t* pd = xbuf + (it_k % NBUF) * 2048;
         cp_async_16(pd + 32 * lane, ps + 32 * lane);
         cp_async_16(pd + 32 * lane + 16, ps + 32 * lane + 16);
         cp_async_16(pd + 1024 + 32 * lane, ps + 1024 + 32 * lane);
@@ -136,7 +142,7 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
     cp_async_wait_group<STAGES - 1>();
     const uint8_t* st = wbase + (b % STAGES) * BGATHER_STAGE_BYTES;
     if (r0 == 0) {
-      const float4* x4 = reinterpret_cast<const float4*>(vbuf + (tk & 1) * 2048);
+      const float4* x4 = reinterpret_cast<const float4*>(vbuf + (tk % NBUF) * 2048);
       const float4 a0 = x4[2 * lane], a1 = x4[2 * lane + 1], c0 = x4[64 + 2 * lane], c1 = x4[64 + 2 * lane + 1];
       gv[0] = a0.x; gv[1] = a0.y; gv[2] = a0.z; gv[3] = a0.w;
       gv[4] = a1.x; gv[5] = a1.y; gv[6] = a1.z; gv[7] = a1.w;
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(BGATHER_THREADS, 1)
         acc2[i] = 0ull;
       }
       // bf16 copy of this token's [dhacc | xp] row for the per-expert pass
-      const float4* p4 = reinterpret_cast<const float4*>(xbuf + (tk & 1) * 2048);
+      const float4* p4 = reinterpret_cast<const float4*>(xbuf + (tk % NBUF) * 2048);
       const float4 e0 = p4[2 * lane], e1 = p4[2 * lane + 1], f0 = p4[64 + 2 * lane], f1 = p4[64 + 2 * lane + 1];
       __nv_bfloat16* gr = gx + static_cast<int64_t>(t) * 1024;
       auto pk = [](float a, float b) {

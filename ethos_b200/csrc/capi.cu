@@ -943,21 +943,23 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
   }
   // (4) per token: dw, a, ddot per selection; dxp (fp32 + bf16 into du)
   {
-    int blocks = (T + BGATHER_WARPS - 1) / BGATHER_WARPS;
-    if (blocks > dev->sm_count) blocks = dev->sm_count;
-    if (BGATHER_STAGES - 1 < 2 * (R / GATHER_ROWS)) {
-      constexpr int bytes = bgather_smem_bytes(BGATHER_STAGES);
-      if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather<BGATHER_STAGES>), bytes)) != ETHOS_OK)
-        return st;
-      k_expert_bwd_gather<BGATHER_STAGES><<<blocks, BGATHER_THREADS, bytes, sm>>>(
-          htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N,
-          dev_err);
-    } else {
-      constexpr int bytes = bgather_smem_bytes(2);
-      if ((st = smem_attr_once(reinterpret_cast<const void*>(k_expert_bwd_gather<2>), bytes)) != ETHOS_OK) return st;
-      k_expert_bwd_gather<2><<<blocks, BGATHER_THREADS, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw,
-                                                                     s.ca, s.cd, s.dxp, s.du, LDU, HQ, save_xp, s.gx,
-                                                                     T, R, N, dev_err);
+    if (BGATHER_STAGES - 1 < R / GATHER_ROWS) {  // one dhacc / xp buffer per warp
+      constexpr int bytes = bgather_smem_bytes(BGATHER_WARPS, BGATHER_STAGES, 1);
+      auto kern = k_expert_bwd_gather<BGATHER_WARPS, BGATHER_STAGES, 1>;
+      if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
+      int blocks = (T + BGATHER_WARPS - 1) / BGATHER_WARPS;
+      if (blocks > dev->sm_count) blocks = dev->sm_count;
+      kern<<<blocks, BGATHER_WARPS * 32, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd,
+                                                      s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N, dev_err);
+    } else {  // R = 4: double buffers, 2 stages
+      constexpr int W = BGATHER_SMALL_R_WARPS;
+      constexpr int bytes = bgather_smem_bytes(W, 2, 2);
+      auto kern = k_expert_bwd_gather<W, 2, 2>;
+      if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
+      int blocks = (T + W - 1) / W;
+      if (blocks > dev->sm_count) blocks = dev->sm_count;
+      kern<<<blocks, W * 32, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du,
+                                          LDU, HQ, save_xp, s.gx, T, R, N, dev_err);
     }
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
