@@ -867,14 +867,12 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          void* const* stage_events, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
-  if (d_latents == nullptr && (dims->num_heads * dims->top_k) < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
   if (!dy || !x || !w_cat || !bn || !key_cat || !latents || !w1 || !wv || !ids || !weights || !save_xp ||
       !save_hacc || !save_dot || !save_qpre || !save_qs || !dx || !d_latents || !d_w1 || !d_w2 || !d_wq || !d_bn ||
       !d_keys || !workspace || !dev_err)
     return ETHOS_ERR_INVALID_ARG;
   if (bn_training && !save_bn) return ETHOS_ERR_INVALID_ARG;
   if ((htab == nullptr) != (gtab == nullptr)) return ETHOS_ERR_INVALID_ARG;
-  if (dims->num_heads * dims->top_k < 16) return ETHOS_ERR_UNSUPPORTED_SHAPE;
   DeviceInfo* dev = nullptr;
   if ((st = device_info(&dev)) != ETHOS_OK) return st;
   if (workspace_bytes < ethos_backward_workspace_size(dims)) return ETHOS_ERR_WORKSPACE;

@@ -231,7 +231,7 @@ size_t ethos_backward_workspace_size(const ethos_dims* dims);
 
 /* Backward of ethos_layer_forward: the gradients autograd computes through
  * SimplifiedHypernetMoE.forward (model.py:288-343) including the router
- * (model.py:208-254) and its BatchNorm.  Needs num_heads * top_k >= 16.
+ * (model.py:208-254) and its BatchNorm.
  *  dy         [T, d] bf16 (dy_fp32 = 0) or fp32 (dy_fp32 = 1): dL/dy
  *  x, w_cat, bn, key_cat, latents, w1, wv, ids, weights: as passed to /
  *             returned by the forward call; bn_training as in the forward

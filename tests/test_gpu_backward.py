@@ -20,6 +20,10 @@ CFG1 = dict(d_model=512, num_experts=4096, top_k=16, num_routing_heads=8, d_late
             d_intermediate_hypernet=512, d_query=512)
 CFG2 = dict(d_model=1024, num_experts=512 * 512, top_k=16, num_routing_heads=8, d_latent=128,
             d_intermediate_hypernet=512, d_query=512)
+# few selections per token: R = 4 runs the double-buffered backward gather,
+# R = 8 the single-buffered one at its smallest safe batch count
+CFG_R4 = dict(CFG1, top_k=4, num_routing_heads=1)
+CFG_R8 = dict(CFG1, top_k=4, num_routing_heads=2)
 
 
 def _bf(t):
@@ -47,7 +51,7 @@ def _grad_tol(name):
 
 
 @pytest.mark.parametrize("cfg,T,training", [(CFG1, 256, False), (CFG1, 256, True), (CFG2, 512, True),
-                                            (CFG2, 1024, False)])
+                                            (CFG2, 1024, False), (CFG_R4, 300, True), (CFG_R8, 300, False)])
 def test_layer_backward_matches_oracle(cfg, T, training):
     layer = EthosExpertLayer(EthosConfig(**cfg))
     sd = _stats_state(seeded_state_dict(layer, seed=3))
