@@ -100,6 +100,7 @@ class ProductKeyRouter(nn.Module):
 
     def forward(self, x_flat):
         ops._require_cuda(x_flat, "x_flat")
+        _check_token_count(x_flat.shape[0], self._bn_training(), self.d_query)
         layer = _RouterOnly(self)
         pw = layer.packed(x_flat.device)
         eps, mom = self._bn_eps_momentum()
@@ -113,6 +114,17 @@ class ProductKeyRouter(nn.Module):
 
 def _bf16(t):
     return t.detach().to(torch.bfloat16).contiguous()
+
+
+def _check_token_count(tokens, bn_training, dq):
+    """The reference's own failures for degenerate batches: an empty batch
+    fails its ``view(T, -1)`` of the routing scores (model.py:222), and
+    BatchNorm1d in training mode rejects a single token (model.py:216)."""
+    if tokens == 0:
+        raise RuntimeError("cannot route an empty batch (0 tokens)")
+    if bn_training and tokens == 1:
+        raise ValueError(f"Expected more than 1 value per channel when training, got input size "
+                         f"torch.Size([1, {dq}])")
 
 
 class _RouterOnly:
@@ -251,6 +263,7 @@ class EthosExpertLayer(nn.Module):
         ops._require_cuda(x, "x")
         batch_size, seq_len, d_model = x.shape
         x2d = x.reshape(-1, d_model)
+        _check_token_count(x2d.shape[0], self.router._bn_training(), self.router.d_query)
         params = self._grad_params()
         need_grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in params))
         y = _EthosLayerFunction.apply(x2d, self, need_grad, *params)

@@ -112,3 +112,18 @@ def test_forward_refuses_cpu_tensors():
         layer(torch.zeros(1, 4, TINY["d_model"]))
     with pytest.raises(RuntimeError, match="no CPU path"):
         layer.router(torch.zeros(4, TINY["d_model"]))
+
+
+def test_degenerate_batches_fail_like_the_reference():
+    """An empty batch and a single token under training-mode BatchNorm are
+    errors in the reference (its view(T, -1) and BatchNorm1d); the layer
+    raises the same exception types before any kernel runs."""
+    from ethos_b200.layer import _check_token_count
+    with pytest.raises(RuntimeError):
+        _check_token_count(0, False, 512)
+    with pytest.raises(RuntimeError):
+        _check_token_count(0, True, 512)
+    with pytest.raises(ValueError, match="Expected more than 1 value per channel when training"):
+        _check_token_count(1, True, 512)
+    _check_token_count(1, False, 512)
+    _check_token_count(2, True, 512)
