@@ -59,9 +59,8 @@ __device__ __forceinline__ void topk_fold_chunk(float (&v)[N], int (&ix)[N], con
   __syncwarp();
 }
 
-// N-th largest of the 2N values a[0..N) and b[0..N) (N a power of two): sort
-// both descending with a bitonic network, then the N-th largest of the union
-// is min_i max(a[i], b[N-1-i]).
+// Sorts a[0..N) descending (N a power of two) with a bitonic network of
+// min/max exchanges.
 template <int N>
 __device__ __forceinline__ void bitonic_sort_desc(float (&a)[N]) {
 #pragma unroll
@@ -80,15 +79,6 @@ __device__ __forceinline__ void bitonic_sort_desc(float (&a)[N]) {
       }
     }
   }
-}
-template <int N>
-__device__ __forceinline__ float nth_largest_of_union(float (&a)[N], float (&b)[N]) {
-  bitonic_sort_desc<N>(a);
-  bitonic_sort_desc<N>(b);
-  float t = INFINITY;
-#pragma unroll
-  for (int i = 0; i < N; ++i) t = fminf(t, fmaxf(a[i], b[N - 1 - i]));
-  return t;
 }
 
 // Sorting networks over (score, id) pairs in registers: fixed, branch-free
@@ -112,25 +102,6 @@ __device__ __forceinline__ void bitonic_merge_desc_kv(float (&v)[N], int (&ix)[N
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       if ((i & j) == 0) ce_desc(v[i], ix[i], v[i | j], ix[i | j]);
-    }
-  }
-}
-template <int N>
-__device__ __forceinline__ void bitonic_sort_desc_kv(float (&v)[N], int (&ix)[N]) {
-#pragma unroll
-  for (int k = 2; k <= N; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const int l = i ^ j;
-        if (l > i) {
-          if ((i & k) == 0)
-            ce_desc(v[i], ix[i], v[l], ix[l]);
-          else
-            ce_desc(v[l], ix[l], v[i], ix[i]);
-        }
-      }
     }
   }
 }
@@ -351,10 +322,6 @@ struct RouterGeom {
   int a_col_p;    // A column offset per half
   int split;      // 1: A = [hi | lo] (KA columns), keys in columns [0, KA / 2)
 };
-
-__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
 
 template <int TOPK>
 __global__ void __launch_bounds__(ROUTER_THREADS, 1)

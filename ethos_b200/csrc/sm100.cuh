@@ -128,14 +128,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* t
       : "memory");
 }
 
-// Prefetch one box of a 2D tensor map into L2 (no shared-memory destination).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* tm, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tm)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 // Make generic-proxy writes to shared memory visible to the async proxy
 // (tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
