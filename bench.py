@@ -60,7 +60,7 @@ STAGE_WORK = {
     "experts": ("hbm", lambda T: (128 * 1024 + 512 * 4 + 128 * 8 + 512 * 2) * float(T)),
     "end": ("tensor", lambda T: 2.0 * 512 * 1024 * T),
 }
-STAGE_KERNEL = {"projection": "k_gemm_bf16_tn<EpiProj>", "topk": "k_score_topk<16>",
+STAGE_KERNEL = {"projection": "k_gemm2sm<EpiProj> (2-SM pairs)", "topk": "k_score_topk<16>",
                 "expert_table": "k_gemm_bf16_tn<EpiGeluF16>", "experts": "k_expert_gather",
                 "end": "k_gemm_bf16_tn<EpiStoreBF16>"}
 

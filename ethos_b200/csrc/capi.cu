@@ -14,6 +14,7 @@
 #include "expert_table.cuh"
 #include "backward.cuh"
 #include "gemm.cuh"
+#include "gemm2sm.cuh"
 #include "router.cuh"
 #include "optim.cuh"
 
@@ -170,6 +171,12 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   return launch_status();
 }
 
+template <class Epi, bool AMN = false, bool BMN = false>
+int launch_gemm2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int* err,
+                   cudaStream_t stream, const DeviceInfo& dev, int ksplit = 1);
+
+// D = A B^T.  N % 256 == 0 with an 8-warp epilogue runs on the 2-SM kernel
+// (256 x 256 tiles per SM pair), everything else on k_gemm.
 template <class Epi>
 int gemm(const GemmOperand& a, const GemmOperand& b, int M, int N, int K, int ksplit, const Epi& epi, int* err,
          cudaStream_t stream, const DeviceInfo& dev) {
@@ -177,20 +184,25 @@ int gemm(const GemmOperand& a, const GemmOperand& b, int M, int N, int K, int ks
   if (!a.mn_major && K % 8 != 0) return ETHOS_ERR_ALIGNMENT;
   if (!b.mn_major && K % 8 != 0) return ETHOS_ERR_ALIGNMENT;
   const bool wide = N % 256 == 0;
+  constexpr bool kPairable = Epi::kEpiWarps == 8;
+  const bool pair = wide && kPairable;
   CUtensorMap ta, tb;
   int st;
   if ((st = operand_tmap(&ta, a, M, K, 128)) != ETHOS_OK) return st;
-  if ((st = operand_tmap(&tb, b, N, K, wide ? 256 : 128)) != ETHOS_OK) return st;
+  if ((st = operand_tmap(&tb, b, N, K, pair ? G2_BN / 2 : (wide ? 256 : 128))) != ETHOS_OK) return st;
   // never leave a K slice empty
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   if (ksplit > num_kb) ksplit = num_kb;
   if (ksplit < 1) ksplit = 1;
   const int kpb = (num_kb + ksplit - 1) / ksplit;
   ksplit = (num_kb + kpb - 1) / kpb;
-#define ETHOS_GEMM_CASE(AM, BM_)                                                                     \
-  if (a.mn_major == AM && b.mn_major == BM_) {                                                      \
-    return wide ? launch_gemm_t<Epi, AM, BM_, 256>(ta, tb, M, N, K, ksplit, epi, err, stream, dev)   \
-                : launch_gemm_t<Epi, AM, BM_, 128>(ta, tb, M, N, K, ksplit, epi, err, stream, dev);  \
+#define ETHOS_GEMM_CASE(AM, BM_)                                                                       \
+  if (a.mn_major == AM && b.mn_major == BM_) {                                                        \
+    if constexpr (kPairable) {                                                                        \
+      if (pair) return launch_gemm2sm<Epi, AM, BM_>(ta, tb, M, N, K, epi, err, stream, dev, ksplit);  \
+    }                                                                                                 \
+    return wide ? launch_gemm_t<Epi, AM, BM_, 256>(ta, tb, M, N, K, ksplit, epi, err, stream, dev)     \
+                : launch_gemm_t<Epi, AM, BM_, 128>(ta, tb, M, N, K, ksplit, epi, err, stream, dev);    \
   }
   ETHOS_GEMM_CASE(false, false)
   ETHOS_GEMM_CASE(true, false)
@@ -208,6 +220,73 @@ int auto_ksplit(int M, int N, int K, const DeviceInfo& dev) {
   if (ks < 1) ks = 1;
   if (ks > num_kb) ks = num_kb;
   return ks;
+}
+
+// Clusters of two that can run at once for a 2-SM GEMM kernel (queried once
+// per kernel and device: the SM-pair topology decides it, not the tile count).
+int max_pair_clusters(const void* fn, int threads, int smem, const DeviceInfo& dev) {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return 0;
+  static std::mutex mu;
+  static const void* seen[64][8];
+  static int val[64][8];
+  static int nseen[64];
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < nseen[d]; ++i)
+    if (seen[d][i] == fn) return val[d][i];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(dev.sm_count & ~1));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (nseen[d] < 8) {
+    seen[d][nseen[d]] = fn;
+    val[d][nseen[d]++] = n;
+  }
+  return n;
+}
+
+// 2-SM GEMM (k_gemm2sm).  A K-major `tb` has 128-row boxes (each CTA of a
+// pair stages half of the 256-wide N tile), an MN-major one 64-column boxes.
+// N % 256 == 0; ksplit > 1 requires an accumulating epilogue.
+template <class Epi, bool AMN, bool BMN>
+int launch_gemm2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int* err,
+                   cudaStream_t stream, const DeviceInfo& dev, int ksplit) {
+  using Cfg = Gemm2Cfg<Epi>;
+  auto kern = k_gemm2sm<Epi, AMN, BMN>;
+  int st = smem_attr_once(reinterpret_cast<const void*>(kern), Cfg::kSmem);
+  if (st != ETHOS_OK) return st;
+  if (N % G2_BN != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  const int units = ((M + 2 * G2_BM - 1) / (2 * G2_BM)) * (N / G2_BN) * ksplit;
+  int pairs = max_pair_clusters(reinterpret_cast<const void*>(kern), Cfg::kThreads, Cfg::kSmem, dev);
+  if (pairs <= 0) return ETHOS_ERR_CUDA;
+  if (pairs > units) pairs = units;
+  if (pairs <= 0) return ETHOS_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(static_cast<unsigned>(Cfg::kThreads));
+  cfg.dynamicSmemBytes = static_cast<size_t>(Cfg::kSmem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, epi, err) != cudaSuccess) return ETHOS_ERR_CUDA;
+  return launch_status();
 }
 
 // Forward-path GEMM: both operands K-major (tensor maps built by the caller).
@@ -418,7 +497,7 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   CUtensorMap tm_x, tm_w, tm_q, tm_k;
   int st;
   if ((st = make_tmap_bf16(&tm_x, x, T, d.d_model, 128)) != ETHOS_OK) return st;
-  if ((st = make_tmap_bf16(&tm_w, w_cat, ncat, d.d_model, 256)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tm_w, w_cat, ncat, d.d_model, G2_BN / 2)) != ETHOS_OK) return st;
   if ((st = make_tmap_bf16(&tm_q, qs, static_cast<int64_t>(d.num_heads) * 2 * T, dq, 128, 0, ROUTER_KB)) != ETHOS_OK)
     return st;
   const int box_keys = d.num_sub_keys < 256 ? static_cast<int>(d.num_sub_keys) : 256;
@@ -440,7 +519,7 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   epi.qs = qs;
   epi.qpre = qpre;
   epi.xp = xp_out;
-  if ((st = launch_gemm(tm_x, tm_w, T, ncat, static_cast<int>(d.d_model), epi, err, stream, dev)) != ETHOS_OK)
+  if ((st = launch_gemm2sm(tm_x, tm_w, T, ncat, static_cast<int>(d.d_model), epi, err, stream, dev)) != ETHOS_OK)
     return st;
   mark(ev, ETHOS_STAGE_PROJECTION, stream);
   if (two_pass) {
