@@ -331,6 +331,12 @@ __device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsign
   return d;
 }
 
+__device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ float ex2_approx(float t) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
@@ -338,68 +344,59 @@ __device__ __forceinline__ float ex2_approx(float t) {
 }
 
 // The erf-form GELU, GELU(x) = x Phi(x) (torch.nn.functional.gelu with
-// approximate='none'), with the normal CDF written through the scaled
-// complementary error function:
-//   Phi(x) = 1 - h (x >= 0),  Phi(x) = h (x < 0),
-//   h = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt(2)),
-// erfcx evaluated by a degree-11 least-squares polynomial in
-// s = min(|x| / (4.2 sqrt(2)), 1) (csrc/fit_gelu.py derives the coefficients:
-// |Phi error| <= 1.8e-6, |GELU error| <= 1e-6 with fp32 evaluation) and the
-// exponential by one ex2.  d GELU / dx = Phi(x) + x phi(x) reuses the same
-// exponential: phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
+// approximate='none'), with the normal CDF written through its tail mass
+//   h = 1 - Phi(|x|) = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt(2)):
+//   Phi(x) = 1 - h (x >= 0),  Phi(x) = h (x < 0),  GELU(x) = max(x, 0) - |x| h.
+// erfcx is evaluated in the rational form of Hastings' erfc approximation
+// (Abramowitz & Stegun 7.1.26), erfcx(z) ~ t (C0 + C1 t + ... + C4 t^4) with
+// t = 1 / (1 + P z), P and C_k refit by csrc/fit_gelu.py (fp32 evaluation:
+// |Phi error| <= 3e-7, |GELU error| <= 1.2e-7); t takes one rcp.approx and
+// the exponential one ex2.approx.  d GELU / dx = Phi(x) + x phi(x) reuses the
+// same exponential: phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
 namespace gelu_detail {
-constexpr float kS = 0.16835875f;      // 1 / (4.2 sqrt(2))
-constexpr float kE = -0.72134752f;     // -log2(e) / 2
-constexpr float kPdf = 0.39894228f;    // 1 / sqrt(2 pi)
-constexpr float C0 = 9.999964237e-01f, C1 = -4.738096237e+00f, C2 = 1.758333588e+01f, C3 = -5.456176758e+01f,
-                C4 = 1.427009735e+02f, C5 = -3.059054565e+02f, C6 = 5.142192993e+02f, C7 = -6.464071045e+02f,
-                C8 = 5.776085815e+02f, C9 = -3.432381897e+02f, C10 = 1.208973465e+02f, C11 = -1.902811050e+01f;
+constexpr float kP = 3.327062726e-01f;  // P / sqrt(2): t = 1 / (1 + kP |x|)
+constexpr float kE = -0.72134752f;      // -log2(e) / 2
+constexpr float kPdf = 0.39894228f;     // 1 / sqrt(2 pi)
+constexpr float C0 = 2.474880069e-01f, C1 = 3.996735513e-01f, C2 = -1.586927176e-01f, C3 = 7.302848697e-01f,
+                C4 = -2.187540382e-01f;
 }  // namespace gelu_detail
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
 // h = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt 2) -- the tail mass 1 - Phi(|x|) --
 // for two values, the polynomial on packed pairs; the 0.5 rides in the ex2
 // argument (log2 0.5 = -1) and the half-exponential e = 0.5 exp(-x^2 / 2) is
-// returned too.  Then Phi(x) = x >= 0 ? 1 - h : h and
-// GELU(x) = x Phi(x) = max(x, 0) - |x| h for either sign.
+// returned too.
 __device__ __forceinline__ void gelu_tail2(float x0, float x1, float& h0, float& h1, float& e0, float& e1) {
   using namespace gelu_detail;
-  const unsigned long long s = pk2(fminf(fabsf(x0) * kS, 1.0f), fminf(fabsf(x1) * kS, 1.0f));
-  unsigned long long p = pk2(C11, C11);
-  p = ffma2(p, s, pk2(C10, C10));
-  p = ffma2(p, s, pk2(C9, C9));
-  p = ffma2(p, s, pk2(C8, C8));
-  p = ffma2(p, s, pk2(C7, C7));
-  p = ffma2(p, s, pk2(C6, C6));
-  p = ffma2(p, s, pk2(C5, C5));
-  p = ffma2(p, s, pk2(C4, C4));
-  p = ffma2(p, s, pk2(C3, C3));
-  p = ffma2(p, s, pk2(C2, C2));
-  p = ffma2(p, s, pk2(C1, C1));
-  p = ffma2(p, s, pk2(C0, C0));
-  float p0, p1;
-  upk2(p, p0, p1);
+  const unsigned long long d = ffma2(pk2(fabsf(x0), fabsf(x1)), pk2(kP, kP), pk2(1.0f, 1.0f));
+  float d0, d1;
+  upk2(d, d0, d1);
+  const unsigned long long t = pk2(rcp_approx(d0), rcp_approx(d1));
+  unsigned long long q = pk2(C4, C4);
+  q = ffma2(q, t, pk2(C3, C3));
+  q = ffma2(q, t, pk2(C2, C2));
+  q = ffma2(q, t, pk2(C1, C1));
+  q = ffma2(q, t, pk2(C0, C0));
   e0 = ex2_approx(fmaf(x0 * kE, x0, -1.0f));  // 0.5 exp(-x^2 / 2)
   e1 = ex2_approx(fmaf(x1 * kE, x1, -1.0f));
-  h0 = e0 * p0;
-  h1 = e1 * p1;
+  const unsigned long long h = fmul2(fmul2(q, t), pk2(e0, e1));
+  upk2(h, h0, h1);
 }
 __device__ __forceinline__ float gelu_tail(float x, float& e) {
   using namespace gelu_detail;
-  const float s = fminf(fabsf(x) * kS, 1.0f);
-  float p = C11;
-  p = fmaf(p, s, C10);
-  p = fmaf(p, s, C9);
-  p = fmaf(p, s, C8);
-  p = fmaf(p, s, C7);
-  p = fmaf(p, s, C6);
-  p = fmaf(p, s, C5);
-  p = fmaf(p, s, C4);
-  p = fmaf(p, s, C3);
-  p = fmaf(p, s, C2);
-  p = fmaf(p, s, C1);
-  p = fmaf(p, s, C0);
+  const float t = rcp_approx(fmaf(fabsf(x), kP, 1.0f));
+  float q = C4;
+  q = fmaf(q, t, C3);
+  q = fmaf(q, t, C2);
+  q = fmaf(q, t, C1);
+  q = fmaf(q, t, C0);
   e = ex2_approx(fmaf(x * kE, x, -1.0f));  // 0.5 exp(-x^2 / 2)
-  return e * p;
+  return e * (q * t);
 }
 __device__ __forceinline__ float gelu_erf(float x) {
   float e;
