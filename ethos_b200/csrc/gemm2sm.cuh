@@ -175,8 +175,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<Epi>::kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      int stage = 0;
-      uint32_t phase = 0;
+      RingPos rp;
       bool ok = true;
       for (int u = pair; ok && u < num_units; u += num_pairs) {
         const int tile = u % num_tiles;
@@ -185,14 +184,14 @@ __global__ void __launch_bounds__(Gemm2Cfg<Epi>::kThreads, 1)
         const int n0 = (tile % num_n) * G2_BN + static_cast<int>(rank) * (G2_BN / 2);
         const int kb1 = min(num_kb, (ks + 1) * kpb);
         for (int kb = ks * kpb; kb < kb1; ++kb) {
-          if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, abort, err, 1)) {
+          if (!mbar_wait(&ctl->empty[rp.stage], rp.phase ^ 1u, abort, err, 1)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * G2_STAGE_BYTES;
+          uint8_t* sa = smem + rp.stage * G2_STAGE_BYTES;
           uint8_t* sb = sa + G2_A_BYTES;
-          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * G2_STAGE_BYTES);
-          const uint32_t fb = cluster_map(smem_u32(&ctl->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&ctl->full[rp.stage], 2 * G2_STAGE_BYTES);
+          const uint32_t fb = cluster_map(smem_u32(&ctl->full[rp.stage]), 0);
           if (kAMN) {
             tma_load_2d_pair(sa, &tmA, fb, m0, kb * G2_BK);
             tma_load_2d_pair(sa + 8192, &tmA, fb, m0 + 64, kb * G2_BK);
@@ -205,15 +204,23 @@ __global__ void __launch_bounds__(Gemm2Cfg<Epi>::kThreads, 1)
           } else {
             tma_load_2d_pair(sb, &tmB, fb, kb * G2_BK, n0);
           }
-          if (++stage == G2_STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          rp.advance(G2_STAGES);
+        }
+      }
+      if (!ok) {
+        // Copies still in flight must land before the CTA's shared memory
+        // goes away.  Both CTAs' copies complete on the leader's full
+        // barriers: the leader waits for the phases of its most recent
+        // stages (bounded waits); the peer, which cannot see those barriers,
+        // waits a bounded 100 us, far above the latency of a 16 KB copy.
+        if (leader) {
+          rp.drain(ctl->full, G2_STAGES, err, 5);
+        } else {
+          const uint64_t t0 = global_timer_ns();
+          while (global_timer_ns() - t0 < 100000ull) {
           }
         }
       }
-      // After an abort the copies still in flight complete on the leader's
-      // full barriers; the teardown cluster barrier follows the leader's
-      // drain below.
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
