@@ -8,6 +8,7 @@
 
 #include <cmath>
 #include <mutex>
+#include <utility>
 
 #include "ethos_b200.h"
 #include "expert.cuh"
@@ -142,6 +143,26 @@ int launch_status() {
   return e == cudaSuccess ? ETHOS_OK : ETHOS_ERR_CUDA;
 }
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel of the stream finishes (its set-up overlaps that tail)
+// and waits in pdl_wait() for it before touching global memory.  Only kernels
+// that call pdl_wait() before their first global access are launched so.
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) return ETHOS_ERR_CUDA;
+  return launch_status();
+}
+
 // Operand of a GEMM: bf16 matrix stored row-major with row pitch ld; K-major
 // means stored [rows = M or N][K], MN-major means stored [K][M or N].
 struct GemmOperand {
@@ -167,8 +188,8 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   const int units = tiles * ksplit;
   const int grid = units < dev.sm_count ? units : dev.sm_count;
   if (grid <= 0) return ETHOS_OK;
-  kern<<<grid, GemmCfg<Epi>::kThreads, GemmCfg<Epi>::kSmem, stream>>>(ta, tb, M, N, K, ksplit, epi, err);
-  return launch_status();
+  return launch_pdl(kern, dim3(grid), dim3(GemmCfg<Epi>::kThreads), GemmCfg<Epi>::kSmem, stream, ta, tb, M, N, K,
+                    ksplit, epi, err);
 }
 
 template <class Epi, bool AMN = false, bool BMN = false>
@@ -278,13 +299,15 @@ int launch_gemm2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   cfg.blockDim = dim3(static_cast<unsigned>(Cfg::kThreads));
   cfg.dynamicSmemBytes = static_cast<size_t>(Cfg::kSmem);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel calls pdl_wait()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, epi, err) != cudaSuccess) return ETHOS_ERR_CUDA;
   return launch_status();
 }
@@ -419,9 +442,8 @@ int launch_gather(const __half* table, const int32_t* ids, const float* weights,
                   const DeviceInfo& dev) {
   int blocks = (T + GATHER_WARPS - 1) / GATHER_WARPS;
   if (blocks > dev.sm_count) blocks = dev.sm_count;
-  k_expert_gather<<<blocks, GATHER_THREADS, GATHER_SMEM_BYTES, stream>>>(table, ids, weights, xp, hacc, dot, T, R,
-                                                                         N, err);
-  return launch_status();
+  return launch_pdl(k_expert_gather, dim3(blocks), dim3(GATHER_THREADS), GATHER_SMEM_BYTES, stream, table, ids,
+                    weights, xp, hacc, dot, T, R, N, err);
 }
 
 int run_experts(const ethos_dims& d, int path, const void* latents, const void* w1, const int32_t* ids,
@@ -463,8 +485,8 @@ int launch_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom&
                  int* err, cudaStream_t stream, const DeviceInfo& dev) {
   const int items = g.H * ((g.T + 127) / 128);
   const int grid = items < dev.sm_count ? items : dev.sm_count;
-  k_score_topk<TOPK><<<grid, ROUTER_THREADS, ROUTER_SMEM_BYTES, stream>>>(ta, tb, g, ids, w, err);
-  return launch_status();
+  return launch_pdl(k_score_topk<TOPK>, dim3(grid), dim3(ROUTER_THREADS), ROUTER_SMEM_BYTES, stream, ta, tb, g, ids,
+                    w, err);
 }
 
 int run_score(const CUtensorMap& ta, const CUtensorMap& tb, const RouterGeom& g, int top_k, int32_t* ids,
@@ -505,8 +527,9 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
 
   const int cb = 256;
   if (!bn_training) {
-    k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(bn, HQ, bn_eps, two_pass ? 1 : 0, s.colp);
-    if ((st = launch_status()) != ETHOS_OK) return st;
+    if ((st = launch_pdl(k_bn_eval_colp, dim3((HQ + cb - 1) / cb), dim3(cb), 0, stream, bn, HQ, bn_eps,
+                         two_pass ? 1 : 0, s.colp)) != ETHOS_OK)
+      return st;
   }
   EpiProj epi;
   epi.M = T;

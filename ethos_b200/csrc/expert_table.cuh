@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
     k_expert_gather(const __half* __restrict__ table, const int32_t* __restrict__ ids, const float* __restrict__ w,
                     const float* __restrict__ xp, __nv_bfloat16* __restrict__ hacc_out,
                     float* __restrict__ dot_out, int T, int R, int N, int* err) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;

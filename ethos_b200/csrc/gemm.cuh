@@ -393,6 +393,8 @@ __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  pdl_launch_dependents();
+  pdl_wait();  // set-up above touched only shared memory, TMEM and parameters
   volatile int* abort = &ctl->abort;
 
   if (warp == 0) {

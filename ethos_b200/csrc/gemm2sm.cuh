@@ -169,6 +169,8 @@ __global__ void __launch_bounds__(Gemm2Cfg<Epi>::kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers initialised before any remote arrive or commit
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  pdl_launch_dependents();
+  pdl_wait();  // set-up above touched only shared memory, TMEM and parameters
   volatile int* abort = &ctl->abort;
 
   if (warp == 0) {

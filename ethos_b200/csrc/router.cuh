@@ -360,6 +360,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  pdl_launch_dependents();
+  pdl_wait();  // set-up above touched only shared memory, TMEM and parameters
   volatile int* abort = &ctl->abort;
 
   if (warp == 0) {
@@ -850,6 +852,8 @@ __global__ void k_bn_finalize(const float* __restrict__ qpre, const float* __res
 // With on_qpre != 0 the affine applies to qpre = v + bias instead.
 __global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, int on_qpre,
                                float2* __restrict__ colp) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= C) return;
   const float bias = on_qpre ? 0.f : bn[col], gamma = bn[1 * C + col], beta = bn[2 * C + col];

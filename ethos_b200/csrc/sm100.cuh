@@ -33,6 +33,18 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ------------------------------------------------ dependent launches --
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running.  pdl_launch_dependents() lets the next kernel start launching;
+// pdl_wait() blocks until the previous kernel has completed and its memory
+// is visible, and must come before this kernel's first global-memory access.
+// Both are no-ops for a kernel launched the ordinary way.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
