@@ -327,6 +327,80 @@ def run_router(args, rank, world, local, dev):
         print(json.dumps(line), flush=True)
 
 
+def run_stack(args, rank, world, local, dev):
+    """Config 4, the expert layers of the decoder: 12 ETHOS expert layers
+    (config-2 dimensions, each with its own seeded parameters) on one residual
+    stream, h = h + layer(rms_norm(h)), over the embeddings of 16 384 token ids
+    drawn Zipf(1.1) over a 100 277-entry vocabulary.  The decoder's attention,
+    embedding and output head are the reference's own model code, which is not
+    part of this repository, so they are not timed; the line reports the expert
+    layers' share of the forward."""
+    import numpy as np
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from ethos_b200 import EthosConfig, EthosExpertLayer, ops
+    from ethos_b200.init import seeded_init_
+    n_layers, vocab, T = 12, 100277, args.tokens
+    rng = np.random.default_rng(1000 + rank)
+    ids = rng.zipf(1.1, size=4 * T)
+    ids = torch.from_numpy(ids[ids <= vocab][:T] - 1).to(dev)
+    assert ids.numel() == T
+    g = torch.Generator().manual_seed(7)
+    emb = (torch.randn((vocab, CFG2["d_model"]), generator=g) / CFG2["d_model"] ** 0.5).to(dev, torch.bfloat16)
+    layers = []
+    for i in range(n_layers):
+        layer = EthosExpertLayer(EthosConfig(**CFG2))
+        seeded_init_(layer, seed=100 + i)
+        layers.append(layer.to(device=dev, dtype=torch.bfloat16).eval())
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def forward():
+        h = emb[ids].view(1, T, -1)
+        for layer in layers:
+            h = h + layer(F.rms_norm(h, (h.shape[-1],)))
+        return h
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            forward()
+        torch.cuda.synchronize()
+        ops.check_device_error(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        sampler = ClockSampler(local)
+        sampler.start()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for s_, e_ in ev:
+            flush.zero_()
+            s_.record(stream)
+            forward()
+            e_.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    if rank == 0:
+        line = dict(metric="decoder expert-layer stack tokens/s (12 x ETHOS expert layer, 262K experts, k=16x8)",
+                    value=T * world / (ms / 1e3), unit="tokens/s", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=ms, ms_per_layer=ms / n_layers, higher_is_better=True,
+                    scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic (Zipf(1.1) token ids)",
+                    config=dict(workload="config 4, expert layers only: embedding lookup, then 12 x (RMSNorm, "
+                                         "ETHOS expert layer, residual add); MLA attention and the output head "
+                                         "are not included",
+                                tokens_per_gpu=T, layers=n_layers, vocab=vocab, parallelism=f"dp{world}",
+                                l2="flushed between timed steps (256 MiB write)"),
+                    gpu_launches=6 * n_layers * args.steps, clocks=clocks)
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -336,9 +410,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
-    ap.add_argument("--mode", default="forward", choices=["forward", "train", "router"],
+    ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "stack"],
                     help="forward: config 2 (headline); train: config 5 training step; "
-                         "router: config 3 routing microbenchmark")
+                         "router: config 3 routing microbenchmark; stack: config 4's 12 expert layers")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -357,8 +431,8 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    if args.mode in ("train", "router"):
-        (run_train if args.mode == "train" else run_router)(args, rank, world, local, dev)
+    if args.mode in ("train", "router", "stack"):
+        {"train": run_train, "router": run_router, "stack": run_stack}[args.mode](args, rank, world, local, dev)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
