@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the ETHOS expert layer on B200 (one process per GPU).
 
-Metric: expert-layer tokens/s at the default size -- config 2:
-16384 tokens per GPU (batch 8 x seq 2048), d_model 1024, 262144 experts (two
+Headline metric: expert-layer tokens/s at the default size -- config 2: 16384
+tokens per GPU (batch 8 x seq 2048), d_model 1024, 262144 experts (two
 512-entry sub-key tables), d_latent 128, d_hidden 512, 8 heads, top_k 16, bf16
 forward with BatchNorm in eval mode, seeded synthetic N(0,1) inputs and
 N(0, 1/sqrt(fan_in)) parameters (no dataset is used).
@@ -12,6 +12,13 @@ N(0, 1/sqrt(fan_in)) parameters (no dataset is used).
 For N > 1 run it under torchrun (one rank per GPU): tokens shard across ranks
 with the parameters replicated and no collective in the forward (weak scaling,
 16384 tokens per GPU).  ``value`` = all ranks' tokens / max-over-ranks time.
+
+The same line carries a ``train`` block (config 5): the training step --
+forward with BatchNorm on batch statistics, backward through all parameters,
+the NCCL all-reduce of every gradient overlapped with the backward (N > 1) and
+a fused AdamW update -- timed at the same N, with the all-reduce time left
+exposed and a cross-rank checksum of the reduced gradients and updated
+parameters (the run exits non-zero if the ranks disagree).
 
 ``--impl reference`` times the reference path's CPU implementation on the
 host cores (the vectorised fp32 restatement in oracle/ethos_oracle.py of
@@ -32,6 +39,8 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+CFG1 = dict(d_model=512, num_experts=4096, top_k=16, num_routing_heads=8, d_latent=128,
+            d_intermediate_hypernet=512, d_query=512)
 CFG2 = dict(d_model=1024, num_experts=512 * 512, top_k=16, num_routing_heads=8, d_latent=128,
             d_intermediate_hypernet=512, d_query=512)
 TOKENS = 16384
@@ -44,20 +53,30 @@ L2_FLUSH_BYTES = 256 << 20
 #         expansion 128*128*512, dot + weighted sum 2*128*512, W_v 512*1024
 FLOP_PER_TOKEN = 2 * (8 * 512 * 1024 + 8 * 2 * 512 * 256 + 1024 * 512 + 128 * 128 * 512
                       + 2 * 128 * 512 + 512 * 1024)
+# Algorithmic HBM bytes per token of the whole forward: x in (2 KiB bf16),
+# y out (2 KiB), the 128 selected latent rows (128 x 256 B), plus the weights
+# (11.2 MB per step) spread over the step's tokens
+HBM_BYTES_PER_TOKEN = 2048 + 2048 + 128 * 256
+WEIGHT_BYTES = 11.2e6
 N_EXPERTS = 512 * 512
 # per-stage algorithmic work for the kernel roofline (kind, amount per step as
-# a function of T): GEMM stages in FLOPs, the table gather in HBM bytes
+# a function of T): GEMM stages in FLOPs, the expert stage in HBM bytes
 #   projection   x @ [Wq_0..Wq_7 | W_u]       2 * 1024 * 4608 per token
 #   topk         sub-key scores q . K          2 * 8 * 2 * 512 * 256 per token
 #   expert_table gelu(E @ W1^T), once per expert  2 * N * 128 * 512 per step
-#   experts      per token: 128 selected 1 KB fp16 table rows + xp (2 KB fp32)
-#                + ids/weights (1 KB) + hacc out (1 KB bf16)
+#   experts      the layer's HBM-gather term: the token's 128 selected latent
+#                rows of 256 B (bf16 x 128).  This kernel reads 1 KB fp16 rows
+#                of the expert table instead (4x the bytes, in exchange for
+#                evaluating each expert's hidden row once per step rather than
+#                once per selection), so its fraction of this roof is at most
+#                about 1/4; its DRAM rate against the copy peak is reported
+#                beside it as "dram".
 #   end          hacc @ W_v                     2 * 512 * 1024 per token
 STAGE_WORK = {
     "projection": ("tensor", lambda T: 2.0 * 1024 * 4608 * T),
     "topk": ("tensor", lambda T: 2.0 * 8 * 2 * 512 * 256 * T),
     "expert_table": ("tensor", lambda T: 2.0 * N_EXPERTS * 128 * 512),
-    "experts": ("hbm", lambda T: (128 * 1024 + 512 * 4 + 128 * 8 + 512 * 2) * float(T)),
+    "experts": ("hbm", lambda T: 128 * 256 * float(T)),
     "end": ("tensor", lambda T: 2.0 * 512 * 1024 * T),
 }
 STAGE_KERNEL = {"projection": "k_gemm2sm<EpiProj> (2-SM pairs)", "topk": "k_score_topk<16>",
@@ -89,6 +108,12 @@ def load_traffic(stage):
     except OSError:
         pass
     return None
+
+
+def launches():
+    """Kernels libethos_b200 has launched so far in this process."""
+    from ethos_b200._lib import lib
+    return int(lib().ethos_launch_count())
 
 
 class ClockSampler:
@@ -154,33 +179,83 @@ def build_layer(device, dtype=torch.bfloat16):
     return layer.to(device=device, dtype=dtype).eval()
 
 
-def cpu_baseline(tokens_budget_s=12.0, sample_tokens=512):
-    """Times the oracle restatement of the reference forward (fp32, all host
-    threads) on repeated 512-token chunks of the config-2 workload for about
-    `tokens_budget_s` seconds."""
+def _oracle_setup(cfg, tokens, round_bf16):
     from ethos_b200 import EthosConfig, EthosExpertLayer
     from ethos_b200.config import layer_dims
     from ethos_b200.init import seeded_input, seeded_state_dict
     from oracle import ethos_oracle as orc
+    c = EthosConfig(**cfg)
+    sd = seeded_state_dict(EthosExpertLayer(c), seed=0)
+    p = orc.params_from_state_dict(sd, layer_dims(c), round_bf16=round_bf16)
+    x = seeded_input(tokens, cfg["d_model"], seed=0)
+    if round_bf16:
+        x = x.to(torch.bfloat16).float()
+    return orc, p, x
+
+
+def _timed_loop(fn, tokens, budget_s):
+    """Runs ``fn`` (which processes ``tokens`` tokens) until ``budget_s``
+    seconds have passed; returns (tokens/s, tokens done, seconds)."""
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        done += tokens
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            return done / el, done, el
+
+
+def cpu_baseline(tokens_budget_s=12.0, sample_tokens=512):
+    """Times the oracle restatement of the reference forward (fp32, all host
+    threads) on repeated 512-token chunks of the config-2 workload for about
+    `tokens_budget_s` seconds."""
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    cfg = EthosConfig(**CFG2)
-    sd = seeded_state_dict(EthosExpertLayer(cfg), seed=0)
-    p = orc.params_from_state_dict(sd, layer_dims(cfg), round_bf16=True)
-    x = seeded_input(sample_tokens, CFG2["d_model"], seed=0).to(torch.bfloat16).float()
-    done, t0 = 0, time.perf_counter()
+    orc, p, x = _oracle_setup(CFG2, sample_tokens, round_bf16=True)
     with torch.no_grad():
         orc.layer_forward(x[:64], p, CFG2["top_k"])  # warm-up
-        t0 = time.perf_counter()
-        while True:
-            orc.layer_forward(x, p, CFG2["top_k"])
-            done += sample_tokens
-            el = time.perf_counter() - t0
-            if el >= tokens_budget_s:
-                break
-    return dict(value=done / el, unit=UNIT, cores=cores, kind="port",
+        val, done, el = _timed_loop(lambda: orc.layer_forward(x, p, CFG2["top_k"]), sample_tokens, tokens_budget_s)
+    return dict(value=val, unit=UNIT, cores=cores, kind="port",
                 sample=f"{done} tokens in {sample_tokens}-token chunks of config 2 (oracle fp32 restatement "
                        f"of model.py:288-343, torch CPU, {cores} threads), {el:.1f} s")
+
+
+def cpu_baseline_config1(budget_s=2.0):
+    """Config 1 in full: the 256-token fp32 forward at d_model 512 with 4096
+    experts (the reference's own CPU-runnable case), repeated for ~budget_s."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    orc, p, x = _oracle_setup(CFG1, 256, round_bf16=False)
+    with torch.no_grad():
+        orc.layer_forward(x[:32], p, CFG1["top_k"])
+        val, done, el = _timed_loop(lambda: orc.layer_forward(x, p, CFG1["top_k"]), 256, budget_s)
+    return dict(value=val, unit=UNIT, cores=cores, kind="port",
+                sample=f"config 1 in full (256 tokens, d_model 512, 4096 experts, fp32, BN eval), "
+                       f"{done // 256} forwards in {el:.1f} s")
+
+
+def cpu_baseline_train(budget_s=5.0, sample_tokens=256):
+    """The training step's CPU counterpart: forward with BatchNorm on batch
+    statistics and autograd backward through every parameter, on 256-token
+    samples at config-2 dimensions (fp32 oracle restatement)."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    orc, p, x = _oracle_setup(CFG2, sample_tokens, round_bf16=True)
+    p.requires_grad_(True)
+    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(1))
+
+    def step():
+        for t in p.tensors():
+            t.grad = None
+        xr = x.clone().requires_grad_(True)
+        y, _, _, _ = orc.layer_forward(xr, p, CFG2["top_k"], training=True)
+        (y * gy).sum().backward()
+
+    step()
+    val, done, el = _timed_loop(step, sample_tokens, budget_s)
+    return dict(value=val, unit=UNIT, cores=cores, kind="port",
+                sample=f"{done} tokens in {sample_tokens}-token forward+backward samples at config-2 dims "
+                       f"(oracle fp32 restatement, BN train, autograd through model.py:208-343), {el:.1f} s")
 
 
 def run_reference(args, rank, world):
@@ -204,16 +279,32 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def run_train(args, rank, world, local, dev):
-    """Config 5: one training step per iteration -- forward (BatchNorm in
-    training mode), backward through all 37 parameters, NCCL all-reduce of
-    the gradients (world > 1) and a fused AdamW update, 16384 tokens per GPU."""
+def _bits_hash(t):
+    """Order-dependent hash of a tensor's bit pattern (int64, on its device):
+    equal tensors give equal hashes on every rank."""
+    v = t.detach().contiguous().view(-1)
+    if v.numel() == 0:
+        return torch.zeros((), dtype=torch.int64, device=v.device)
+    iv = v.view(torch.int16).to(torch.int64) & 0xFFFF
+    w = torch.arange(iv.numel(), device=iv.device, dtype=torch.int64) % 65521 + 1
+    return (iv * w).sum()
+
+
+def train_block(args, rank, world, local, dev, layer=None, steps=None, sampler=True):
+    """Config 5: the training step -- forward with BatchNorm on batch
+    statistics, backward through every parameter, the NCCL AVG all-reduce of
+    the flat fp32 gradient buffer overlapped with the backward (world > 1),
+    then a fused AdamW update with fp32 master weights -- 16384 tokens per GPU.
+    Returns the rank-0 report (every rank must call it: it runs collectives)."""
     import torch.distributed as dist
     from ethos_b200 import ops
     from ethos_b200.dist import overlap_grad_allreduce
     from ethos_b200.init import seeded_input, tensor_generator
     from ethos_b200.optim import FusedAdamW
-    layer = build_layer(dev).train()
+    steps = steps or args.steps
+    if layer is None:
+        layer = build_layer(dev)
+    layer.train()
     T = args.tokens
     x = seeded_input(T, CFG2["d_model"], seed=rank).to(device=dev, dtype=torch.bfloat16)
     gy = (torch.randn((T, CFG2["d_model"]), generator=tensor_generator(rank, "bench.gy")) * 1e-3).to(
@@ -221,8 +312,10 @@ def run_train(args, rank, world, local, dev):
     # AdamW as the reference's DeepSpeed config (train.py:74-79), fused over all
     # of the layer's parameters in one launch, fp32 master weights for bf16
     opt = FusedAdamW(layer.parameters(), lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    comm = None
     if world > 1:
         overlap_grad_allreduce(layer)  # all-reduce inside the backward, overlapped
+        comm = layer._grad_comm
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -232,42 +325,94 @@ def run_train(args, rank, world, local, dev):
         y.backward(gy.view(1, T, -1))
         opt.step()
 
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     ops.check_device_error(dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    sampler = ClockSampler(local)
-    sampler.start()
+    if comm is not None:
+        comm["log"] = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    clk = ClockSampler(local) if sampler else None
+    if clk:
+        clk.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    n_launch = launches()
     for s_, e_ in ev:
         flush.zero_()
         s_.record(stream)
         step()
         e_.record(stream)
     torch.cuda.synchronize()
+    n_launch = launches() - n_launch
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
+    clocks = clk.stop() if clk else None
+    ops.check_device_error(dev)
     ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
+    ar = None
+    if comm is not None:
+        log = comm.pop("log")
+        span = sum(a.elapsed_time(b) for _, _, a, b in log) / len(log)
+        exposed = sum(max(0.0, end.elapsed_time(b)) for _, end, _, b in log) / len(log)
+        tail = sum(e0.elapsed_time(end) for e0, end, _, _ in log) / len(log)
+        ar = [span, exposed, tail]
+    # cross-rank agreement: the reduced gradients of the last step and the
+    # parameters after its update must be bit-identical on every rank
+    params = list(layer.parameters())
+    hashes = torch.stack([_bits_hash(p.grad) for p in params] + [_bits_hash(p) for p in params])
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([ms] + (ar or [0.0, 0.0, 0.0]), dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
+        ms, ar = t[0].item(), t[1:].tolist()
+        gathered = [torch.empty_like(hashes) for _ in range(world)]
+        dist.all_gather(gathered, hashes)
+        identical = all(torch.equal(g_, gathered[0]) for g_ in gathered)
+    else:
+        identical = True
+    grad_bytes = sum(p.numel() for p in params) * 4
+    out = dict(metric="expert-layer training tokens/s (262K experts, k=16x8 heads)",
+               value=T * world / (ms / 1e3), unit=UNIT, ms_per_step=ms, steps=steps, tokens_per_gpu=T,
+               global_batch=T * world, parallelism=f"dp{world}", dtype="bf16 (fp32 gradients and master weights)",
+               workload="config 5: forward (BN on batch statistics), backward through all 37 parameters, "
+                        "NCCL AVG all-reduce of the fp32 gradients overlapped with the backward (N > 1), "
+                        "fused AdamW with fp32 master weights",
+               l2="flushed between timed steps (256 MiB write)", gpu_launches=n_launch,
+               allreduce=dict(bytes_per_step=grad_bytes if world > 1 else 0,
+                              span_ms=ar[0] if ar else 0.0, exposed_ms=ar[1] if ar else 0.0,
+                              overlap_window_ms=ar[2] if ar else 0.0,
+                              note="span: first all-reduce start to last end on the side stream; exposed: "
+                                   "after the backward's last kernel; overlap window: backward time after "
+                                   "the latent-table gradient is final (max over ranks)"),
+               grads_and_params_identical_across_ranks=identical)
+    if clocks is not None:
+        out["clocks"] = clocks
+    if comm is not None:
+        del layer._grad_comm
+        for p in params:
+            p._ethos_allreduced = False
+    del opt
+    return out
+
+
+def run_train(args, rank, world, local, dev):
+    """--mode train: config 5 alone, as its own JSON line."""
+    tr = train_block(args, rank, world, local, dev)
     if rank == 0:
-        line = dict(metric="expert-layer training tokens/s (262K experts, k=16x8 heads)",
-                    value=T * world / (ms / 1e3), unit=UNIT, n_gpus=world, steps=args.steps,
-                    warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
+        line = dict(metric=tr["metric"], value=tr["value"], unit=UNIT, n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=tr["ms_per_step"], higher_is_better=True, scaling="weak",
                     vs_baseline=None, dtype="bf16", data="synthetic",
-                    config=dict(workload="config 5: ETHOS expert layer training step (forward, backward, "
-                                         "gradient all-reduce, fused AdamW update with fp32 master "
-                                         "weights), BN train mode",
-                                tokens_per_gpu=T, global_batch=T * world, parallelism=f"dp{world}",
-                                l2="flushed between timed steps (256 MiB write)"),
-                    clocks=clocks)
+                    config=dict(workload=tr["workload"], tokens_per_gpu=tr["tokens_per_gpu"],
+                                global_batch=tr["global_batch"], parallelism=tr["parallelism"], l2=tr["l2"]),
+                    allreduce=tr["allreduce"], gpu_launches=tr["gpu_launches"],
+                    grads_and_params_identical_across_ranks=tr["grads_and_params_identical_across_ranks"],
+                    clocks=tr.get("clocks"))
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_train()
         print(json.dumps(line), flush=True)
+    if not tr["grads_and_params_identical_across_ranks"]:
+        raise SystemExit("ranks disagree on the reduced gradients / updated parameters")
 
 
 def run_router(args, rank, world, local, dev):
@@ -289,6 +434,7 @@ def run_router(args, rank, world, local, dev):
     torch.cuda.synchronize()
     ops.check_device_error(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    n_launch = launches()
     sampler = ClockSampler(local)
     sampler.start()
     if world > 1:
@@ -300,6 +446,7 @@ def run_router(args, rank, world, local, dev):
         ops.product_key_topk(q, keys, k)
         e_.record(stream)
     torch.cuda.synchronize()
+    n_launch = launches() - n_launch
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
@@ -323,7 +470,7 @@ def run_router(args, rank, world, local, dev):
                     roofline=dict(bound="tensor", kernel="k_score_topk<16>", achieved=tf,
                                   peak=peaks["bf16_tflops"], unit="TFLOP/s", frac=tf / peaks["bf16_tflops"],
                                   traffic=None, peak_source=peaks["source"] + " bf16 burst"),
-                    clocks=clocks)
+                    gpu_launches=n_launch, clocks=clocks)
         print(json.dumps(line), flush=True)
 
 
@@ -368,6 +515,7 @@ def run_stack(args, rank, world, local, dev):
         ops.check_device_error(dev)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
+        n_launch = launches()
         sampler = ClockSampler(local)
         sampler.start()
         if world > 1:
@@ -379,6 +527,7 @@ def run_stack(args, rank, world, local, dev):
             forward()
             e_.record(stream)
         torch.cuda.synchronize()
+        n_launch = launches() - n_launch
         if world > 1:
             dist.barrier()
         clocks = sampler.stop()
@@ -397,7 +546,7 @@ def run_stack(args, rank, world, local, dev):
                                          "are not included",
                                 tokens_per_gpu=T, layers=n_layers, vocab=vocab, parallelism=f"dp{world}",
                                 l2="flushed between timed steps (256 MiB write)"),
-                    gpu_launches=6 * n_layers * args.steps, clocks=clocks)
+                    gpu_launches=n_launch, clocks=clocks)
         print(json.dumps(line), flush=True)
 
 
@@ -409,9 +558,11 @@ def main():
     ap.add_argument("--impl", default="ethos", choices=["ethos", "reference"])
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-train", action="store_true", help="leave the training block out of the forward line")
+    ap.add_argument("--train-steps", type=int, default=20, help="timed training steps in the train block")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
     ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "stack"],
-                    help="forward: config 2 (headline); train: config 5 training step; "
+                    help="forward: config 2 (headline, with the config-5 train block); train: config 5 alone; "
                          "router: config 3 routing microbenchmark; stack: config 4's 12 expert layers")
     args = ap.parse_args()
 
@@ -431,13 +582,24 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    if args.mode in ("train", "router", "stack"):
-        {"train": run_train, "router": run_router, "stack": run_stack}[args.mode](args, rank, world, local, dev)
+    ok = True
+    try:
+        if args.mode in ("train", "router", "stack"):
+            {"train": run_train, "router": run_router, "stack": run_stack}[args.mode](args, rank, world, local, dev)
+        else:
+            ok = run_forward(args, rank, world, local, dev)
+    finally:
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
-        return
+    if not ok:
+        raise SystemExit("ranks disagree on the reduced gradients / updated parameters")
 
+
+def run_forward(args, rank, world, local, dev):
+    """Config 2 (the headline) plus the config-5 train block; returns False if
+    the ranks' reduced gradients or updated parameters differ."""
+    import torch.distributed as dist
     from ethos_b200 import ops
     from ethos_b200.init import seeded_input
     layer = build_layer(dev)
@@ -471,12 +633,14 @@ def main():
         sampler.start()
         barrier()
         torch.cuda.synchronize()
+        n_launch = launches()
         for s, e in ev:
             flush.zero_()  # L2 flush between timed steps (outside the events)
             s.record(stream)
             layer(x_dev.view(1, T, -1))
             e.record(stream)
         torch.cuda.synchronize()
+        n_launch = launches() - n_launch
         barrier()
         clocks = sampler.stop()
         ms = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
@@ -518,14 +682,16 @@ def main():
         # still uploads its input from pinned host memory, runs the layer
         # (after a 256 MiB L2 flush on the compute stream, inside the timed
         # region) and downloads its output; the timed span runs from before
-        # the first upload to after the last download.
+        # the first upload to after the last download.  With compute=False
+        # the same copies run alone (the host-link floor of the pipeline).
         e2e_steps = max(4, args.steps)  # the pipeline fills and drains once per run
         s_in = torch.cuda.Stream(dev)
         s_out = torch.cuda.Stream(dev)
         xd = [torch.empty_like(x_dev) for _ in range(2)]
         yh = [y_host, torch.empty_like(y_host).pin_memory()]
+        y_stub = torch.zeros((T, CFG2["d_model"]), dtype=torch.bfloat16, device=dev)
 
-        def pipeline(n, t0=None, t1=None):
+        def pipeline(n, t0=None, t1=None, compute=True):
             up = [torch.cuda.Event() for _ in range(n)]
             used = [torch.cuda.Event() for _ in range(n)]
             done = [torch.cuda.Event() for _ in range(n)]
@@ -540,8 +706,11 @@ def main():
                     xd[b].copy_(x_host, non_blocking=True)
                     up[i].record(s_in)
                 stream.wait_event(up[i])
-                flush.zero_()
-                y = layer(xd[b].view(1, T, -1)).view(T, -1)
+                if compute:
+                    flush.zero_()
+                    y = layer(xd[b].view(1, T, -1)).view(T, -1)
+                else:
+                    y = y_stub
                 used[i].record(stream)
                 done[i].record(stream)
                 with torch.cuda.stream(s_out):
@@ -564,6 +733,15 @@ def main():
         barrier()
         ems = max_over_ranks(t0.elapsed_time(t1) / e2e_steps)
         ops.check_device_error(dev)
+        # the same copies alone, concurrently on every rank
+        pipeline(3, compute=False)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        pipeline(e2e_steps, t0, t1, compute=False)
+        torch.cuda.synchronize()
+        barrier()
+        copy_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps)
 
         # the same steps strictly one after another on one stream, for reference
         sev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(5)]
@@ -592,6 +770,13 @@ def main():
         layer.cache_expert_table = False
         cached_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in cev) / len(cev))
         ops.check_device_error(dev)
+        del xd, yh, y_stub
+
+    # ---------------- config 5: the training step at the same N --------------
+    train = None
+    if not args.no_train:
+        train = train_block(args, rank, world, local, dev, layer=layer, steps=args.train_steps, sampler=False)
+    del layer
 
     peaks = load_peaks()
     total_tokens = T * world
@@ -610,10 +795,27 @@ def main():
     for k, v in stages.items():
         kk, ww = STAGE_WORK[k]
         a = ww(T) / (v / 1e3)
-        stage_report[k] = dict(ms=v, kernel=STAGE_KERNEL[k],
-                               achieved=a / (1e12 if kk == "tensor" else 1e9),
-                               unit="TFLOP/s" if kk == "tensor" else "GB/s",
-                               frac=(a / 1e12 / peaks["bf16_tflops"]) if kk == "tensor" else (a / 1e9 / peaks["hbm_gbs"]))
+        rep = dict(ms=v, kernel=STAGE_KERNEL[k], achieved=a / (1e12 if kk == "tensor" else 1e9),
+                   unit="TFLOP/s" if kk == "tensor" else "GB/s",
+                   frac=(a / 1e12 / peaks["bf16_tflops"]) if kk == "tensor" else (a / 1e9 / peaks["hbm_gbs"]))
+        tr_k = load_traffic(k)
+        if tr_k is not None:
+            rep["dram_gbs"] = tr_k / (v / 1e3) / 1e9
+            rep["dram_frac"] = rep["dram_gbs"] / peaks["hbm_gbs"]
+        stage_report[k] = rep
+    roofline = dict(bound=kind, kernel=STAGE_KERNEL[dom], stage=dom, achieved=achieved, peak=peak, unit=unit,
+                    frac=achieved / peak, traffic=traffic,
+                    peak_source=peaks["source"] + (" bf16 burst" if kind == "tensor" else " HBM copy"))
+    if kind == "hbm":
+        roofline["algorithmic_bytes_per_launch"] = amount
+        roofline["note"] = ("achieved = the layer's HBM-gather term (128 selected latent rows x 256 B per token) "
+                            "/ launch time; the kernel reads 1 KB fp16 expert-table rows per selection instead, "
+                            "see dram")
+        if traffic is not None:
+            roofline["dram"] = dict(achieved=traffic / (stages[dom] / 1e3) / 1e9, unit="GB/s",
+                                    frac=traffic / (stages[dom] / 1e3) / 1e9 / peak,
+                                    source="dram_bytes_per_launch of profiles/experts_config2.md / launch time")
+    layer_bytes = HBM_BYTES_PER_TOKEN * T + WEIGHT_BYTES
     line = dict(
         metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
@@ -623,9 +825,11 @@ def main():
                     tokens_per_gpu=T, global_batch=total_tokens, parallelism=f"dp{world} (token shards)",
                     l2="flushed between timed steps (256 MiB write)", expert_path="auto (table at this size)"),
         layer_tflops=FLOP_PER_TOKEN * T / (ms / 1e3) / 1e12,
-        roofline=dict(bound=kind, kernel=STAGE_KERNEL[dom], stage=dom, achieved=achieved, peak=peak, unit=unit,
-                      frac=achieved / peak, traffic=traffic,
-                      peak_source=peaks["source"] + (" bf16 burst" if kind == "tensor" else " HBM copy")),
+        layer_roof=dict(tensor_frac=FLOP_PER_TOKEN * T / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                        hbm_frac=layer_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                        note="whole forward: algorithmic FLOPs / bf16 burst peak and algorithmic HBM bytes "
+                             "(x, y, 128 latent rows per token, weights) / copy peak"),
+        roofline=roofline,
         stages=stage_report,
         fused_expert_path_ms=fused_ms,
         cached_table_serving=dict(value=total_tokens / (cached_ms / 1e3), unit=UNIT, ms_per_step=cached_ms,
@@ -633,17 +837,22 @@ def main():
         e2e=dict(value=total_tokens / (ems / 1e3), unit=UNIT, h2d_bytes_per_step=x_host.numel() * 2,
                  d2h_bytes_per_step=y_host.numel() * 2, ms_per_step=ems, steps=e2e_steps,
                  pipeline="upload / layer / download on three streams, L2 flush per step inside the span",
-                 serial_ms_per_step=serial_ms),
-        gpu_launches=6 * args.steps,
+                 serial_ms_per_step=serial_ms, copy_only_ms_per_step=copy_ms,
+                 copy_only_note="the same uploads and downloads without the layer, concurrently on every rank "
+                                "(max over ranks)"),
+        gpu_launches=n_launch,
         clocks=clocks,
     )
+    if train is not None:
+        line["train"] = train
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
+        line["cpu_baseline"]["config1"] = cpu_baseline_config1()
+        if train is not None:
+            train["cpu_baseline"] = cpu_baseline_train()
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    return train is None or train["grads_and_params_identical_across_ranks"]
 
 
 if __name__ == "__main__":

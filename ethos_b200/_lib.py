@@ -52,6 +52,7 @@ _DIMS = ctypes.POINTER(EthosDims)
 # name -> (restype, argtypes); must match include/ethos_b200.h
 EXPORTS = {
     "ethos_abi_version": (_I, []),
+    "ethos_launch_count": (ctypes.c_uint64, []),
     "ethos_status_string": (ctypes.c_char_p, [_I]),
     "ethos_read_device_error": (_I, [_P, ctypes.POINTER(_I), _I, _P]),
     "ethos_check_dims": (_I, [_DIMS]),
@@ -71,6 +72,9 @@ EXPORTS = {
     "ethos_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _F, _I, _P, _P]),
     "ethos_gemm_bf16_ex": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _F, _I, _P, _P]),
     "ethos_adamw_step": (_I, [_P, _I, _I64, _F, _F, _F, _F, _F, _I64, _P, _P]),
+    "ethos_set_wait_limit_ns": (_I, [ctypes.c_uint64]),
+    "ethos_test_gelu": (_I, [_P, _P, _I64, _P]),
+    "ethos_test_gemm_withhold": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
 }
 
 _lock = threading.Lock()

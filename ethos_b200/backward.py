@@ -20,7 +20,9 @@ def _overlapped_allreduce(layer, g, events):
     ``ethos_b200.dist.overlap_grad_allreduce``: the latent and W1 slice as soon
     as the backward marks them final (ETHOS_BWD_STAGE_EXPERTS), the rest at
     its end, both on a side stream so the first overlaps the router and
-    BatchNorm gradient kernels; the current stream then waits for both."""
+    BatchNorm gradient kernels; the current stream then waits for both.
+    When the layer's ``_grad_comm["log"]`` is a list, each call appends its
+    timing events to it (benchmarks: how much of the all-reduce is exposed)."""
     comm = layer._grad_comm
     flat = g["flat"]
     boundary = g["layout"][2][1]  # d_latents, d_w1 come first; d_w2 starts here
@@ -28,13 +30,23 @@ def _overlapped_allreduce(layer, g, events):
         comm["stream"] = torch.cuda.Stream(flat.device)
     side = comm["stream"]
     works = []
+    timing = comm.get("log") is not None
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(2)] if timing else None
     with torch.cuda.stream(side):
         side.wait_event(events[0])
+        if timing:
+            marks[0].record(side)
         works.append(dist.all_reduce(flat[:boundary], op=dist.ReduceOp.AVG, group=comm["group"], async_op=True))
         side.wait_event(events[1])
         works.append(dist.all_reduce(flat[boundary:], op=dist.ReduceOp.AVG, group=comm["group"], async_op=True))
+        if timing:
+            marks[1].record(side)
     for w in works:
         w.wait()  # the current stream waits; the host does not block
+    if timing:
+        # (experts done, backward kernels done, all-reduce start, all-reduce
+        # done): read after a synchronize by whoever set comm["log"]
+        comm["log"].append((events[0], events[1], marks[0], marks[1]))
 
 
 def layer_backward(ctx, gy):
@@ -47,7 +59,8 @@ def layer_backward(ctx, gy):
     comm = getattr(layer, "_grad_comm", None)
     overlap = comm is not None and dist.is_available() and dist.is_initialized() and \
         dist.get_world_size(comm["group"]) > 1
-    events = [torch.cuda.Event(), torch.cuda.Event()] if overlap else None
+    timing = overlap and comm.get("log") is not None
+    events = [torch.cuda.Event(enable_timing=timing), torch.cuda.Event(enable_timing=timing)] if overlap else None
     g = ops.layer_backward(gy.reshape(-1, gy.shape[-1]), sv["x16"], pw, sv, ctx.training_bn, eps,
                            stage_events=events)
     if overlap:

@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <mutex>
 #include <utility>
@@ -29,7 +30,30 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[ETHOS_NOALLOC_S
 
 namespace {
 
-constexpr int kAbiVersion = 4;
+constexpr int kAbiVersion = 5;
+
+// The device GELU variants the kernels use, evaluated on x [n] (n even) into
+// out [5, n]: gelu_erf, gelu_erf2 (pairs), gelu_erf_and_grad2 (value, then
+// derivative) and gelu_erf_grad (ethos_test_gelu).
+__global__ void k_test_gelu(const float* __restrict__ x, float* __restrict__ out, int64_t n) {
+  const int64_t pairs = n / 2;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < pairs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float2 v = reinterpret_cast<const float2*>(x)[i];
+    float a0, a1, g0, g1, d0, d1;
+    gelu_erf2(v.x, v.y, a0, a1);
+    gelu_erf_and_grad2(v.x, v.y, g0, g1, d0, d1);
+    reinterpret_cast<float2*>(out)[i] = make_float2(gelu_erf(v.x), gelu_erf(v.y));
+    reinterpret_cast<float2*>(out + n)[i] = make_float2(a0, a1);
+    reinterpret_cast<float2*>(out + 2 * n)[i] = make_float2(g0, g1);
+    reinterpret_cast<float2*>(out + 3 * n)[i] = make_float2(d0, d1);
+    reinterpret_cast<float2*>(out + 4 * n)[i] = make_float2(gelu_erf_grad(v.x), gelu_erf_grad(v.y));
+  }
+}
+
+// Kernels this library has launched in this process (ethos_launch_count).
+std::atomic<unsigned long long> g_launch_count{0};
+inline void count_launch() { g_launch_count.fetch_add(1, std::memory_order_relaxed); }
 
 // ------------------------------------------------------------ device cache --
 struct DeviceInfo {
@@ -159,6 +183,7 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  count_launch();
   if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) return ETHOS_ERR_CUDA;
   return launch_status();
 }
@@ -180,7 +205,7 @@ int operand_tmap(CUtensorMap* m, const GemmOperand& o, int64_t mn, int64_t k, in
 // that accumulates (EpiAtomicF32).  BN = 256 when N allows, else 128.
 template <class Epi, bool AMN, bool BMN, int BN>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit, const Epi& epi,
-                  int* err, cudaStream_t stream, const DeviceInfo& dev) {
+                  int* err, cudaStream_t stream, const DeviceInfo& dev, int hold_unit = -1) {
   auto kern = k_gemm<Epi, AMN, BMN, BN>;
   int st = smem_attr_once(reinterpret_cast<const void*>(kern), GemmCfg<Epi>::kSmem);
   if (st != ETHOS_OK) return st;
@@ -189,7 +214,7 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   const int grid = units < dev.sm_count ? units : dev.sm_count;
   if (grid <= 0) return ETHOS_OK;
   return launch_pdl(kern, dim3(grid), dim3(GemmCfg<Epi>::kThreads), GemmCfg<Epi>::kSmem, stream, ta, tb, M, N, K,
-                    ksplit, epi, err);
+                    ksplit, epi, err, hold_unit);
 }
 
 template <class Epi, bool AMN = false, bool BMN = false>
@@ -308,6 +333,7 @@ int launch_gemm2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  count_launch();
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ksplit, epi, err) != cudaSuccess) return ETHOS_ERR_CUDA;
   return launch_status();
 }
@@ -468,6 +494,7 @@ int run_experts(const ethos_dims& d, int path, const void* latents, const void* 
     ea.N = N;
     const int grid = T < dev.sm_count ? T : dev.sm_count;
     mark(ev, ETHOS_STAGE_EXPERT_TABLE, stream);
+    count_launch();
     k_expert_fwd<<<grid, EX_THREADS, EX_SMEM_BYTES, stream>>>(tm_w1, ea, err);
     return launch_status();
   }
@@ -548,11 +575,14 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   if (two_pass) {
     if (bn_training) {
       dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+      count_launch();
       k_bn_partial<<<grid_p, cb, 0, stream>>>(qpre, T, HQ, s.bn_part);
+      count_launch();
       k_bn_finalize<<<(HQ + cb - 1) / cb, cb, 0, stream>>>(qpre, s.bn_part, T, HQ, s.slabs, bn + HQ, bn + 2 * HQ,
                                                            bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, save_bn,
                                                            s.colp);
     }
+    count_launch();
     k_bn_apply<<<bn_rows_grid(HQ, T, cb, dev), cb, 0, stream>>>(qpre, s.colp, T, static_cast<int>(d.num_heads),
                                                                  dq, qs);
     if ((st = launch_status()) != ETHOS_OK) return st;
@@ -639,6 +669,7 @@ int launch_router_bwd(const ethos_dims& d, const int32_t* ids, const float* w, c
   const int TH = static_cast<int>(d.tokens * d.num_heads);
   int blocks = (TH + 7) / 8;
   if (blocks > dev.sm_count * 8) blocks = dev.sm_count * 8;
+  count_launch();
   k_router_bwd<TOPK><<<blocks, 256, 0, stream>>>(ids, w, dw, keys, key_ld, dqhat, dS, static_cast<int>(d.tokens),
                                                   static_cast<int>(d.num_heads), static_cast<int>(d.num_sub_keys),
                                                   static_cast<int>(d.d_query / 2));
@@ -651,6 +682,8 @@ int launch_router_bwd(const ethos_dims& d, const int32_t* ids, const float* w, c
 extern "C" {
 
 int ethos_abi_version(void) { return kAbiVersion; }
+
+uint64_t ethos_launch_count(void) { return g_launch_count.load(std::memory_order_relaxed); }
 
 const char* ethos_status_string(int status) {
   switch (status) {
@@ -895,6 +928,55 @@ int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b
   return gemm(oa, ob, m, n, k, 1, e, dev_err, s, *dev);
 }
 
+int ethos_test_gelu(const float* x, float* out, int64_t n, void* stream) {
+  if (!x || !out || n < 2 || n % 2 != 0 || n > (int64_t(1) << 31)) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(out)) return ETHOS_ERR_ALIGNMENT;
+  int st;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  const int64_t pairs = n / 2;
+  int64_t blocks = (pairs + 255) / 256;
+  if (blocks > 8 * dev->sm_count) blocks = 8 * dev->sm_count;
+  count_launch();
+  k_test_gelu<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, out, n);
+  return launch_status();
+}
+
+int ethos_set_wait_limit_ns(uint64_t limit_ns) {
+  if (limit_ns == 0) limit_ns = kWaitLimitNs;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ETHOS_ERR_NO_DEVICE;
+  const unsigned long long v = limit_ns;
+  if (cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return ETHOS_ERR_CUDA;
+  return ETHOS_OK;
+}
+
+int ethos_test_gemm_withhold(const void* a, const void* b, float* dptr, int64_t M, int64_t N, int64_t K,
+                             int64_t hold_unit, int* dev_err, void* stream) {
+  if (!a || !b || !dptr || !dev_err || hold_unit < 0) return ETHOS_ERR_INVALID_ARG;
+  if (M < 1 || N < 128 || N % 128 != 0 || K < 8 || K % 8 != 0 || M > (int64_t(1) << 30) ||
+      K > (int64_t(1) << 30))
+    return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(dptr)) return ETHOS_ERR_ALIGNMENT;
+  int st;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  CUtensorMap ta, tb;
+  if ((st = make_tmap_bf16(&ta, a, M, K, 128)) != ETHOS_OK) return st;
+  if ((st = make_tmap_bf16(&tb, b, N, K, 128)) != ETHOS_OK) return st;
+  EpiStoreF32 e;
+  e.out = dptr;
+  e.ldo = N;
+  e.M = static_cast<int>(M);
+  e.scale = 1.f;
+  e.accumulate = 0;
+  return launch_gemm_t<EpiStoreF32, false, false, 128>(ta, tb, static_cast<int>(M), static_cast<int>(N),
+                                                       static_cast<int>(K), 1, e, dev_err,
+                                                       static_cast<cudaStream_t>(stream), *dev,
+                                                       static_cast<int>(hold_unit));
+}
+
 }  // extern "C"
 
 namespace {
@@ -1001,6 +1083,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
 
   const void* dy16 = dy;
   if (dy_fp32) {
+    count_launch();
     k_f32_to_bf16<<<eblocks, cb, 0, sm>>>(static_cast<const float*>(dy), static_cast<int64_t>(T) * D, s.dy16);
     dy16 = s.dy16;
   }
@@ -1049,6 +1132,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
       if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
       int blocks = (T + BGATHER_WARPS - 1) / BGATHER_WARPS;
       if (blocks > dev->sm_count) blocks = dev->sm_count;
+      count_launch();
       kern<<<blocks, BGATHER_WARPS * 32, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd,
                                                       s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N, dev_err);
     } else {  // R = 4: double buffers, 2 stages
@@ -1058,6 +1142,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
       if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
       int blocks = (T + W - 1) / W;
       if (blocks > dev->sm_count) blocks = dev->sm_count;
+      count_launch();
       kern<<<blocks, W * 32, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du,
                                           LDU, HQ, save_xp, s.gx, T, R, N, dev_err);
     }
@@ -1066,16 +1151,22 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
   // (5) selections grouped by expert (counting sort)
   {
     const int64_t nsel = static_cast<int64_t>(T) * R;
+    count_launch();
     k_count_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cnt, dev_err);
     const int nblk = (N + 1023) / 1024;
     if (nblk > 1024) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+    count_launch();
     k_scan_blocks<<<nblk, 1024, 0, sm>>>(s.cnt, N, s.offs, s.bsums);
+    count_launch();
     k_scan_sums<<<1, 1024, 0, sm>>>(s.bsums, nblk, s.total);
+    count_launch();
     k_scan_add<<<nblk, 1024, 0, sm>>>(s.offs, N, s.bsums, s.cursor);
+    count_launch();
     k_scatter_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cursor, s.perm);
     if ((st = launch_status()) != ETHOS_OK) return st;
   }
   // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
+  count_launch();
   k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.gx, gtab_, s.dP, N, R);
   if ((st = launch_status()) != ETHOS_OK) return st;
   // (7) dE = dP W1       (W1 read in place, MN-major)
@@ -1132,14 +1223,18 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
     const float* mean = save_bn;
     const float* invstd = save_bn ? save_bn + HQ : nullptr;
     if (!bn_training) {
+      count_launch();
       k_bn_eval_stats<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, s.stats, s.stats + HQ);
       mean = s.stats;
       invstd = s.stats + HQ;
     }
     dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+    count_launch();
     k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, T, HQ, s.part);
+    count_launch();
     k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, mean,
                                                         invstd, d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
+    count_launch();
     k_bn_bwd_apply<<<bn_rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(s.dqhat, save_qpre,
                                                                  reinterpret_cast<const float4*>(s.coef), T, HQ,
                                                                  s.du, LDU);
@@ -1208,6 +1303,7 @@ int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t 
   const int64_t cap = static_cast<int64_t>(dev->sm_count) * 8;
   if (bx > cap) bx = cap;
   if (bx < 1) bx = 1;
+  count_launch();
   k_adamw<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(num_tensors)), threads, 0,
             static_cast<cudaStream_t>(stream)>>>(tensors, s);
   return launch_status();

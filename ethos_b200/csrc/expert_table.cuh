@@ -71,8 +71,9 @@ __device__ __forceinline__ void unpack_h8(const uint4& u, float (&f)[8]) {
 }
 
 // One warp walks tokens gw, gw + nw, ...; its rows are processed in batches of
-// 4 through a 5-stage cp.async ring, so 4 batches (16 KB) per warp are in
-// flight while one is reduced.  Lane l copies and later reads only its own
+// 4 through a GATHER_STAGES-deep cp.async ring (2 stages by default), so
+// GATHER_STAGES - 1 batches (4 KB each) per warp are in flight while one is
+// reduced.  Lane l copies and later reads only its own
 // slices of each row, hidden columns [8l, 8l + 8) and [256 + 8l, 256 + 8l + 8)
 // (bytes [16l, 16l + 16) and [512 + 16l, ...)), so a cp.async.wait_group
 // alone orders copy and use.  Needs R / 4 > STAGES - 1 (so a token's x_proj

@@ -7,6 +7,8 @@
 //   K-major:  one box of 64 K x rows; UMMA steps K by 32 B inside the atom.
 //   MN-major: boxes of 64 M/N x 64 K (8 KB, MN blocks 8 KB apart = LBO),
 //             8-row K groups 1024 B apart (SBO); UMMA steps K by 2 KB.
+// `hold_unit` >= 0 withholds one work unit's operand loads (a test of the
+// bounded waits, see ethos_test_gemm_withhold); production launches pass -1.
 // Roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, warps
 // 2.. = 8 or 16 epilogue warps (warp w reads TMEM lanes 32*(w%4)..+31; each
 // run of four consecutive warps takes one column group of the tile).
@@ -351,7 +353,7 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32_major(int M, int N, b
 template <class Epi, bool kAMN, bool kBMN, int BN>
 __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-           int ksplit, Epi epi, int* err) {
+           int ksplit, Epi epi, int* err, int hold_unit) {
   static_assert(BN == 128 || BN == 256, "N tile is 128 or 256");
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
@@ -409,6 +411,13 @@ __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
         const int m0 = (tile / num_n) * GEMM_BM;
         const int n0 = (tile % num_n) * BN;
         const int kb1 = min(num_kb, (ks + 1) * kpb);
+        if (u == hold_unit) {
+          // failure-detection test hook (ethos_test_gemm_withhold; -1 on
+          // every production launch): this unit's operands are never
+          // loaded, so the MMA issuer's bounded wait for them runs out
+          ok = false;
+          break;
+        }
         for (int kb = ks * kpb; kb < kb1; ++kb) {
           if (!mbar_wait(&ctl->empty[rp.stage], rp.phase ^ 1u, abort, err, 1)) {
             ok = false;

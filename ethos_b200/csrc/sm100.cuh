@@ -1,7 +1,8 @@
 // sm_100a building blocks: mbarriers with bounded waits, TMA tile loads,
 // tcgen05 (UMMA) descriptors / MMA issue / commit, and TMEM alloc, load, store.
 //
-// Every wait in this library is bounded: a wait that exceeds kWaitLimitNs (or
+// Every wait in this library is bounded: a wait that exceeds the wait limit
+// (g_wait_limit_ns, kWaitLimitNs unless ethos_set_wait_limit_ns changed it; or
 // sees the CTA's abort flag) records an error code in the caller's global error
 // word and returns false, and the kernels then drain and free TMEM before they
 // return.  Nothing here traps.
@@ -17,6 +18,11 @@
 namespace ethos {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: no legitimate wait comes close
+
+// Per-device wait limit read by mbar_wait once it starts checking the clock
+// (ethos_set_wait_limit_ns; a test shortens it to make a withheld stage time
+// out quickly).  Only the slow path of a wait reads it.
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -82,11 +88,12 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile 
                                        int site) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  const uint64_t limit = *static_cast<volatile unsigned long long*>(&g_wait_limit_ns);
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0u) {
       if (abort != nullptr && *abort) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > limit) {
         if (abort != nullptr) *abort = 1;
         record_error(err, ETHOS_ERR_TIMEOUT_BASE + site);
         return false;

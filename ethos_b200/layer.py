@@ -156,7 +156,7 @@ class _EthosLayerFunction(torch.autograd.Function):
     def forward(ctx, x2d, layer, need_grad, *params):
         # need_grad is decided by the caller: inside Function.forward grad
         # mode is always off and needs_input_grad ignores torch.no_grad()
-        pw = layer._packed(x2d.device)
+        pw = layer._packed(x2d.device, fresh=need_grad)
         eps, mom = layer.router._bn_eps_momentum()
         training = layer.router._bn_training()
         x16 = x2d.to(torch.bfloat16).contiguous()
@@ -215,30 +215,42 @@ class EthosExpertLayer(nn.Module):
         ps += [m.weight for m in r.query_projs] + [r.sub_keys_1.weight, r.sub_keys_2.weight]
         return ps
 
-    def _packed(self, device):
+    def invalidate_weight_cache(self):
+        """Drop the derived kernel-layout weights (and the cached expert
+        table).  Inference forwards reuse them while every parameter keeps its
+        storage and version counter; a write through ``param.data`` (as
+        DeepSpeed's optimizers do) bumps neither, so a caller that updates the
+        parameters that way must call this before the next inference forward.
+        Forwards that need gradients always re-pack and are unaffected."""
+        self._cache_key = None
+        self._cache = None
+
+    def _packed(self, device, fresh=False):
         """Derived kernel-layout weights, cached while the parameters are
-        unchanged (same storage and version counters)."""
+        unchanged (same storage and version counters).  ``fresh`` rebuilds
+        them unconditionally (training forwards: the optimizer may have
+        written the parameters in a way the version counters do not see)."""
         ps = self._weight_params()
         key = (str(device),) + tuple((p.data_ptr(), p._version, p.dtype) for p in ps)
-        if key != self._cache_key:
+        if fresh or key != self._cache_key:
             d = self.d_model
             r = self.router
             W2 = self.generation_network.net[2].weight
             w_cat = torch.cat([_bf16(m.weight) for m in r.query_projs] + [_bf16(W2[:d].t())], 0)
             self._cache = dict(w_cat=w_cat, key_cat=_key_cat(r), latents=_bf16(self.expert_latents.weight),
                                w1=_bf16(self.generation_network.net[0].weight), wv=_bf16(W2[d:]))
-            self._cache_key = key
+            self._cache_key = None if fresh else key
         c = self._cache
         r = self.router
         bn_src = [m.bias for m in r.query_projs]
         for n in r.query_norms:
             bn_src += [n.weight, n.bias, n.running_mean, n.running_var]
         bn_key = (str(device),) + tuple((t.data_ptr(), t._version) for t in bn_src)
-        if r.training or c.get("bn_key") != bn_key:
+        if fresh or r.training or c.get("bn_key") != bn_key:
             # training mode always gets a fresh block: the kernels update its
             # running-statistics rows in place
             c["bn"] = r._bn_block()
-            c["bn_key"] = None if r.training else bn_key
+            c["bn_key"] = None if (fresh or r.training) else bn_key
         return ops.PackedWeights(w_cat=c["w_cat"], key_cat=c["key_cat"], latents=c["latents"], w1=c["w1"],
                                  wv=c["wv"], bn=c["bn"], dims=self.dims)
 

@@ -13,6 +13,7 @@ there is no CPU path.
 import ctypes
 
 import torch
+from torch.autograd.graph import increment_version
 
 from ._lib import check, lib
 from .ops import _stream, device_error_word
@@ -88,6 +89,10 @@ class FusedAdamW(torch.optim.Optimizer):
                                          beta2, group["eps"], group["weight_decay"], step,
                                          ctypes.c_void_p(err.data_ptr()), _stream(dev)),
                   "ethos_adamw_step")
+            # the kernel wrote the parameters through raw pointers: bump their
+            # version counters so that caches keyed on them (the expert
+            # layer's packed weights and expert table) see the update
+            increment_version(live)
             # the caching allocators order the reuse of these buffers after the
             # kernel; holding them until the next step is belt and braces
             self._inflight = (host, dtab, keep)

@@ -20,7 +20,8 @@
  *    `dev_err` (an int32, zero-initialised by the caller) and read back with
  *    ethos_read_device_error().
  *  - Calls are stateless and re-entrant; the only process-wide state is a
- *    lazily initialised per-device attribute cache.
+ *    lazily initialised per-device attribute cache, the launch counter
+ *    (ethos_launch_count) and the bounded-wait limit (ethos_set_wait_limit_ns).
  *  - Entry points only launch work on `stream`; they do not synchronise.
  */
 #ifndef ETHOS_B200_H
@@ -62,6 +63,12 @@ typedef struct ethos_dims {
 
 int ethos_abi_version(void);
 const char* ethos_status_string(int status);
+
+/* Number of kernels this library has launched in this process, over all
+ * devices and streams (a monotonically increasing count, read by benchmarks
+ * to report how many of the library's kernels ran in a timed region).  No
+ * counterpart in the reference. */
+uint64_t ethos_launch_count(void);
 
 /* Copies the device error word to *host_code (synchronising `stream`) and,
  * when reset != 0, clears it. */
@@ -280,6 +287,38 @@ int ethos_gemm_bf16(const void* a, const void* b, void* d, int64_t M, int64_t N,
 int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb, int b_mn_major,
                        void* d, int64_t ldd, int64_t M, int64_t N, int64_t K, float scale, int out_mode,
                        int* dev_err, void* stream);
+
+/* ------------------------------------------------- failure detection --
+ * Every wait inside the kernels (an mbarrier phase: a TMA copy landing, an
+ * MMA completing, an accumulator released) is bounded.  A wait that runs out
+ * records ETHOS_ERR_TIMEOUT_BASE + site in dev_err; the CTA then drains its
+ * in-flight copies and MMAs, frees its tensor memory and exits, leaving the
+ * CUDA context usable.  No counterpart in the reference, whose kernels have no
+ * waits. */
+
+/* Sets the wait limit of the CURRENT device in nanoseconds (0 restores the
+ * default of 2 s).  Synchronises the device.  Affects every later launch on
+ * that device, so change it only while no other work of this library runs. */
+int ethos_set_wait_limit_ns(uint64_t limit_ns);
+
+/* Test of the bounded waits: the plain GEMM D fp32 [M, N] = A bf16 [M, K] @
+ * B bf16 [N, K]^T on the one-SM kernel, with the operand loads of work unit
+ * `hold_unit` (a 128 x 128 output tile; unit 0 is the top-left tile) never
+ * issued.  The MMA issuer and the epilogue warps of that CTA wait for them
+ * until the wait limit runs out, then record ETHOS_ERR_TIMEOUT_BASE + site in
+ * dev_err and exit; the other tiles complete.  M >= 1, N % 128 == 0,
+ * K % 8 == 0. */
+int ethos_test_gemm_withhold(const void* a, const void* b, float* d, int64_t M, int64_t N, int64_t K,
+                             int64_t hold_unit, int* dev_err, void* stream);
+
+/* Test of the device GELU (no counterpart in the reference, which calls
+ * torch's erf GELU, model.py:323,329): evaluates, on x fp32 [n] (n even, both
+ * buffers 16-byte aligned), the erf-form GELU and its derivative exactly as
+ * the kernels do, into out fp32 [5, n]: row 0 the scalar form (fused expert
+ * path), row 1 the packed-pair form (expert-table epilogue), rows 2 and 3 the
+ * value and derivative of the backward tables' form, row 4 the scalar
+ * derivative. */
+int ethos_test_gelu(const float* x, float* out, int64_t n, void* stream);
 
 /* ------------------------------------------------------ optimizer step --
  * Fused AdamW over many tensors in one launch, the update the reference's

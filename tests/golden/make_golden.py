@@ -132,9 +132,12 @@ def run_case(model_mod, name, spec):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("ETHOS_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("ETHOS_REFERENCE"),
+                    help="reference checkout holding model.py (default: $ETHOS_REFERENCE)")
     ap.add_argument("--cases", default=",".join(CASES))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or ETHOS_REFERENCE")
     sys.path.insert(0, args.reference)
     import model as model_mod  # the reference's model.py
     torch.set_num_threads(os.cpu_count() or 1)

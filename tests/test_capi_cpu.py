@@ -18,7 +18,7 @@ HEADER = os.path.join(ROOT, "include", "ethos_b200.h")
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\s*\*)\s*(ethos_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|uint64_t|const char\s*\*)\s*(ethos_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -103,6 +103,17 @@ def test_null_arguments_rejected_without_gpu(L):
                                 None, None, None)
     assert st == 1
     assert L.ethos_backward_workspace_size(ctypes.byref(d)) > 2 * 512 * 512 * 512 * 2
+
+
+def test_failure_test_hook_and_counter_host_checks(L):
+    """Argument checks of the bounded-wait test entry point (no launch), and
+    the launch counter is readable without a device."""
+    v = ctypes.c_void_p(256)
+    assert L.ethos_test_gemm_withhold(None, v, v, 256, 256, 256, 0, v, None) == 1
+    assert L.ethos_test_gemm_withhold(v, v, v, 256, 256, 256, -1, v, None) == 1   # no unit to hold
+    assert L.ethos_test_gemm_withhold(v, v, v, 256, 200, 256, 0, v, None) == 2    # N % 128
+    assert L.ethos_test_gemm_withhold(v, v, v, 256, 256, 100, 0, v, None) == 2    # K % 8
+    assert L.ethos_launch_count() == L.ethos_launch_count()
 
 
 def test_no_cpu_fallback():

@@ -51,7 +51,8 @@ def _grad_tol(name):
 
 
 @pytest.mark.parametrize("cfg,T,training", [(CFG1, 256, False), (CFG1, 256, True), (CFG2, 512, True),
-                                            (CFG2, 1024, False), (CFG_R4, 300, True), (CFG_R8, 300, False)])
+                                            (CFG2, 1024, False), (CFG2, 2048, True), (CFG_R4, 300, True),
+                                            (CFG_R8, 300, False)])
 def test_layer_backward_matches_oracle(cfg, T, training):
     layer = EthosExpertLayer(EthosConfig(**cfg))
     sd = _stats_state(seeded_state_dict(layer, seed=3))

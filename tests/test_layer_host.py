@@ -66,9 +66,9 @@ def test_golden_state_dict_loads():
 
 
 def test_seeded_init_matches_reference_module_when_available():
-    ref_dir = os.environ.get("ETHOS_REFERENCE", "/root/reference")
-    if not os.path.exists(os.path.join(ref_dir, "model.py")):
-        pytest.skip("reference checkout not present")
+    ref_dir = os.environ.get("ETHOS_REFERENCE")
+    if not ref_dir or not os.path.exists(os.path.join(ref_dir, "model.py")):
+        pytest.skip("ETHOS_REFERENCE does not name a reference checkout")
     sys.path.insert(0, ref_dir)
     try:
         import model as ref_model
