@@ -12,6 +12,12 @@ It imports the reference's ``model.py`` and runs ``SimplifiedHypernetMoE``
 outputs, router decisions, BatchNorm running-stat updates and autograd
 gradients of every parameter and of ``x``.
 
+The "model" case builds the reference's whole decoder (``CompressedMoEModel``,
+``model.py:368-395``: 1 dense and 2 expert layers at a small size), runs its
+forward on CPU and records what each expert layer received and returned,
+with its routing; ``tests/test_reference_model.py`` replays those inputs
+through the oracle and through the GPU layers.
+
 Small cases store every tensor.  The config-1 case (d_model 512, 4096
 experts, 256 tokens) stores the forward outputs in full and, for a 32-token
 backward, the full gradients of the small parameters plus norms and a fixed
@@ -51,6 +57,19 @@ CASES = {
 }
 
 SAMPLE = 4096
+
+# The reference's whole decoder (CompressedMoEModel, model.py:368-395) at a
+# small size: 1 dense + 2 expert layers, the rest of train.Config's fields
+# (train.py:28-58) scaled down.  Each expert layer gets the seeded
+# initialisation (seed 100 + layer index) rounded to bf16, and a forward
+# pre-hook rounds the layer's input to bf16, so the recorded outputs are the
+# reference's fp32 arithmetic on the values the bf16 kernels consume.
+MODEL_CASE = dict(vocab_size=1024, d_model=512, num_layers=3, num_heads=4, num_dense_layers=1,
+                  num_moe_layers=2, q_lora_rank=64, kv_lora_rank=32, v_head_dim=32, qk_nope_head_dim=32,
+                  qk_rope_head_dim=32, num_experts=4096, d_latent=128, d_intermediate_hypernet=512, top_k=16,
+                  num_routing_heads=8, d_query=512, d_ffn_intermediate=512, max_seq_len=64, rms_norm_eps=1e-6,
+                  rope_theta=10000.0, use_triton=False)
+MODEL_BATCH, MODEL_SEQ = 2, 32
 
 
 def checksum(sd):
@@ -130,19 +149,67 @@ def run_case(model_mod, name, spec):
     return rec
 
 
+class _Cfg:
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def run_model_case(model_mod):
+    """Expert-layer inputs, outputs and routing inside the reference's own
+    decoder forward (eval mode, CPU, fp32)."""
+    cfg = _Cfg(**MODEL_CASE)
+    torch.manual_seed(0)
+    model = model_mod.CompressedMoEModel(cfg).eval()
+    layers = []
+    for i, blk in enumerate(model.layers):
+        if i < cfg.num_dense_layers:
+            continue
+        seed = 100 + i
+        seeded_init_(blk.mlp, seed=seed)
+        with torch.no_grad():
+            for v in blk.mlp.state_dict().values():
+                if v.is_floating_point():
+                    v.copy_(v.to(torch.bfloat16).float())
+        entry = dict(prefix=f"layers.{i}.mlp.", seed=seed)
+        blk.mlp.register_forward_pre_hook(lambda m, a: (a[0].to(torch.bfloat16).float(),))
+
+        def keep(m, a, out, entry=entry):
+            entry["x"] = a[0].detach().reshape(-1, a[0].shape[-1]).clone()
+            entry["y"] = out.detach().reshape(-1, out.shape[-1]).clone()
+
+        def keep_route(m, a, out, entry=entry):
+            entry["scores"] = out[0].detach().float().clone()
+            entry["ids"] = out[1].detach().to(torch.int32).clone()
+
+        blk.mlp.register_forward_hook(keep)
+        blk.mlp.router.register_forward_hook(keep_route)
+        layers.append(entry)
+    g = torch.Generator().manual_seed(5)
+    input_ids = torch.randint(0, cfg.vocab_size, (MODEL_BATCH, MODEL_SEQ), generator=g)
+    t0 = time.time()
+    with torch.no_grad():
+        logits = model(input_ids)
+    print(f"[model] decoder forward {time.time() - t0:.1f}s, logits {tuple(logits.shape)}")
+    return dict(model_cfg=dict(MODEL_CASE), batch=MODEL_BATCH, seq=MODEL_SEQ, input_ids=input_ids, layers=layers)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ETHOS_REFERENCE"),
                     help="reference checkout holding model.py (default: $ETHOS_REFERENCE)")
-    ap.add_argument("--cases", default=",".join(CASES))
+    ap.add_argument("--cases", default=",".join(list(CASES) + ["model"]))
     args = ap.parse_args()
     if not args.reference:
         ap.error("name the reference checkout with --reference or ETHOS_REFERENCE")
     sys.path.insert(0, args.reference)
+    # the reference's attention uses flash_attn when it imports (a GPU-only
+    # kernel); hiding the module selects its own matmul fallback
+    # (model.py:156-163), which runs on the CPU
+    sys.modules["flash_attn"] = None
     import model as model_mod  # the reference's model.py
     torch.set_num_threads(os.cpu_count() or 1)
     for name in args.cases.split(","):
-        rec = run_case(model_mod, name, CASES[name])
+        rec = run_model_case(model_mod) if name == "model" else run_case(model_mod, name, CASES[name])
         path = os.path.join(HERE, f"golden_{name}.pt")
         torch.save(rec, path)
         print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")

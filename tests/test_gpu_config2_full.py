@@ -69,7 +69,7 @@ def _check_experts(out, x, w, ids, p, training):
             num[name] += (got.cpu().double() - ref.double()).pow(2).sum().item()
             den[name] += ref.double().pow(2).sum().item()
         d = CFG2["d_model"]
-        y_ref.append(hacc @ p.W2[d:] / CFG2["num_routing_heads"])
+        y_ref.append(hacc @ p.W2[d:].t() / CFG2["num_routing_heads"])
     err = {n: (num[n] / den[n]) ** 0.5 for n in num}
     assert err["xp"] <= 1e-5, err
     assert err["dot"] <= 1e-3, err   # the table stores gelu(E W1^T) in fp16
