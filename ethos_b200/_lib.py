@@ -74,6 +74,16 @@ EXPORTS = {
     "ethos_adamw_step": (_I, [_P, _I, _I64, _F, _F, _F, _F, _F, _I64, _P, _P]),
     "ethos_set_wait_limit_ns": (_I, [ctypes.c_uint64]),
     "ethos_test_gelu": (_I, [_P, _P, _I64, _P]),
+    "ethos_forward_workspace_size_f32": (_SZ, [_DIMS, _I]),
+    # dims, x, w_cat, bn, eps, momentum, bn_training, keys, latents, w1, wv, y, ids, weights,
+    # save_xp, save_hacc, save_dot, save_qpre, save_bn, save_qhat, save_htab, save_gtab,
+    # workspace, workspace_bytes, dev_err, stream
+    "ethos_layer_forward_f32": (_I, [_DIMS, _P, _P, _P, _F, _F, _I] + [_P] * 15 + [_P, _SZ, _P, _P]),
+    "ethos_backward_workspace_size_f32": (_SZ, [_DIMS]),
+    # dims, bn_training, eps, dy, x, w_cat, bn, keys, latents, w1, wv, ids, weights, save_xp,
+    # save_hacc, save_dot, save_qpre, save_bn, save_qhat, htab, gtab, dx, d_latents, d_w1, d_w2,
+    # d_wq, d_bn, d_keys, workspace, workspace_bytes, dev_err, stage_events, stream
+    "ethos_layer_backward_f32": (_I, [_DIMS, _I, _F] + [_P] * 26 + [_SZ, _P, _P, _P]),
     "ethos_test_gemm_withhold": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
 }
 

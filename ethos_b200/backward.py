@@ -61,8 +61,8 @@ def layer_backward(ctx, gy):
         dist.get_world_size(comm["group"]) > 1
     timing = overlap and comm.get("log") is not None
     events = [torch.cuda.Event(enable_timing=timing), torch.cuda.Event(enable_timing=timing)] if overlap else None
-    g = ops.layer_backward(gy.reshape(-1, gy.shape[-1]), sv["x16"], pw, sv, ctx.training_bn, eps,
-                           stage_events=events)
+    bwd = ops.layer_backward_f32 if pw.fp32 else ops.layer_backward
+    g = bwd(gy.reshape(-1, gy.shape[-1]), sv["xin"], pw, sv, ctx.training_bn, eps, stage_events=events)
     if overlap:
         _overlapped_allreduce(layer, g, events)
     params = ctx.params

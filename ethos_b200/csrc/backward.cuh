@@ -324,9 +324,11 @@ __device__ __forceinline__ void unpack_b8(const uint4& u, float (&f)[8]) {
 //   dP[e] = G[e] * sum_{s in seg(e)} (a_s dhacc[t_s] + ddot_s xp[t_s])
 // reading the bf16 token rows gx[t] = [dhacc | xp] (2 KB each, L2-resident)
 // and writing bf16 (operand of the dE / dW1 GEMMs).  Experts without
-// selections get zeros.
+// selections get zeros.  `total` is the device count of sorted selections
+// (k_scan_sums), so segments never reach past the entries k_scatter_experts
+// wrote.
 __global__ void __launch_bounds__(256, 3) k_expert_dP(const int* __restrict__ offs, const int* __restrict__ perm,
-                                                    int total, const float* __restrict__ ca,
+                                                    const int* __restrict__ total, const float* __restrict__ ca,
                                                     const float* __restrict__ cd, const __nv_bfloat16* __restrict__ gx,
                                                     const __half* __restrict__ gtab, __nv_bfloat16* __restrict__ dP,
                                                     int N, int R) {
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(256, 3) k_expert_dP(const int* __restrict__ of
   const int nw = (gridDim.x * blockDim.x) >> 5;
   for (int e = gw; e < N; e += nw) {
     const int s0 = offs[e];
-    const int s1 = e + 1 < N ? offs[e + 1] : total;
+    const int s1 = e + 1 < N ? offs[e + 1] : *total;  // selections with a valid id
     float acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = 0.f;
@@ -431,14 +433,17 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
   for (int th = gw; th < T * H; th += nw) {
     const int t = th / H, h = th - t * H;
     const int64_t o = static_cast<int64_t>(th) * TOPK;
-    const bool act = lane < TOPK;
+    // a selection whose id lies outside [0, K*K) (k_count_experts reports
+    // it) contributes nothing and reads key row 0
+    const int id_in = lane < TOPK ? ids[o + lane] : 0;
+    const bool act = lane < TOPK && static_cast<unsigned>(id_in) < static_cast<unsigned>(K * K);
     const float wr = act ? w[o + lane] : 0.f;
     const float dwr = act ? dw[o + lane] : 0.f;
     float s = wr * dwr;
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     const float dg = act ? wr * (dwr - s) : 0.f;
-    const int id = act ? ids[o + lane] : 0;
+    const int id = act ? id_in : 0;
     const int i1 = id / K, i2 = id - i1 * K;
     // dS scatter: lanes with the same key combine (each lane walks the lanes
     // of its key group, the warp as long as the largest group), the lowest

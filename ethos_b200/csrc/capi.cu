@@ -19,6 +19,7 @@
 #include "gemm2sm.cuh"
 #include "router.cuh"
 #include "optim.cuh"
+#include "fp32.cuh"
 
 using namespace ethos;
 
@@ -1167,7 +1168,7 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
   }
   // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
   count_launch();
-  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, T * R, s.ca, s.cd, s.gx, gtab_, s.dP, N, R);
+  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, s.total, s.ca, s.cd, s.gx, gtab_, s.dP, N, R);
   if ((st = launch_status()) != ETHOS_OK) return st;
   // (7) dE = dP W1       (W1 read in place, MN-major)
   {
@@ -1307,6 +1308,582 @@ int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t 
   k_adamw<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(num_tensors)), threads, 0,
             static_cast<cudaStream_t>(stream)>>>(tensors, s);
   return launch_status();
+}
+
+}  // extern "C"
+
+// ===================================================== fp32 arithmetic path --
+namespace {
+
+// Extra shape rules of the fp32 path: its score GEMMs need d_query / 2 to be
+// a multiple of 128 (their N tile), and the padded key count Kp below.
+int check_dims_f32(const ethos_dims* d) {
+  const int st = check_dims_impl(d);
+  if (st != ETHOS_OK) return st;
+  if ((d->d_query / 2) % 128 != 0) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+  return ETHOS_OK;
+}
+
+// Sub-key count rounded up to the GEMM's 128-column N tile (score rows are
+// Kp wide; the extra key rows are zero and never selected).
+int64_t padded_keys(const ethos_dims& d) { return (d.num_sub_keys + 127) / 128 * 128; }
+
+// Split an fp32 [rows, cols] matrix (row pitch lds) into bf16 segments (see
+// k_split_bf16).
+int launch_split(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, int64_t ldd,
+                 int64_t seg_off, int nseg, int lo_mask, cudaStream_t stream, const DeviceInfo& dev) {
+  const int tx = 128;
+  const int gx = (cols + tx - 1) / tx;
+  int64_t gy = (static_cast<int64_t>(dev.sm_count) * 16) / gx;
+  if (gy < 1) gy = 1;
+  if (gy > rows) gy = rows;
+  if (gy > 65535) gy = 65535;
+  count_launch();
+  k_split_bf16<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), tx, 0, stream>>>(
+      src, rows, cols, lds, dst, ldd, seg_off, nseg, lo_mask);
+  return launch_status();
+}
+
+// Separate hi / lo arrays of an fp32 [rows, cols] matrix: dst holds hi
+// [rows][cols] then lo [rows][cols].
+int split2(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, cudaStream_t stream,
+           const DeviceInfo& dev) {
+  return launch_split(src, rows, cols, lds, dst, cols, rows * cols, 2, 2, stream, dev);
+}
+
+// The K-concatenated operands of one fp32 GEMM, row-major [rows][3 * cols]:
+// A = [hi | lo | hi] (lo_mask 2), B = [hi | hi | lo] (lo_mask 4).
+int split3(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, bool as_b,
+           cudaStream_t stream, const DeviceInfo& dev) {
+  return launch_split(src, rows, cols, lds, dst, 3 * static_cast<int64_t>(cols), cols, 3, as_b ? 4 : 2, stream,
+                      dev);
+}
+
+// A split operand: hi and lo bf16 arrays of one layout (row pitch ld,
+// K-major or MN-major as in GemmOperand).
+struct SplitOperand {
+  const __nv_bfloat16* hi;
+  const __nv_bfloat16* lo;
+  int64_t ld;
+  bool mn_major;
+};
+
+// D (=|+=) scale * A B^T in fp32 from split operands: hi*hi, then lo*hi and
+// hi*lo accumulated.  atomic: all three reduce into D with fp32 atomics
+// (split-K allowed; D pre-initialised by the caller); else the first stores
+// and the other two add.
+int gemm_split(const SplitOperand& a, const SplitOperand& b, int M, int N, int K, float* out, int64_t ldo,
+               float scale, bool atomic, int* err, cudaStream_t stream, const DeviceInfo& dev) {
+  const GemmOperand A[3] = {{a.hi, a.ld, a.mn_major}, {a.lo, a.ld, a.mn_major}, {a.hi, a.ld, a.mn_major}};
+  const GemmOperand B[3] = {{b.hi, b.ld, b.mn_major}, {b.hi, b.ld, b.mn_major}, {b.lo, b.ld, b.mn_major}};
+  const int ks = atomic ? auto_ksplit(M, N, K, dev) : 1;
+  for (int i = 0; i < 3; ++i) {
+    int st;
+    if (atomic) {
+      EpiAtomicF32 e;
+      e.out = out;
+      e.ldo = ldo;
+      e.M = M;
+      e.scale = scale;
+      st = gemm(A[i], B[i], M, N, K, ks, e, err, stream, dev);
+    } else {
+      EpiStoreF32 e;
+      e.out = out;
+      e.ldo = ldo;
+      e.M = M;
+      e.scale = scale;
+      e.accumulate = i > 0 ? 1 : 0;
+      st = gemm(A[i], B[i], M, N, K, 1, e, err, stream, dev);
+    }
+    if (st != ETHOS_OK) return st;
+  }
+  return ETHOS_OK;
+}
+
+dim3 rows_grid(int cols, int64_t rows, int threads, const DeviceInfo& dev) {
+  const int gx = (cols + threads - 1) / threads;
+  int64_t gy = static_cast<int64_t>(dev.sm_count) * 8 / gx;
+  if (gy < 1) gy = 1;
+  if (gy > rows) gy = rows;
+  if (gy > 65535) gy = 65535;
+  return dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+}
+
+int warp_blocks(int64_t items, const DeviceInfo& dev) {
+  int64_t b = (items + 7) / 8;  // 8 warps per 256-thread block
+  const int64_t cap = static_cast<int64_t>(dev.sm_count) * 16;
+  if (b > cap) b = cap;
+  return b < 1 ? 1 : static_cast<int>(b);
+}
+
+struct Fwd32Scratch {
+  __nv_bfloat16* x3;      // [T][3d]
+  __nv_bfloat16* w3;      // [ncat][3d]
+  float* qpre;            // [T][HQ]
+  float* xp;              // [T][dh]
+  float2* colp;           // [HQ]
+  float* save_bn;         // [2][HQ]
+  float* bn_part;
+  float* qhat;            // [2][H][T][half]
+  __nv_bfloat16* qhat_s;  // hi, lo of qhat
+  __nv_bfloat16* keys_s;  // hi [2][Kp][half], lo [2][Kp][half]
+  float* scores;          // [2][H*T][Kp]
+  __nv_bfloat16* e_s;     // hi, lo [N][dl]
+  __nv_bfloat16* w1_s;    // hi, lo [dh][dl]
+  float* tab;             // [N][dh]
+  float* hacc;            // [T][dh]
+  __nv_bfloat16* hacc_s;  // hi, lo [T][dh]
+  __nv_bfloat16* wv_s;    // hi, lo [d][dh]
+  float* dot;             // [T][R]
+  int slabs;
+};
+
+// Scratch of the fp32 forward; a `have_*` flag means the caller passes that
+// buffer (save outputs), so no scratch is carved for it.
+void carve_forward_f32(Carve& c, const ethos_dims& d, int bn_training, bool experts, bool have_qpre, bool have_xp,
+                       bool have_bn, bool have_qhat, bool have_tab, bool have_hacc, bool have_dot, Fwd32Scratch* s) {
+  const int64_t T = d.tokens, D = d.d_model, H = d.num_heads, HQ = H * d.d_query, half = d.d_query / 2;
+  const int64_t dh = d.d_hidden, N = d.num_experts, Kp = padded_keys(d), R = H * d.top_k;
+  const int64_t ncat = experts ? HQ + dh : HQ;
+  s->x3 = c.take<__nv_bfloat16>(static_cast<size_t>(T * 3 * D));
+  s->w3 = c.take<__nv_bfloat16>(static_cast<size_t>(ncat * 3 * D));
+  s->qpre = have_qpre ? nullptr : c.take<float>(static_cast<size_t>(T * HQ));
+  s->xp = (!experts || have_xp) ? nullptr : c.take<float>(static_cast<size_t>(T * dh));
+  s->colp = c.take<float2>(static_cast<size_t>(HQ));
+  s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
+  s->save_bn = (bn_training && !have_bn) ? c.take<float>(static_cast<size_t>(2 * HQ)) : nullptr;
+  s->bn_part = bn_training ? c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2) : nullptr;
+  s->qhat = have_qhat ? nullptr : c.take<float>(static_cast<size_t>(2 * H * T * half));
+  s->qhat_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * 2 * H * T * half));
+  s->keys_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * 2 * Kp * half));
+  s->scores = c.take<float>(static_cast<size_t>(2 * H * T * Kp));
+  if (experts) {
+    s->e_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * N * d.d_latent));
+    s->w1_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * dh * d.d_latent));
+    s->tab = have_tab ? nullptr : c.take<float>(static_cast<size_t>(N * dh));
+    s->hacc = have_hacc ? nullptr : c.take<float>(static_cast<size_t>(T * dh));
+    s->hacc_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * T * dh));
+    s->wv_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * D * dh));
+    s->dot = have_dot ? nullptr : c.take<float>(static_cast<size_t>(T * R));
+  } else {
+    s->e_s = s->w1_s = s->hacc_s = s->wv_s = nullptr;
+    s->tab = s->hacc = s->dot = nullptr;
+  }
+}
+
+// Pre-activations of the expert table in fp32 (E @ W1^T on split operands),
+// then GELU in place (and its derivative into g when given).
+int build_table_f32(const ethos_dims& d, const float* latents, const float* w1, __nv_bfloat16* e_s,
+                    __nv_bfloat16* w1_s, float* tab, float* g, int* err, cudaStream_t stream, const DeviceInfo& dev) {
+  const int64_t N = d.num_experts, dl = d.d_latent, dh = d.d_hidden;
+  int st;
+  if ((st = split2(latents, N, static_cast<int>(dl), dl, e_s, stream, dev)) != ETHOS_OK) return st;
+  if ((st = split2(w1, dh, static_cast<int>(dl), dl, w1_s, stream, dev)) != ETHOS_OK) return st;
+  const SplitOperand a{e_s, e_s + N * dl, dl, false};
+  const SplitOperand b{w1_s, w1_s + dh * dl, dl, false};
+  if ((st = gemm_split(a, b, static_cast<int>(N), static_cast<int>(dh), static_cast<int>(dl), tab, dh, 1.0f, false,
+                       err, stream, dev)) != ETHOS_OK)
+    return st;
+  const int64_t n = N * dh;
+  int64_t blocks = (n / 2 + 255) / 256;
+  if (blocks > dev.sm_count * 16) blocks = dev.sm_count * 16;
+  count_launch();
+  k_gelu_table_f32<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(tab, g, n);
+  return launch_status();
+}
+
+struct Bwd32Scratch {
+  __nv_bfloat16* dy_s;    // hi, lo [T][d]
+  __nv_bfloat16* wv_s;    // hi, lo [d][dh]
+  float* dhacc;           // [T][dh]
+  __nv_bfloat16* hacc_s;  // hi, lo [T][dh]
+  __nv_bfloat16* e_s;     // hi, lo [N][dl]
+  __nv_bfloat16* w1_s;    // hi, lo [dh][dl]
+  float* tab;             // [N][dh] (when the forward kept none)
+  float* gtab;            // [N][dh]
+  float* dw;              // [T][R]
+  float* ca;
+  float* cd;
+  float* du;              // [T][LDU] = [dq | dxp]
+  __nv_bfloat16* du_s;    // hi, lo [T][LDU]
+  int* cnt;
+  int* offs;
+  int* cursor;
+  int* bsums;
+  int* total;
+  int* perm;
+  float* dP;              // [N][dh]
+  __nv_bfloat16* dP_s;    // hi, lo
+  float* dqhat;           // [T][HQ]
+  float* dS;              // [2][H*T][K]
+  __nv_bfloat16* dS_s;    // hi, lo
+  __nv_bfloat16* qhat_s;  // hi, lo [2][H*T][half]
+  float* part;
+  float* coef;
+  float* stats;
+  __nv_bfloat16* wcat_s;  // hi, lo [ncat][d]
+  __nv_bfloat16* x_s;     // hi, lo [T][d]
+  int slabs;
+};
+
+void carve_backward_f32(Carve& c, const ethos_dims& d, bool have_tables, Bwd32Scratch* s) {
+  const int64_t T = d.tokens, D = d.d_model, H = d.num_heads, HQ = H * d.d_query, half = d.d_query / 2;
+  const int64_t dh = d.d_hidden, dl = d.d_latent, N = d.num_experts, K = d.num_sub_keys, R = H * d.top_k;
+  const int64_t LDU = HQ + dh;
+  s->dy_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * T * D));
+  s->wv_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * D * dh));
+  s->dhacc = c.take<float>(static_cast<size_t>(T * dh));
+  s->hacc_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * T * dh));
+  s->e_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * N * dl));
+  s->w1_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * dh * dl));
+  s->tab = have_tables ? nullptr : c.take<float>(static_cast<size_t>(N * dh));
+  s->gtab = have_tables ? nullptr : c.take<float>(static_cast<size_t>(N * dh));
+  s->dw = c.take<float>(static_cast<size_t>(T * R));
+  s->ca = c.take<float>(static_cast<size_t>(T * R));
+  s->cd = c.take<float>(static_cast<size_t>(T * R));
+  s->du = c.take<float>(static_cast<size_t>(T * LDU));
+  s->du_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * T * LDU));
+  s->cnt = c.take<int>(static_cast<size_t>(N));
+  s->offs = c.take<int>(static_cast<size_t>(N));
+  s->cursor = c.take<int>(static_cast<size_t>(N));
+  s->bsums = c.take<int>(1024);
+  s->total = c.take<int>(1);
+  s->perm = c.take<int>(static_cast<size_t>(T * R));
+  s->dP = c.take<float>(static_cast<size_t>(N * dh));
+  s->dP_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * N * dh));
+  s->dqhat = c.take<float>(static_cast<size_t>(T * HQ));
+  s->dS = c.take<float>(static_cast<size_t>(2 * H * T * K));
+  s->dS_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * 2 * H * T * K));
+  s->qhat_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * 2 * H * T * half));
+  s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
+  s->part = c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2);
+  s->coef = c.take<float>(static_cast<size_t>(4 * HQ));
+  s->stats = c.take<float>(static_cast<size_t>(2 * HQ));
+  s->wcat_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * LDU * D));
+  s->x_s = c.take<__nv_bfloat16>(static_cast<size_t>(2 * T * D));
+}
+
+template <int TOPK>
+int launch_topk_f32(const float* scores, int64_t ldk, const ethos_dims& d, int32_t* ids, float* w,
+                    cudaStream_t stream, const DeviceInfo& dev) {
+  count_launch();
+  k_topk_f32<TOPK><<<warp_blocks(d.num_heads * d.tokens, dev), 256, 0, stream>>>(
+      scores, ldk, static_cast<int>(d.tokens), static_cast<int>(d.num_heads), static_cast<int>(d.num_sub_keys), ids,
+      w);
+  return launch_status();
+}
+
+template <int TOPK>
+int launch_router_bwd_f32(const ethos_dims& d, const int32_t* ids, const float* w, const float* dw,
+                          const float* keys, float* dqhat, float* dS, cudaStream_t stream, const DeviceInfo& dev) {
+  count_launch();
+  k_router_bwd_f32<TOPK><<<warp_blocks(d.num_heads * d.tokens, dev), 256, 0, stream>>>(
+      ids, w, dw, keys, dqhat, dS, static_cast<int>(d.tokens), static_cast<int>(d.num_heads),
+      static_cast<int>(d.num_sub_keys), static_cast<int>(d.d_query));
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ethos_forward_workspace_size_f32(const ethos_dims* dims, int bn_training) {
+  if (check_dims_f32(dims) != ETHOS_OK) return 0;
+  Carve c{nullptr, 0, 0};
+  Fwd32Scratch s;
+  carve_forward_f32(c, *dims, bn_training, true, false, false, false, false, false, false, false, &s);
+  return c.off + 256;
+}
+
+int ethos_layer_forward_f32(const ethos_dims* dims, const float* x, const float* w_cat, float* bn, float bn_eps,
+                            float bn_momentum, int bn_training, const float* keys, const float* latents,
+                            const float* w1, const float* wv, float* y, int32_t* ids, float* weights,
+                            float* save_xp, float* save_hacc, float* save_dot, float* save_qpre, float* save_bn,
+                            float* save_qhat, float* save_htab, float* save_gtab, void* workspace,
+                            size_t workspace_bytes, int* dev_err, void* stream) {
+  int st = check_dims_f32(dims);
+  if (st != ETHOS_OK) return st;
+  const bool experts = y != nullptr;
+  if (!x || !w_cat || !bn || !keys || !ids || !weights || !workspace || !dev_err) return ETHOS_ERR_INVALID_ARG;
+  if (experts && (!latents || !w1 || !wv)) return ETHOS_ERR_INVALID_ARG;
+  if (save_gtab != nullptr && save_htab == nullptr) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w_cat) || !aligned16(keys) || (experts && (!aligned16(latents) ||
+      !aligned16(w1) || !aligned16(wv) || !aligned16(y))))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  const ethos_dims& d = *dims;
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  Fwd32Scratch s;
+  carve_forward_f32(c, d, bn_training, experts, save_qpre != nullptr, save_xp != nullptr, save_bn != nullptr,
+                    save_qhat != nullptr, save_htab != nullptr, save_hacc != nullptr, save_dot != nullptr, &s);
+  if (c.off > workspace_bytes) return ETHOS_ERR_WORKSPACE;
+  cudaStream_t sm = static_cast<cudaStream_t>(stream);
+  const int T = static_cast<int>(d.tokens), D = static_cast<int>(d.d_model), H = static_cast<int>(d.num_heads);
+  const int dq = static_cast<int>(d.d_query), HQ = H * dq, half = dq / 2, dh = static_cast<int>(d.d_hidden);
+  const int K = static_cast<int>(d.num_sub_keys), R = H * static_cast<int>(d.top_k);
+  const int N = static_cast<int>(d.num_experts);
+  const int64_t Kp = padded_keys(d), HT = static_cast<int64_t>(H) * T;
+  const int ncat = experts ? HQ + dh : HQ;
+  float* qpre = save_qpre ? save_qpre : s.qpre;
+  float* xp = experts ? (save_xp ? save_xp : s.xp) : nullptr;
+  float* sbn = save_bn ? save_bn : s.save_bn;
+  float* qhat = save_qhat ? save_qhat : s.qhat;
+  const int cb = 256;
+
+  // (1) queries and x_proj: one GEMM on K-concatenated split operands, the
+  //     bias added in the epilogue (model.py:215, 326)
+  if ((st = split3(x, T, D, D, s.x3, false, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split3(w_cat, ncat, D, D, s.w3, true, sm, *dev)) != ETHOS_OK) return st;
+  if (!bn_training) {
+    count_launch();
+    k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, 1, s.colp);
+  }
+  {
+    CUtensorMap tm_x, tm_w;
+    if ((st = make_tmap_bf16(&tm_x, s.x3, T, 3 * D, 128)) != ETHOS_OK) return st;
+    if ((st = make_tmap_bf16(&tm_w, s.w3, ncat, 3 * D, G2_BN / 2)) != ETHOS_OK) return st;
+    EpiProj epi;
+    epi.M = T;
+    epi.HQ = HQ;
+    epi.dq = dq;
+    epi.dh = dh;
+    epi.mode = 1;
+    epi.bias = bn;
+    epi.colp = s.colp;
+    epi.qs = nullptr;
+    epi.qpre = qpre;
+    epi.xp = xp;
+    if ((st = launch_gemm2sm(tm_x, tm_w, T, ncat, 3 * D, epi, dev_err, sm, *dev)) != ETHOS_OK) return st;
+  }
+  // (2) BatchNorm (model.py:216): batch statistics and running-stat update in
+  //     training mode, running statistics in eval mode
+  if (bn_training) {
+    dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+    count_launch();
+    k_bn_partial<<<grid_p, cb, 0, sm>>>(qpre, T, HQ, s.bn_part);
+    count_launch();
+    k_bn_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(qpre, s.bn_part, T, HQ, s.slabs, bn + HQ, bn + 2 * HQ,
+                                                     bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, sbn, s.colp);
+  }
+  count_launch();
+  k_bn_apply_f32<<<rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(qpre, s.colp, T, H, dq, qhat);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  // (3) sub-key scores of both halves (model.py:217-221), then top-k, grid
+  //     top-k, softmax and id decode (model.py:224-245)
+  if ((st = split2(qhat, 2 * HT, half, half, s.qhat_s, sm, *dev)) != ETHOS_OK) return st;
+  if (cudaMemsetAsync(s.keys_s, 0, sizeof(__nv_bfloat16) * 2 * 2 * Kp * half, sm) != cudaSuccess)
+    return ETHOS_ERR_CUDA;
+  for (int p = 0; p < 2; ++p) {
+    if ((st = launch_split(keys + static_cast<int64_t>(p) * K * half, K, half, half,
+                           s.keys_s + static_cast<int64_t>(p) * Kp * half, half, 2 * Kp * half, 2, 2, sm, *dev)) !=
+        ETHOS_OK)
+      return st;
+  }
+  const int64_t qlo = 2 * HT * half;
+  for (int p = 0; p < 2; ++p) {
+    const SplitOperand a{s.qhat_s + p * HT * half, s.qhat_s + qlo + p * HT * half, half, false};
+    const SplitOperand b{s.keys_s + p * Kp * half, s.keys_s + 2 * Kp * half + p * Kp * half, half, false};
+    if ((st = gemm_split(a, b, static_cast<int>(HT), static_cast<int>(Kp), half, s.scores + p * HT * Kp, Kp, 1.0f,
+                         false, dev_err, sm, *dev)) != ETHOS_OK)
+      return st;
+  }
+  switch (d.top_k) {
+    case 4: st = launch_topk_f32<4>(s.scores, Kp, d, ids, weights, sm, *dev); break;
+    case 8: st = launch_topk_f32<8>(s.scores, Kp, d, ids, weights, sm, *dev); break;
+    default: st = launch_topk_f32<16>(s.scores, Kp, d, ids, weights, sm, *dev); break;
+  }
+  if (st != ETHOS_OK || !experts) return st;
+  // (4) expert table H = gelu(E W1^T) in fp32, once per expert (model.py:323)
+  float* tab = save_htab ? save_htab : s.tab;
+  if ((st = build_table_f32(d, latents, w1, s.e_s, s.w1_s, tab, save_gtab, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  // (5) per token: dot, activation, weighted hidden sum (model.py:320-338)
+  float* hacc = save_hacc ? save_hacc : s.hacc;
+  float* dot = save_dot ? save_dot : s.dot;
+  count_launch();
+  k_gather_f32<<<warp_blocks(T, *dev), 256, 0, sm>>>(tab, ids, weights, xp, hacc, dot, T, R, N, dev_err);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  // (6) y = hacc W_v^T / H (model.py:332-341)
+  if ((st = split2(hacc, T, dh, dh, s.hacc_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split2(wv, D, dh, dh, s.wv_s, sm, *dev)) != ETHOS_OK) return st;
+  const SplitOperand a{s.hacc_s, s.hacc_s + static_cast<int64_t>(T) * dh, dh, false};
+  const SplitOperand b{s.wv_s, s.wv_s + static_cast<int64_t>(D) * dh, dh, false};
+  return gemm_split(a, b, T, D, dh, y, D, 1.0f / static_cast<float>(H), false, dev_err, sm, *dev);
+}
+
+size_t ethos_backward_workspace_size_f32(const ethos_dims* dims) {
+  if (check_dims_f32(dims) != ETHOS_OK) return 0;
+  Carve c{nullptr, 0, 0};
+  Bwd32Scratch s;
+  carve_backward_f32(c, *dims, false, &s);
+  return c.off + 256;
+}
+
+int ethos_layer_backward_f32(const ethos_dims* dims, int bn_training, float bn_eps, const float* dy, const float* x,
+                             const float* w_cat, const float* bn, const float* keys, const float* latents,
+                             const float* w1, const float* wv, const int32_t* ids, const float* weights,
+                             const float* save_xp, const float* save_hacc, const float* save_dot,
+                             const float* save_qpre, const float* save_bn, const float* save_qhat, const float* htab,
+                             const float* gtab, float* dx, float* d_latents, float* d_w1, float* d_w2, float* d_wq,
+                             float* d_bn, float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
+                             void* const* stage_events, void* stream) {
+  int st = check_dims_f32(dims);
+  if (st != ETHOS_OK) return st;
+  if (!dy || !x || !w_cat || !bn || !keys || !latents || !w1 || !wv || !ids || !weights || !save_xp ||
+      !save_hacc || !save_dot || !save_qpre || !save_qhat || !dx || !d_latents || !d_w1 || !d_w2 || !d_wq ||
+      !d_bn || !d_keys || !workspace || !dev_err)
+    return ETHOS_ERR_INVALID_ARG;
+  if (bn_training && !save_bn) return ETHOS_ERR_INVALID_ARG;
+  if ((htab == nullptr) != (gtab == nullptr)) return ETHOS_ERR_INVALID_ARG;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  const ethos_dims& d = *dims;
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  Bwd32Scratch s;
+  carve_backward_f32(c, d, htab != nullptr, &s);
+  if (c.off > workspace_bytes) return ETHOS_ERR_WORKSPACE;
+  cudaStream_t sm = static_cast<cudaStream_t>(stream);
+  const int T = static_cast<int>(d.tokens), D = static_cast<int>(d.d_model), N = static_cast<int>(d.num_experts);
+  const int H = static_cast<int>(d.num_heads), R = static_cast<int>(d.num_heads * d.top_k);
+  const int dq = static_cast<int>(d.d_query), HQ = H * dq, K = static_cast<int>(d.num_sub_keys), half = dq / 2;
+  const int dh = static_cast<int>(d.d_hidden), dl = static_cast<int>(d.d_latent);
+  const int LDU = HQ + dh;
+  const int64_t HT = static_cast<int64_t>(H) * T;
+  const float invH = 1.0f / static_cast<float>(H);
+  const int cb = 256;
+  const int eblocks = dev->sm_count * 8;
+
+  // accumulated outputs and the dense score gradient start at zero
+  if (cudaMemsetAsync(d_w1, 0, sizeof(float) * dh * dl, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(d_w2, 0, sizeof(float) * 2 * D * dh, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(d_keys, 0, sizeof(float) * 2 * K * half, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(s.cnt, 0, sizeof(int) * N, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(s.dS, 0, sizeof(float) * 2 * HT * K, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+
+  // (1) dhacc = dy W_v / H (W_v = net.2.weight[d:] read as [K = d][N = dh])
+  if ((st = split2(dy, T, D, D, s.dy_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split2(wv, D, dh, dh, s.wv_s, sm, *dev)) != ETHOS_OK) return st;
+  const SplitOperand dyK{s.dy_s, s.dy_s + static_cast<int64_t>(T) * D, D, false};
+  const SplitOperand dyM{s.dy_s, s.dy_s + static_cast<int64_t>(T) * D, D, true};
+  if ((st = gemm_split(dyK, SplitOperand{s.wv_s, s.wv_s + static_cast<int64_t>(D) * dh, dh, true}, T, dh, D, s.dhacc,
+                       dh, invH, false, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  // (2) dW_v = dy^T hacc / H -> d_w2[d:]
+  if ((st = split2(save_hacc, T, dh, dh, s.hacc_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = gemm_split(dyM, SplitOperand{s.hacc_s, s.hacc_s + static_cast<int64_t>(T) * dh, dh, true}, D, dh, T,
+                       d_w2 + static_cast<int64_t>(D) * dh, dh, invH, true, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  // (3) expert tables H and G = gelu'(E W1^T), unless the forward kept them
+  if ((st = split2(latents, N, dl, dl, s.e_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split2(w1, dh, dl, dl, s.w1_s, sm, *dev)) != ETHOS_OK) return st;
+  const float* tab = htab;
+  const float* gt = gtab;
+  if (htab == nullptr) {
+    if ((st = build_table_f32(d, latents, w1, s.e_s, s.w1_s, s.tab, s.gtab, dev_err, sm, *dev)) != ETHOS_OK)
+      return st;
+    tab = s.tab;
+    gt = s.gtab;
+  }
+  // (4) per token: dw, a, ddot per selection; dxp into du[:, HQ:]
+  count_launch();
+  k_bwd_token_f32<<<warp_blocks(T, *dev), 256, 0, sm>>>(tab, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.du,
+                                                         LDU, HQ, T, R, N, dev_err);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  // (5) selections grouped by expert (counting sort)
+  {
+    const int64_t nsel = static_cast<int64_t>(T) * R;
+    const int nblk = (N + 1023) / 1024;
+    if (nblk > 1024) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+    count_launch();
+    k_count_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cnt, dev_err);
+    count_launch();
+    k_scan_blocks<<<nblk, 1024, 0, sm>>>(s.cnt, N, s.offs, s.bsums);
+    count_launch();
+    k_scan_sums<<<1, 1024, 0, sm>>>(s.bsums, nblk, s.total);
+    count_launch();
+    k_scan_add<<<nblk, 1024, 0, sm>>>(s.offs, N, s.bsums, s.cursor);
+    count_launch();
+    k_scatter_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cursor, s.perm);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
+  count_launch();
+  k_expert_dP_f32<<<warp_blocks(N, *dev), 256, 0, sm>>>(s.offs, s.perm, s.total, s.ca, s.cd, s.dhacc, save_xp, gt,
+                                                         s.dP, N, R);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  if ((st = split2(s.dP, N, dh, dh, s.dP_s, sm, *dev)) != ETHOS_OK) return st;
+  // (7) dE = dP W1 (W1 [dh][dl] read as [K = dh][N = dl])
+  const int64_t ndh = static_cast<int64_t>(N) * dh;
+  if ((st = gemm_split(SplitOperand{s.dP_s, s.dP_s + ndh, dh, false},
+                       SplitOperand{s.w1_s, s.w1_s + static_cast<int64_t>(dh) * dl, dl, true}, N, dl, dh, d_latents,
+                       dl, 1.0f, false, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  // (8) dW1 = dP^T E (split-K over the experts)
+  if ((st = gemm_split(SplitOperand{s.dP_s, s.dP_s + ndh, dh, true},
+                       SplitOperand{s.e_s, s.e_s + static_cast<int64_t>(N) * dl, dl, true}, dh, dl, N, d_w1, dl, 1.0f,
+                       true, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  mark(stage_events, ETHOS_BWD_STAGE_EXPERTS, sm);  // d_latents, d_w1 final
+  // (9) router: softmax backward, dq^ and the dense score gradient dS
+  switch (d.top_k) {
+    case 4: st = launch_router_bwd_f32<4>(d, ids, weights, s.dw, keys, s.dqhat, s.dS, sm, *dev); break;
+    case 8: st = launch_router_bwd_f32<8>(d, ids, weights, s.dw, keys, s.dqhat, s.dS, sm, *dev); break;
+    default: st = launch_router_bwd_f32<16>(d, ids, weights, s.dw, keys, s.dqhat, s.dS, sm, *dev); break;
+  }
+  if (st != ETHOS_OK) return st;
+  // (10) dK_p = dS_p^T q^_p over all (head, token) rows
+  if ((st = split2(s.dS, 2 * HT, K, K, s.dS_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split2(save_qhat, 2 * HT, half, half, s.qhat_s, sm, *dev)) != ETHOS_OK) return st;
+  for (int p = 0; p < 2; ++p) {
+    const SplitOperand a{s.dS_s + p * HT * K, s.dS_s + 2 * HT * K + p * HT * K, K, true};
+    const SplitOperand b{s.qhat_s + p * HT * half, s.qhat_s + 2 * HT * half + p * HT * half, half, true};
+    if ((st = gemm_split(a, b, K, half, static_cast<int>(HT), d_keys + static_cast<int64_t>(p) * K * half, half,
+                         1.0f, true, dev_err, sm, *dev)) != ETHOS_OK)
+      return st;
+  }
+  // (11) BatchNorm backward -> dq into du[:, :HQ], dbias, dgamma, dbeta
+  {
+    const float* mean = save_bn;
+    const float* invstd = save_bn ? save_bn + HQ : nullptr;
+    if (!bn_training) {
+      count_launch();
+      k_bn_eval_stats<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, s.stats, s.stats + HQ);
+      mean = s.stats;
+      invstd = s.stats + HQ;
+    }
+    dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+    count_launch();
+    k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, T, HQ, s.part);
+    count_launch();
+    k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, mean, invstd,
+                                                        d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
+    count_launch();
+    k_bn_bwd_apply_f32<<<rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(s.dqhat, save_qpre,
+                                                                  reinterpret_cast<const float4*>(s.coef), T, HQ,
+                                                                  s.du, LDU);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  if ((st = split2(s.du, T, LDU, LDU, s.du_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split2(w_cat, LDU, D, D, s.wcat_s, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split2(x, T, D, D, s.x_s, sm, *dev)) != ETHOS_OK) return st;
+  const int64_t tlu = static_cast<int64_t>(T) * LDU, td = static_cast<int64_t>(T) * D;
+  // (12) dx = du W_cat (W_cat [ncat][d] read as [K = ncat][N = d])
+  if ((st = gemm_split(SplitOperand{s.du_s, s.du_s + tlu, LDU, false},
+                       SplitOperand{s.wcat_s, s.wcat_s + static_cast<int64_t>(LDU) * D, D, true}, T, D, LDU, dx, D,
+                       1.0f, false, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  // (13) dWq = dq^T x   [HQ, d]
+  if ((st = gemm_split(SplitOperand{s.du_s, s.du_s + tlu, LDU, true}, SplitOperand{s.x_s, s.x_s + td, D, true}, HQ, D,
+                       T, d_wq, D, 1.0f, false, dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  // (14) dW_u = x^T dxp -> d_w2[:d]   [d, dh]
+  if ((st = gemm_split(SplitOperand{s.x_s, s.x_s + td, D, true},
+                       SplitOperand{s.du_s + HQ, s.du_s + tlu + HQ, LDU, true}, D, dh, T, d_w2, dh, 1.0f, true,
+                       dev_err, sm, *dev)) != ETHOS_OK)
+    return st;
+  mark(stage_events, ETHOS_BWD_STAGE_END, sm);
+  return ETHOS_OK;
 }
 
 }  // extern "C"

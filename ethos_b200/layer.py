@@ -105,8 +105,12 @@ class ProductKeyRouter(nn.Module):
         pw = layer.packed(x_flat.device)
         eps, mom = self._bn_eps_momentum()
         training = self._bn_training()
-        x16 = x_flat.detach().to(torch.bfloat16).contiguous()
-        w, ids = ops.router_forward(x16, pw, training, eps, mom)
+        if pw.fp32:
+            x32 = x_flat.detach().to(torch.float32).contiguous()
+            w, ids = ops.router_forward_f32(x32, pw, training, eps, mom)
+        else:
+            x16 = x_flat.detach().to(torch.bfloat16).contiguous()
+            w, ids = ops.router_forward(x16, pw, training, eps, mom)
         if training:
             self._write_back_running(pw.bn)
         return w.to(x_flat.dtype), ids.to(torch.int64)
@@ -114,6 +118,17 @@ class ProductKeyRouter(nn.Module):
 
 def _bf16(t):
     return t.detach().to(torch.bfloat16).contiguous()
+
+
+def _f32(t):
+    return t.detach().to(torch.float32).contiguous()
+
+
+def _fp32_arithmetic(module):
+    """The layer computes in fp32 when its parameters are fp32 (the
+    reference's model.py:208-343 then runs in fp32 too); bf16 or fp16
+    parameters select the bf16 tensor-core path."""
+    return next(module.parameters()).dtype == torch.float32
 
 
 def _check_token_count(tokens, bn_training, dq):
@@ -138,9 +153,18 @@ class _RouterOnly:
         dims = dict(d_model=r.d_model, num_experts=r.num_experts, num_sub_keys=r.num_sub_keys,
                     top_k=r.top_k, num_heads=r.num_heads, d_latent=128, d_hidden=512,
                     d_query=r.d_query)
+        if _fp32_arithmetic(r):
+            w_cat = torch.cat([_f32(m.weight) for m in r.query_projs], 0)
+            return ops.PackedWeights(w_cat=w_cat, key_cat=_keys_f32(r), latents=None, w1=None, wv=None,
+                                     bn=r._bn_block(), dims=dims, fp32=True)
         w_cat = torch.cat([_bf16(m.weight) for m in r.query_projs], 0)
         return ops.PackedWeights(w_cat=w_cat, key_cat=_key_cat(r), latents=None, w1=None, wv=None,
                                  bn=r._bn_block(), dims=dims)
+
+
+def _keys_f32(router):
+    """fp32 [2, K, dq/2]: sub_keys_1.weight, sub_keys_2.weight."""
+    return torch.stack([_f32(router.sub_keys_1.weight), _f32(router.sub_keys_2.weight)]).contiguous()
 
 
 def _key_cat(router):
@@ -159,9 +183,14 @@ class _EthosLayerFunction(torch.autograd.Function):
         pw = layer._packed(x2d.device, fresh=need_grad)
         eps, mom = layer.router._bn_eps_momentum()
         training = layer.router._bn_training()
-        x16 = x2d.to(torch.bfloat16).contiguous()
-        htab = layer._expert_table() if (layer.cache_expert_table and not need_grad) else None
-        out = ops.layer_forward(x16, pw, training, eps, mom, save=need_grad, path=layer.expert_path, htab=htab)
+        if pw.fp32:
+            # fp32 arithmetic throughout (no expert-path choice, no cached table)
+            xin = x2d.to(torch.float32).contiguous()
+            out = ops.layer_forward_f32(xin, pw, training, eps, mom, save=need_grad)
+        else:
+            xin = x2d.to(torch.bfloat16).contiguous()
+            htab = layer._expert_table() if (layer.cache_expert_table and not need_grad) else None
+            out = ops.layer_forward(xin, pw, training, eps, mom, save=need_grad, path=layer.expert_path, htab=htab)
         if training:
             layer.router._write_back_running(pw.bn)
         ctx.layer = layer
@@ -169,7 +198,7 @@ class _EthosLayerFunction(torch.autograd.Function):
         ctx.x_dtype = x2d.dtype
         ctx.params = params
         if need_grad:
-            ctx.saved = dict(out, x16=x16, pw=pw)
+            ctx.saved = dict(out, xin=xin, pw=pw)
         return out["y"].to(x2d.dtype)
 
     @staticmethod
@@ -236,9 +265,14 @@ class EthosExpertLayer(nn.Module):
             d = self.d_model
             r = self.router
             W2 = self.generation_network.net[2].weight
-            w_cat = torch.cat([_bf16(m.weight) for m in r.query_projs] + [_bf16(W2[:d].t())], 0)
-            self._cache = dict(w_cat=w_cat, key_cat=_key_cat(r), latents=_bf16(self.expert_latents.weight),
-                               w1=_bf16(self.generation_network.net[0].weight), wv=_bf16(W2[d:]))
+            if _fp32_arithmetic(self):
+                w_cat = torch.cat([_f32(m.weight) for m in r.query_projs] + [_f32(W2[:d].t())], 0)
+                self._cache = dict(w_cat=w_cat, key_cat=_keys_f32(r), latents=_f32(self.expert_latents.weight),
+                                   w1=_f32(self.generation_network.net[0].weight), wv=_f32(W2[d:]), fp32=True)
+            else:
+                w_cat = torch.cat([_bf16(m.weight) for m in r.query_projs] + [_bf16(W2[:d].t())], 0)
+                self._cache = dict(w_cat=w_cat, key_cat=_key_cat(r), latents=_bf16(self.expert_latents.weight),
+                                   w1=_bf16(self.generation_network.net[0].weight), wv=_bf16(W2[d:]), fp32=False)
             self._cache_key = None if fresh else key
         c = self._cache
         r = self.router
@@ -252,7 +286,7 @@ class EthosExpertLayer(nn.Module):
             c["bn"] = r._bn_block()
             c["bn_key"] = None if (fresh or r.training) else bn_key
         return ops.PackedWeights(w_cat=c["w_cat"], key_cat=c["key_cat"], latents=c["latents"], w1=c["w1"],
-                                 wv=c["wv"], bn=c["bn"], dims=self.dims)
+                                 wv=c["wv"], bn=c["bn"], dims=self.dims, fp32=c["fp32"])
 
     def _expert_table(self):
         """The cached expert table for the weights ``_packed`` last saw (its

@@ -13,7 +13,8 @@ from ._lib import EthosDims, EthosError, check, lib
 
 __all__ = [
     "make_dims", "gemm_bf16", "gemm_ex", "product_key_topk", "expert_forward", "router_forward", "layer_forward",
-    "device_error_word", "check_device_error", "PackedWeights", "layer_backward",
+    "device_error_word", "check_device_error", "PackedWeights", "layer_backward", "layer_forward_f32",
+    "router_forward_f32", "layer_backward_f32",
 ]
 
 _ERR_WORDS = {}
@@ -180,17 +181,20 @@ def expert_table_build(latents, w1, dims, with_grad=False):
 
 class PackedWeights:
     """Kernel-layout copies of the layer parameters (derived caches, never
-    state): bf16 ``w_cat [H*dq + dh, d]`` (query projections stacked, then
-    ``W_u^T``), ``key_cat [2, K, dq]`` (each sub-key row written twice for the
-    split-bf16 scoring), ``latents [N, dl]``, ``w1 [dh, dl]``, ``wv [d, dh]``,
-    and the fp32 ``bn [5, H*dq]`` (bias, gamma, beta, running mean, running
-    var)."""
+    state): ``w_cat [H*dq + dh, d]`` (query projections stacked, then
+    ``W_u^T``), ``key_cat``, ``latents [N, dl]``, ``w1 [dh, dl]``,
+    ``wv [d, dh]`` and the fp32 ``bn [5, H*dq]`` (bias, gamma, beta, running
+    mean, running var).  bf16 path (``fp32`` False): bf16 tensors, key_cat
+    ``[2, K, dq]`` with each sub-key row written twice (split-bf16 scoring).
+    fp32 path: fp32 tensors, key_cat ``[2, K, dq/2]`` (the two sub-key
+    tables)."""
 
-    __slots__ = ("w_cat", "key_cat", "latents", "w1", "wv", "bn", "dims")
+    __slots__ = ("w_cat", "key_cat", "latents", "w1", "wv", "bn", "dims", "fp32")
 
-    def __init__(self, w_cat, key_cat, latents, w1, wv, bn, dims):
+    def __init__(self, w_cat, key_cat, latents, w1, wv, bn, dims, fp32=False):
         self.w_cat, self.key_cat, self.latents = w_cat, key_cat, latents
         self.w1, self.wv, self.bn, self.dims = w1, wv, bn, dims
+        self.fp32 = fp32
 
 
 def router_forward(x2d, pw, bn_training, eps, momentum, save_qpre=None, save_bn=None):
@@ -351,4 +355,103 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
                                  _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws), ws_bytes, _vp(err),
                                  _events(stage_events), _stream(dev)),
           "ethos_layer_backward")
+    return g
+
+
+# ----------------------------------------------------------- fp32 path --
+def _grad_layout(d):
+    """Flat fp32 buffer for every parameter gradient (256-B aligned slices)."""
+    HQ = d["num_heads"] * d["d_query"]
+    shapes = [("d_latents", (d["num_experts"], d["d_latent"])), ("d_w1", (d["d_hidden"], d["d_latent"])),
+              ("d_w2", (2 * d["d_model"], d["d_hidden"])), ("d_wq", (HQ, d["d_model"])), ("d_bn", (3, HQ)),
+              ("d_keys", (2, d["num_sub_keys"], d["d_query"] // 2))]
+    layout, off = [], 0
+    for name, shp in shapes:
+        layout.append((name, off, shp))
+        off += (_numel(shp) + 63) // 64 * 64
+    return layout, off
+
+
+def layer_forward_f32(x2d, pw, bn_training, eps, momentum, save=False, router_only=False):
+    """fp32 arithmetic (ethos_layer_forward_f32): fp32 ``x2d [T, d]`` and an
+    fp32 ``PackedWeights``.  Returns ``y`` (fp32 [T, d]; absent with
+    ``router_only``), ``ids``, ``weights`` and, when ``save``, the tensors the
+    backward needs."""
+    _require_cuda(x2d, "x")
+    if not pw.fp32 or x2d.dtype != torch.float32:
+        raise ValueError("layer_forward_f32 takes fp32 inputs and fp32 packed weights")
+    d = pw.dims
+    T = x2d.shape[0]
+    dev = x2d.device
+    dims = make_dims(T, d)
+    L = lib()
+    ws_bytes = L.ethos_forward_workspace_size_f32(ctypes.byref(dims), 1 if bn_training else 0)
+    if ws_bytes == 0:
+        st = L.ethos_check_dims(ctypes.byref(dims))
+        check(st if st != 0 else 2, "ethos_forward_workspace_size_f32")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    H, k, dh, HQ, dq = d["num_heads"], d["top_k"], d["d_hidden"], d["num_heads"] * d["d_query"], d["d_query"]
+    f32 = dict(dtype=torch.float32, device=dev)
+    out = dict(ids=torch.empty((T, H, k), dtype=torch.int32, device=dev), weights=torch.empty((T, H, k), **f32))
+    if not router_only:
+        out["y"] = torch.empty((T, d["d_model"]), **f32)
+    if save and not router_only:
+        out["xp"] = torch.empty((T, dh), **f32)
+        out["hacc"] = torch.empty((T, dh), **f32)
+        out["dot"] = torch.empty((T, H * k), **f32)
+        out["qpre"] = torch.empty((T, HQ), **f32)
+        out["qhat"] = torch.empty((2, H, T, dq // 2), **f32)
+        out["htab"] = torch.empty((d["num_experts"], dh), **f32)
+        out["gtab"] = torch.empty((d["num_experts"], dh), **f32)
+        if bn_training:
+            out["bn_stats"] = torch.empty((2, HQ), **f32)
+    g = out.get
+    err = device_error_word(dev)
+    check(L.ethos_layer_forward_f32(ctypes.byref(dims), _vp(x2d), _vp(pw.w_cat), _vp(pw.bn), float(eps),
+                                    float(momentum), 1 if bn_training else 0, _vp(pw.key_cat), _vp(pw.latents),
+                                    _vp(pw.w1), _vp(pw.wv), _vp(g("y")), _vp(out["ids"]), _vp(out["weights"]),
+                                    _vp(g("xp")), _vp(g("hacc")), _vp(g("dot")), _vp(g("qpre")), _vp(g("bn_stats")),
+                                    _vp(g("qhat")), _vp(g("htab")), _vp(g("gtab")), _vp(ws), ws_bytes, _vp(err),
+                                    _stream(dev)), "ethos_layer_forward_f32")
+    return out
+
+
+def router_forward_f32(x2d, pw, bn_training, eps, momentum):
+    """``(weights fp32 [T,H,k], ids int32 [T,H,k])`` in fp32 arithmetic."""
+    out = layer_forward_f32(x2d, pw, bn_training, eps, momentum, router_only=True)
+    return out["weights"], out["ids"]
+
+
+def layer_backward_f32(dy, x32, pw, saved, bn_training, eps, stage_events=None):
+    """Gradients of ``layer_forward_f32(save=True)`` (ethos_layer_backward_f32);
+    the same dict as ``layer_backward``."""
+    if stage_events is not None and len(stage_events) != 2:
+        raise ValueError("stage_events: one event (or None) per ETHOS_BWD_STAGE_*")
+    _require_cuda(dy, "dy")
+    d = pw.dims
+    T = dy.shape[0]
+    dev = dy.device
+    dims = make_dims(T, d)
+    L = lib()
+    ws_bytes = L.ethos_backward_workspace_size_f32(ctypes.byref(dims))
+    if ws_bytes == 0:
+        check(2, "ethos_backward_workspace_size_f32")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    layout, total = _grad_layout(d)
+    flat = torch.empty(total, dtype=torch.float32, device=dev)
+    g = {name: flat[o:o + _numel(shp)].view(shp) for name, o, shp in layout}
+    g["dx"] = torch.empty((T, d["d_model"]), dtype=torch.float32, device=dev)
+    g["flat"] = flat
+    g["layout"] = layout
+    dy = dy.contiguous().float()
+    err = device_error_word(dev)
+    check(L.ethos_layer_backward_f32(ctypes.byref(dims), 1 if bn_training else 0, float(eps), _vp(dy), _vp(x32),
+                                     _vp(pw.w_cat), _vp(pw.bn), _vp(pw.key_cat), _vp(pw.latents), _vp(pw.w1),
+                                     _vp(pw.wv), _vp(saved["ids"]), _vp(saved["weights"]), _vp(saved["xp"]),
+                                     _vp(saved["hacc"]), _vp(saved["dot"]), _vp(saved["qpre"]),
+                                     _vp(saved.get("bn_stats")), _vp(saved["qhat"]), _vp(saved.get("htab")),
+                                     _vp(saved.get("gtab")), _vp(g["dx"]), _vp(g["d_latents"]), _vp(g["d_w1"]),
+                                     _vp(g["d_w2"]), _vp(g["d_wq"]), _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws),
+                                     ws_bytes, _vp(err), _events(stage_events), _stream(dev)),
+          "ethos_layer_backward_f32")
     return g

@@ -288,6 +288,44 @@ int ethos_gemm_bf16_ex(const void* a, int64_t lda, int a_mn_major, const void* b
                        void* d, int64_t ldd, int64_t M, int64_t N, int64_t K, float scale, int out_mode,
                        int* dev_err, void* stream);
 
+/* ------------------------------------------------------ fp32 arithmetic --
+ * The same layer computed in fp32, for modules whose parameters are fp32 (the
+ * reference's SimplifiedHypernetMoE / ProductKeyRouter, model.py:208-343,
+ * then run entirely in fp32).  Contractions use the tcgen05 GEMMs on
+ * split-bf16 operands (v = hi + lo, products hi*hi + lo*hi + hi*lo with fp32
+ * accumulation: about 2^-16 relative error per product); BatchNorm, scores,
+ * top-k, softmax, the expert table (fp32, rebuilt every call), GELU and all
+ * reductions stay fp32.  Extra shape rule: d_query / 2 a multiple of 128.
+ * Same argument meanings as the bf16 entry points, with fp32 tensors:
+ *  x [T, d]; w_cat [H*dq + dh, d] (only the first H*dq rows when y is NULL);
+ *  keys [2, K, dq/2] = sub_keys_1.weight, sub_keys_2.weight (NOT doubled);
+ *  latents [N, dl]; w1 [dh, dl]; wv [d, dh]; y [T, d] or NULL for the router
+ *  alone (ProductKeyRouter.forward, model.py:208-254: then latents, w1, wv
+ *  and every save_* may be NULL).  save_qhat [2, H, T, dq/2] holds the
+ *  normalised query halves; save_htab / save_gtab [N, dh] the expert table
+ *  and its GELU derivative (save_gtab needs save_htab). */
+size_t ethos_forward_workspace_size_f32(const ethos_dims* dims, int bn_training);
+int ethos_layer_forward_f32(const ethos_dims* dims, const float* x, const float* w_cat, float* bn, float bn_eps,
+                            float bn_momentum, int bn_training, const float* keys, const float* latents,
+                            const float* w1, const float* wv, float* y, int32_t* ids, float* weights,
+                            float* save_xp, float* save_hacc, float* save_dot, float* save_qpre, float* save_bn,
+                            float* save_qhat, float* save_htab, float* save_gtab, void* workspace,
+                            size_t workspace_bytes, int* dev_err, void* stream);
+
+/* Backward of ethos_layer_forward_f32 (autograd through model.py:208-343 in
+ * fp32): dy fp32 [T, d], the forward's inputs and save buffers (save_bn in
+ * training; htab / gtab may be NULL together, the backward then rebuilds
+ * them); outputs and stage events as for ethos_layer_backward. */
+size_t ethos_backward_workspace_size_f32(const ethos_dims* dims);
+int ethos_layer_backward_f32(const ethos_dims* dims, int bn_training, float bn_eps, const float* dy, const float* x,
+                             const float* w_cat, const float* bn, const float* keys, const float* latents,
+                             const float* w1, const float* wv, const int32_t* ids, const float* weights,
+                             const float* save_xp, const float* save_hacc, const float* save_dot,
+                             const float* save_qpre, const float* save_bn, const float* save_qhat, const float* htab,
+                             const float* gtab, float* dx, float* d_latents, float* d_w1, float* d_w2, float* d_wq,
+                             float* d_bn, float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
+                             void* const* stage_events, void* stream);
+
 /* ------------------------------------------------- failure detection --
  * Every wait inside the kernels (an mbarrier phase: a TMA copy landing, an
  * MMA completing, an accumulator released) is bounded.  A wait that runs out

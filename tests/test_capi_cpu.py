@@ -40,6 +40,16 @@ def test_every_declared_symbol_is_exported(L):
     assert set(names) == set(_lib.EXPORTS), "ctypes table and header disagree"
 
 
+def test_ctypes_argument_counts_match_header():
+    """Every ctypes prototype has as many arguments as the header declares."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    for m in re.finditer(r"^\s*(?:int|size_t|uint64_t|const char\s*\*)\s*(ethos_\w+)\s*\(([^)]*)\)\s*;", text,
+                         flags=re.M):
+        name, args = m.group(1), m.group(2).strip()
+        n = 0 if args in ("", "void") else len(args.split(","))
+        assert len(_lib.EXPORTS[name][1]) == n, (name, n, len(_lib.EXPORTS[name][1]))
+
+
 def test_abi_version_and_status_strings(L):
     assert L.ethos_abi_version() >= 1
     assert L.ethos_status_string(0) == b"ok"
