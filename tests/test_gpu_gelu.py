@@ -60,9 +60,9 @@ def test_device_gelu_and_derivative_match_erf_gelu():
         err = (out[row] - d_ref).abs()
         report[name] = err.max().item()
         assert (err <= 5e-7 + ulp * d_ref.abs()).all(), (name, err.max().item())
-    # the scalar and paired forms are the same computation, step for step
-    assert (out[0] - out[1]).abs().max().item() <= 1e-7
-    assert (out[1] - out[2]).abs().max().item() <= 1e-7
+    # the two paired forms share one evaluation (the scalar form takes its
+    # reciprocal differently and is held to the same bound above)
+    assert torch.equal(out[1], out[2])
     # torch's fp32 CUDA erf GELU on the same points, for scale
     torch_err = (torch.nn.functional.gelu(xg).cpu().double() - g_ref).abs().max().item()
     print(f"max |error| {report}; torch fp32 F.gelu {torch_err:.2e}")
