@@ -104,6 +104,21 @@ def test_workspace_size(L):
     assert L.ethos_forward_workspace_size(ctypes.byref(bad), 0, 0) == 0
 
 
+def test_fp32_workspace_and_shape_rule(L):
+    """The fp32 path needs d_query / 2 to be a multiple of 128 (its score
+    GEMMs' N tile); other shapes are rejected before any launch."""
+    d = _dims()
+    assert L.ethos_forward_workspace_size_f32(ctypes.byref(d), 0) > 2 * 8 * 16384 * 512 * 4
+    assert L.ethos_backward_workspace_size_f32(ctypes.byref(d)) > 2 * 8 * 16384 * 512 * 4
+    small_q = _dims(d_query=128)
+    assert L.ethos_check_dims(ctypes.byref(small_q)) == 0          # fine for the bf16 path
+    assert L.ethos_forward_workspace_size_f32(ctypes.byref(small_q), 0) == 0
+    assert L.ethos_backward_workspace_size_f32(ctypes.byref(small_q)) == 0
+    st = L.ethos_layer_forward_f32(ctypes.byref(small_q), *([None] * 3), 1e-5, 0.1, 0, *([None] * 15), None, 0,
+                                   None, None)
+    assert st == 2  # ETHOS_ERR_UNSUPPORTED_SHAPE
+
+
 def test_null_arguments_rejected_without_gpu(L):
     d = _dims()
     st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None, 0, None, None,
