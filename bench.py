@@ -18,7 +18,9 @@ forward with BatchNorm on batch statistics, backward through all parameters,
 the NCCL all-reduce of every gradient overlapped with the backward (N > 1) and
 a fused AdamW update -- timed at the same N, with the all-reduce time left
 exposed and a cross-rank checksum of the reduced gradients and updated
-parameters (the run exits non-zero if the ranks disagree).
+parameters (the run exits non-zero if the ranks disagree) -- and short
+``router`` (config 3, the routing microbenchmark) and ``stack`` (config 4's
+12 expert layers) blocks.
 
 ``--impl reference`` times the reference path's CPU implementation on the
 host cores (the vectorised fp32 restatement in oracle/ethos_oracle.py of
@@ -415,28 +417,31 @@ def run_train(args, rank, world, local, dev):
         raise SystemExit("ranks disagree on the reduced gradients / updated parameters")
 
 
-def run_router(args, rank, world, local, dev):
+def router_block(args, rank, world, local, dev, steps=None, sampler=True):
     """Config 3: product-key routing micro-benchmark -- 65 536 normalised
     queries per head for 8 heads (N(0,1), bf16, d_key 256), two 512 x 128
     sub-key tables, top-16 per half, top-16 of the candidate sums, int32 ids
-    and fp32 softmax weights (ethos_product_key_topk).  Unit: query-heads."""
+    and fp32 softmax weights (ethos_product_key_topk).  Unit: query-heads.
+    Returns the report (every rank must call it)."""
     import torch.distributed as dist
     from ethos_b200 import ops
     from ethos_b200.init import tensor_generator
+    steps = steps or args.steps
     H, Q, dk, K, k = 8, 65536, 256, 512, 16
     g = tensor_generator(rank, "bench.router")
     q = torch.randn((H, Q, dk), generator=g).to(device=dev, dtype=torch.bfloat16)
     keys = (torch.randn((2, K, dk // 2), generator=g) / (dk // 2) ** 0.5).to(device=dev, dtype=torch.bfloat16)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, 3)):
         ops.product_key_topk(q, keys, k)
     torch.cuda.synchronize()
     ops.check_device_error(dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     n_launch = launches()
-    sampler = ClockSampler(local)
-    sampler.start()
+    clk = ClockSampler(local) if sampler else None
+    if clk:
+        clk.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -449,7 +454,7 @@ def run_router(args, rank, world, local, dev):
     n_launch = launches() - n_launch
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
+    clocks = clk.stop() if clk else None
     ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -457,36 +462,49 @@ def run_router(args, rank, world, local, dev):
         ms = t.item()
     peaks = load_peaks()
     flops = 2.0 * 2 * K * (dk // 2) * H * Q
+    tf = flops / (ms / 1e3) / 1e12
+    out = dict(metric="product-key routing query-heads/s (2 x 512 sub-keys, d_key 256, top-16)",
+               value=H * Q * world / (ms / 1e3), unit="query-heads/s", ms_per_step=ms, steps=steps,
+               workload="config 3: product-key routing microbenchmark, 65536 queries x 8 heads, "
+                        "bf16 queries, fp32 scores, int32 ids + fp32 weights",
+               queries_per_head=Q, heads=H, parallelism=f"dp{world}",
+               l2="flushed between timed steps (256 MiB write)",
+               roofline=dict(bound="tensor", kernel="k_score_topk<16>", achieved=tf, peak=peaks["bf16_tflops"],
+                             unit="TFLOP/s", frac=tf / peaks["bf16_tflops"], traffic=None,
+                             peak_source=peaks["source"] + " bf16 burst"),
+               gpu_launches=n_launch)
+    if clocks is not None:
+        out["clocks"] = clocks
+    return out
+
+
+def run_router(args, rank, world, local, dev):
+    """--mode router: config 3 alone, as its own JSON line."""
+    r = router_block(args, rank, world, local, dev)
     if rank == 0:
-        tf = flops / (ms / 1e3) / 1e12
-        line = dict(metric="product-key routing query-heads/s (2 x 512 sub-keys, d_key 256, top-16)",
-                    value=H * Q * world / (ms / 1e3), unit="query-heads/s", n_gpus=world, steps=args.steps,
-                    warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
+        line = dict(metric=r["metric"], value=r["value"], unit=r["unit"], n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=r["ms_per_step"], higher_is_better=True, scaling="weak",
                     vs_baseline=None, dtype="bf16", data="synthetic",
-                    config=dict(workload="config 3: product-key routing microbenchmark, 65536 queries x 8 heads, "
-                                         "bf16 queries, fp32 scores, int32 ids + fp32 weights",
-                                queries_per_head=Q, heads=H, parallelism=f"dp{world}",
-                                l2="flushed between timed steps (256 MiB write)"),
-                    roofline=dict(bound="tensor", kernel="k_score_topk<16>", achieved=tf,
-                                  peak=peaks["bf16_tflops"], unit="TFLOP/s", frac=tf / peaks["bf16_tflops"],
-                                  traffic=None, peak_source=peaks["source"] + " bf16 burst"),
-                    gpu_launches=n_launch, clocks=clocks)
+                    config=dict(workload=r["workload"], queries_per_head=r["queries_per_head"], heads=r["heads"],
+                                parallelism=r["parallelism"], l2=r["l2"]),
+                    roofline=r["roofline"], gpu_launches=r["gpu_launches"], clocks=r.get("clocks"))
         print(json.dumps(line), flush=True)
 
 
-def run_stack(args, rank, world, local, dev):
+def stack_block(args, rank, world, local, dev, steps=None, sampler=True):
     """Config 4, the expert layers of the decoder: 12 ETHOS expert layers
     (config-2 dimensions, each with its own seeded parameters) on one residual
     stream, h = h + layer(rms_norm(h)), over the embeddings of 16 384 token ids
     drawn Zipf(1.1) over a 100 277-entry vocabulary.  The decoder's attention,
     embedding and output head are the reference's own model code, which is not
-    part of this repository, so they are not timed; the line reports the expert
-    layers' share of the forward."""
+    part of this repository, so they are not timed; the report gives the
+    expert layers' share of the forward.  Every rank must call it."""
     import numpy as np
     import torch.distributed as dist
     import torch.nn.functional as F
     from ethos_b200 import EthosConfig, EthosExpertLayer, ops
     from ethos_b200.init import seeded_init_
+    steps = steps or args.steps
     n_layers, vocab, T = 12, 100277, args.tokens
     rng = np.random.default_rng(1000 + rank)
     ids = rng.zipf(1.1, size=4 * T)
@@ -509,15 +527,15 @@ def run_stack(args, rank, world, local, dev):
         return h
 
     with torch.no_grad():
-        for _ in range(args.warmup):
+        for _ in range(max(args.warmup, 3)):
             forward()
         torch.cuda.synchronize()
         ops.check_device_error(dev)
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         n_launch = launches()
-        sampler = ClockSampler(local)
-        sampler.start()
+        clk = ClockSampler(local) if sampler else None
+        if clk:
+            clk.start()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -530,23 +548,36 @@ def run_stack(args, rank, world, local, dev):
         n_launch = launches() - n_launch
         if world > 1:
             dist.barrier()
-        clocks = sampler.stop()
+        clocks = clk.stop() if clk else None
+        ops.check_device_error(dev)
     ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
+    out = dict(metric="decoder expert-layer stack tokens/s (12 x ETHOS expert layer, 262K experts, k=16x8)",
+               value=T * world / (ms / 1e3), unit="tokens/s", ms_per_step=ms, ms_per_layer=ms / n_layers,
+               steps=steps, data="synthetic (Zipf(1.1) token ids)",
+               workload="config 4, expert layers only: embedding lookup, then 12 x (RMSNorm, ETHOS expert layer, "
+                        "residual add); MLA attention and the output head are not included",
+               tokens_per_gpu=T, layers=n_layers, vocab=vocab, parallelism=f"dp{world}",
+               l2="flushed between timed steps (256 MiB write)", gpu_launches=n_launch)
+    if clocks is not None:
+        out["clocks"] = clocks
+    del layers
+    return out
+
+
+def run_stack(args, rank, world, local, dev):
+    """--mode stack: config 4's expert layers alone, as their own JSON line."""
+    r = stack_block(args, rank, world, local, dev)
     if rank == 0:
-        line = dict(metric="decoder expert-layer stack tokens/s (12 x ETHOS expert layer, 262K experts, k=16x8)",
-                    value=T * world / (ms / 1e3), unit="tokens/s", n_gpus=world, steps=args.steps,
-                    warmup=args.warmup, ms_per_step=ms, ms_per_layer=ms / n_layers, higher_is_better=True,
-                    scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic (Zipf(1.1) token ids)",
-                    config=dict(workload="config 4, expert layers only: embedding lookup, then 12 x (RMSNorm, "
-                                         "ETHOS expert layer, residual add); MLA attention and the output head "
-                                         "are not included",
-                                tokens_per_gpu=T, layers=n_layers, vocab=vocab, parallelism=f"dp{world}",
-                                l2="flushed between timed steps (256 MiB write)"),
-                    gpu_launches=n_launch, clocks=clocks)
+        line = dict(metric=r["metric"], value=r["value"], unit=r["unit"], n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=r["ms_per_step"], ms_per_layer=r["ms_per_layer"],
+                    higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16", data=r["data"],
+                    config=dict(workload=r["workload"], tokens_per_gpu=r["tokens_per_gpu"], layers=r["layers"],
+                                vocab=r["vocab"], parallelism=r["parallelism"], l2=r["l2"]),
+                    gpu_launches=r["gpu_launches"], clocks=r.get("clocks"))
         print(json.dumps(line), flush=True)
 
 
@@ -560,6 +591,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-train", action="store_true", help="leave the training block out of the forward line")
     ap.add_argument("--train-steps", type=int, default=20, help="timed training steps in the train block")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="leave the config-3 router and config-4 stack blocks out of the forward line")
     ap.add_argument("--ref-seconds", type=float, default=6.0)
     ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "stack"],
                     help="forward: config 2 (headline, with the config-5 train block); train: config 5 alone; "
@@ -777,6 +810,13 @@ def run_forward(args, rank, world, local, dev):
     if not args.no_train:
         train = train_block(args, rank, world, local, dev, layer=layer, steps=args.train_steps, sampler=False)
     del layer
+    # configs 3 and 4 in the same run (short blocks; their own modes print
+    # full lines): the routing microbenchmark and the 12 expert layers
+    extra = {}
+    if not args.no_extra and args.tokens == TOKENS:
+        torch.cuda.empty_cache()
+        extra["router"] = router_block(args, rank, world, local, dev, steps=20, sampler=False)
+        extra["stack"] = stack_block(args, rank, world, local, dev, steps=5, sampler=False)
 
     peaks = load_peaks()
     total_tokens = T * world
@@ -845,6 +885,7 @@ def run_forward(args, rank, world, local, dev):
     )
     if train is not None:
         line["train"] = train
+    line.update(extra)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
         line["cpu_baseline"]["config1"] = cpu_baseline_config1()
