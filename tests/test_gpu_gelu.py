@@ -65,4 +65,11 @@ def test_device_gelu_and_derivative_match_erf_gelu():
     assert torch.equal(out[1], out[2])
     # torch's fp32 CUDA erf GELU on the same points, for scale
     torch_err = (torch.nn.functional.gelu(xg).cpu().double() - g_ref).abs().max().item()
-    print(f"max |error| {report}; torch fp32 F.gelu {torch_err:.2e}")
+    report["torch fp32 F.gelu"] = torch_err
+    print(f"max |error| {report}")
+    import json
+    import os
+    path = os.environ.get("ETHOS_TEST_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(dict(test="device_gelu_max_abs_error", **report)) + "\n")
