@@ -24,7 +24,9 @@ namespace ethos {
 // 16 warps x 2 stages: the kernel is bound by load latency per warp, so
 // resident warps matter more than ring depth (measured on B200 at 16384
 // tokens x 128 selections: 8x5 0.47 ms, 12x3 0.40, 14x3 0.36, 16x2 0.31;
-// 18 and more warps spill registers).
+// 18 and more warps spill registers).  Restricting the routed ids to an
+// L2-resident eighth of the table saves only 6 %: the per-SM copy and
+// arithmetic pipeline binds, not DRAM.
 #ifndef ETHOS_GATHER_WARPS
 #define ETHOS_GATHER_WARPS 16
 #endif
@@ -39,9 +41,19 @@ constexpr int GATHER_STAGE_BYTES = GATHER_ROWS * 1024 + 16;          // rows + 4
 // + one x_proj buffer: a token's x_proj moves to registers at its first batch,
 // and the next token's copy is issued at least one batch later (R/4 > STAGES-1)
 // (the table path runs with R >= 16 selections per token, i.e. 4 batches)
-constexpr int GATHER_WARP_BYTES = GATHER_STAGES * GATHER_STAGE_BYTES + 2048;
+// ETHOS_GATHER_XP_REGS (the default): a token's x_proj row is loaded straight
+// into the lanes' registers at its first batch instead of through a
+// shared-memory buffer (0.266 against 0.270 ms at 16 384 tokens; the 2 KB per
+// warp it frees did not pay as a third ring stage: 16 x 3 0.269 ms, 14 x 4
+// 0.286 ms, 15 x 3 with the buffer 0.285 ms).
+#ifndef ETHOS_GATHER_XP_REGS
+#define ETHOS_GATHER_XP_REGS 1
+#endif
+constexpr int GATHER_XP_BYTES = ETHOS_GATHER_XP_REGS ? 0 : 2048;
+constexpr int GATHER_WARP_BYTES = GATHER_STAGES * GATHER_STAGE_BYTES + GATHER_XP_BYTES;
 constexpr int GATHER_SMEM_BYTES = GATHER_WARPS * GATHER_WARP_BYTES;
-static_assert(GATHER_STAGES >= 2 && GATHER_STAGES <= 4, "single x_proj buffer needs STAGES-1 < 4 batches");
+static_assert(GATHER_STAGES >= 2 && (ETHOS_GATHER_XP_REGS || GATHER_STAGES <= 4),
+              "single x_proj buffer needs STAGES-1 < 4 batches");
 static_assert(GATHER_SMEM_BYTES <= 227 * 1024, "gather ring exceeds shared memory");
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -73,11 +85,13 @@ __device__ __forceinline__ void unpack_h8(const uint4& u, float (&f)[8]) {
 // One warp walks tokens gw, gw + nw, ...; its rows are processed in batches of
 // 4 through a GATHER_STAGES-deep cp.async ring (2 stages by default), so
 // GATHER_STAGES - 1 batches (4 KB each) per warp are in flight while one is
-// reduced.  Lane l copies and later reads only its own
-// slices of each row, hidden columns [8l, 8l + 8) and [256 + 8l, 256 + 8l + 8)
-// (bytes [16l, 16l + 16) and [512 + 16l, ...)), so a cp.async.wait_group
-// alone orders copy and use.  Needs R / 4 > STAGES - 1 (so a token's x_proj
-// buffer is read into registers before the next token's copy is issued).
+// reduced; the token's x_proj slices move to registers at its first batch.
+// Lane l copies and later reads only its own slices of each row, hidden
+// columns [8l, 8l + 8) and [256 + 8l, 256 + 8l + 8) (bytes [16l, 16l + 16)
+// and [512 + 16l, ...)), so a cp.async.wait_group alone orders copy and use.
+// With the shared x_proj buffer (ETHOS_GATHER_XP_REGS 0) it needs
+// R / 4 > STAGES - 1, so that a token's x_proj is read into registers before
+// the next token's copy is issued.
 __global__ void __launch_bounds__(GATHER_THREADS, 1)
     k_expert_gather(const __half* __restrict__ table, const int32_t* __restrict__ ids, const float* __restrict__ w,
                     const float* __restrict__ xp, __nv_bfloat16* __restrict__ hacc_out,
@@ -99,7 +113,6 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
 
   // Cursors instead of div/mod by the runtime batch count: the issue cursor
   // (token it_t, row it_r) runs STAGES-1 batches ahead of the consume cursor.
-  static_assert((GATHER_STAGES & (GATHER_STAGES - 1)) == 0, "ring depth is a power of two");
   int it_t = gw, it_r = 0, it_n = 0;
   bool bad_id = false;
   // ids of the batch at the issue cursor, loaded one issue ahead (int4 broadcast)
@@ -108,7 +121,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
   auto issue_next = [&]() {
     if (it_n < nb) {
       const int t = it_t, r0 = it_r;
-      uint8_t* st = wbase + (it_n & (GATHER_STAGES - 1)) * GATHER_STAGE_BYTES;
+      uint8_t* st = wbase + (static_cast<unsigned>(it_n) % GATHER_STAGES) * GATHER_STAGE_BYTES;
       const int idv[4] = {next_ids.x, next_ids.y, next_ids.z, next_ids.w};
 #pragma unroll
       for (int u = 0; u < GATHER_ROWS; ++u) {
@@ -119,7 +132,7 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
         cp_async_16(st + u * 1024 + 512 + 16 * lane, src + 512 + 16 * lane);
       }
       if (lane == 0) cp_async_16(st + GATHER_ROWS * 1024, w + static_cast<int64_t>(t) * R + r0);
-      if (r0 == 0) {  // first batch of a token also brings this lane's x_proj slices
+      if (!ETHOS_GATHER_XP_REGS && r0 == 0) {  // first batch of a token also brings this lane's x_proj slices
         const char* xs = reinterpret_cast<const char*>(xp + static_cast<int64_t>(t) * 512);
         cp_async_16(xpbuf + 32 * lane, xs + 32 * lane);
         cp_async_16(xpbuf + 32 * lane + 16, xs + 32 * lane + 16);
@@ -149,9 +162,10 @@ __global__ void __launch_bounds__(GATHER_THREADS, 1)
   for (int b = 0; b < nb; ++b) {
     issue_next();
     cp_async_wait_group<GATHER_STAGES - 1>();
-    const uint8_t* st = wbase + (b & (GATHER_STAGES - 1)) * GATHER_STAGE_BYTES;
+    const uint8_t* st = wbase + (static_cast<unsigned>(b) % GATHER_STAGES) * GATHER_STAGE_BYTES;
     if (r0 == 0) {
-      const float4* x4 = reinterpret_cast<const float4*>(xpbuf);
+      const float4* x4 = ETHOS_GATHER_XP_REGS ? reinterpret_cast<const float4*>(xp + static_cast<int64_t>(t) * 512)
+                                              : reinterpret_cast<const float4*>(xpbuf);
       // this lane's x_proj columns [8l, 8l+8) and [256+8l, 256+8l+8)
       const float4 a0 = x4[2 * lane], a1 = x4[2 * lane + 1], c0 = x4[64 + 2 * lane], c1 = x4[64 + 2 * lane + 1];
       xv2[0] = pk2(a0.x, a0.y); xv2[1] = pk2(a0.z, a0.w); xv2[2] = pk2(a1.x, a1.y); xv2[3] = pk2(a1.z, a1.w);
