@@ -593,7 +593,8 @@ def main():
     ap.add_argument("--train-steps", type=int, default=20, help="timed training steps in the train block")
     ap.add_argument("--no-extra", action="store_true",
                     help="leave the config-3 router and config-4 stack blocks out of the forward line")
-    ap.add_argument("--ref-seconds", type=float, default=6.0)
+    ap.add_argument("--ref-seconds", type=float, default=3.0,
+                    help="CPU seconds per reference-arm step (a bounded sample of the workload)")
     ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "stack"],
                     help="forward: config 2 (headline, with the config-5 train block); train: config 5 alone; "
                          "router: config 3 routing microbenchmark; stack: config 4's 12 expert layers")
