@@ -515,7 +515,11 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
 //   train: dq = gamma*invstd*(dq^ - sum(dq^)/T - x^ * sum(dq^ x^)/T), dbias = 0
 //   eval:  dq = gamma*invstd*dq^,                           dbias = sum(dq)
 // dgamma = sum(dq^ x^), dbeta = sum(dq^).  dq is written as bf16 into the
-// GEMM operand du[:, :C].
+// GEMM operand du[:, :C].  The apply pass evaluates
+//   dq = A dq^ + B (qpre - mean) + D,  A = gamma*invstd, B = -A*invstd*m2,
+//   D = -A*m1
+// with coef[c] = (A, B, D, mean): centring qpre before the multiply keeps the
+// cancellation exact where qpre and the mean agree to many bits.
 __global__ void k_bn_bwd_partial(const float* __restrict__ dqh, const float* __restrict__ qpre,
                                  const float* __restrict__ mean, const float* __restrict__ invstd, int T, int C,
                                  float* __restrict__ part) {
@@ -551,17 +555,16 @@ __global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int
   dgamma[col] = static_cast<float>(sx);
   dbeta[col] = static_cast<float>(s);
   const float gi = gamma[col] * invstd[col];
-  // dq = gi * (dq^ - m1 - x^ * m2) with x^ = (qpre - mean) * invstd, folded
-  // into dq = A dq^ + B qpre + C
+  // dq = gi * (dq^ - m1 - x^ * m2) with x^ = (qpre - mean) * invstd
   const float m1 = training ? static_cast<float>(s / T) : 0.f;
   const float m2 = training ? static_cast<float>(sx / T) : 0.f;
   dbias[col] = training ? 0.f : static_cast<float>(gi * s);
   const float B = -gi * m2 * invstd[col];
-  reinterpret_cast<float4*>(coef)[col] = make_float4(gi, B, -gi * m1 - B * mean[col], 0.f);
+  reinterpret_cast<float4*>(coef)[col] = make_float4(gi, B, -gi * m1, mean[col]);
 }
 
 // One thread per 8 consecutive columns (C % 8 == 0), grid x over the column
-// groups and y over the token rows (as k_bn_apply); coef[c] = (A, B, C, 0)
+// groups and y over the token rows (as k_bn_apply); coef[c] = (A, B, D, mean)
 // from k_bn_bwd_finalize.
 __global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __restrict__ qpre,
                                const float4* __restrict__ coef, int T, int C, __nv_bfloat16* __restrict__ du,
@@ -580,8 +583,8 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __res
     uint32_t out[4];
 #pragma unroll
     for (int u = 0; u < 8; u += 2) {
-      const float r0 = fmaf(k[u].x, gv[u], fmaf(k[u].y, qv[u], k[u].z));
-      const float r1 = fmaf(k[u + 1].x, gv[u + 1], fmaf(k[u + 1].y, qv[u + 1], k[u + 1].z));
+      const float r0 = fmaf(k[u].x, gv[u], fmaf(k[u].y, qv[u] - k[u].w, k[u].z));
+      const float r1 = fmaf(k[u + 1].x, gv[u + 1], fmaf(k[u + 1].y, qv[u + 1] - k[u + 1].w, k[u + 1].z));
       const __nv_bfloat162 b = __floats2bfloat162_rn(r0, r1);
       out[u >> 1] = *reinterpret_cast<const uint32_t*>(&b);
     }

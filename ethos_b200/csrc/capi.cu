@@ -570,6 +570,8 @@ int router_core(const ethos_dims& d, const void* x, const void* w_cat, float* bn
   epi.qs = qs;
   epi.qpre = qpre;
   epi.xp = xp_out;
+  epi.part = nullptr;
+  epi.ldp = 0;
   if ((st = launch_gemm2sm(tm_x, tm_w, T, ncat, static_cast<int>(d.d_model), epi, err, stream, dev)) != ETHOS_OK)
     return st;
   mark(ev, ETHOS_STAGE_PROJECTION, stream);
@@ -1331,7 +1333,7 @@ int64_t padded_keys(const ethos_dims& d) { return (d.num_sub_keys + 127) / 128 *
 // Split an fp32 [rows, cols] matrix (row pitch lds) into bf16 segments (see
 // k_split_bf16).
 int launch_split(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, int64_t ldd,
-                 int64_t seg_off, int nseg, int lo_mask, cudaStream_t stream, const DeviceInfo& dev) {
+                 int64_t seg_off, int nseg, int parts, cudaStream_t stream, const DeviceInfo& dev) {
   const int tx = 128;
   const int gx = (cols + tx - 1) / tx;
   int64_t gy = (static_cast<int64_t>(dev.sm_count) * 16) / gx;
@@ -1340,7 +1342,7 @@ int launch_split(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfl
   if (gy > 65535) gy = 65535;
   count_launch();
   k_split_bf16<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), tx, 0, stream>>>(
-      src, rows, cols, lds, dst, ldd, seg_off, nseg, lo_mask);
+      src, rows, cols, lds, dst, ldd, seg_off, nseg, parts);
   return launch_status();
 }
 
@@ -1348,15 +1350,16 @@ int launch_split(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfl
 // [rows][cols] then lo [rows][cols].
 int split2(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, cudaStream_t stream,
            const DeviceInfo& dev) {
-  return launch_split(src, rows, cols, lds, dst, cols, rows * cols, 2, 2, stream, dev);
+  return launch_split(src, rows, cols, lds, dst, cols, rows * cols, 2, SPLIT_HI_LO, stream, dev);
 }
 
-// The K-concatenated operands of one fp32 GEMM, row-major [rows][3 * cols]:
-// A = [hi | lo | hi] (lo_mask 2), B = [hi | hi | lo] (lo_mask 4).
-int split3(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, bool as_b,
+// The K-concatenated operands of the six-product projection GEMM, row-major
+// [rows][6 * cols]: A = [hi | r | lo | lo | hi | hi], B = [r | hi | lo | hi |
+// lo | hi] (hi*hi last; see SPLIT6_A).
+int split6(const float* src, int64_t rows, int cols, int64_t lds, __nv_bfloat16* dst, bool as_b,
            cudaStream_t stream, const DeviceInfo& dev) {
-  return launch_split(src, rows, cols, lds, dst, 3 * static_cast<int64_t>(cols), cols, 3, as_b ? 4 : 2, stream,
-                      dev);
+  return launch_split(src, rows, cols, lds, dst, 6 * static_cast<int64_t>(cols), cols, 6,
+                      as_b ? SPLIT6_B : SPLIT6_A, stream, dev);
 }
 
 // A split operand: hi and lo bf16 arrays of one layout (row pitch ld,
@@ -1417,8 +1420,9 @@ int warp_blocks(int64_t items, const DeviceInfo& dev) {
 }
 
 struct Fwd32Scratch {
-  __nv_bfloat16* x3;      // [T][3d]
-  __nv_bfloat16* w3;      // [ncat][3d]
+  __nv_bfloat16* x6;      // [T][6d]
+  __nv_bfloat16* w6;      // [ncat][6d]
+  float* pcat;            // [T][ncat] projection partial over K [0, 5.5d)
   float* qpre;            // [T][HQ]
   float* xp;              // [T][dh]
   float2* colp;           // [HQ]
@@ -1445,8 +1449,9 @@ void carve_forward_f32(Carve& c, const ethos_dims& d, int bn_training, bool expe
   const int64_t T = d.tokens, D = d.d_model, H = d.num_heads, HQ = H * d.d_query, half = d.d_query / 2;
   const int64_t dh = d.d_hidden, N = d.num_experts, Kp = padded_keys(d), R = H * d.top_k;
   const int64_t ncat = experts ? HQ + dh : HQ;
-  s->x3 = c.take<__nv_bfloat16>(static_cast<size_t>(T * 3 * D));
-  s->w3 = c.take<__nv_bfloat16>(static_cast<size_t>(ncat * 3 * D));
+  s->x6 = c.take<__nv_bfloat16>(static_cast<size_t>(T * 6 * D));
+  s->w6 = c.take<__nv_bfloat16>(static_cast<size_t>(ncat * 6 * D));
+  s->pcat = c.take<float>(static_cast<size_t>(T * ncat));
   s->qpre = have_qpre ? nullptr : c.take<float>(static_cast<size_t>(T * HQ));
   s->xp = (!experts || have_xp) ? nullptr : c.take<float>(static_cast<size_t>(T * dh));
   s->colp = c.take<float2>(static_cast<size_t>(HQ));
@@ -1631,18 +1636,33 @@ int ethos_layer_forward_f32(const ethos_dims* dims, const float* x, const float*
   float* qhat = save_qhat ? save_qhat : s.qhat;
   const int cb = 256;
 
-  // (1) queries and x_proj: one GEMM on K-concatenated split operands, the
-  //     bias added in the epilogue (model.py:215, 326)
-  if ((st = split3(x, T, D, D, s.x3, false, sm, *dev)) != ETHOS_OK) return st;
-  if ((st = split3(w_cat, ncat, D, D, s.w3, true, sm, *dev)) != ETHOS_OK) return st;
+  // (1) queries and x_proj on the six-product K-concatenated split operands
+  //     (fp32-level qpre, which small-batch BatchNorm amplifies), the bias
+  //     added in the epilogue (model.py:215, 326).  Two launches, each
+  //     accumulating from zero in TMEM: the small products and the first half
+  //     of hi*hi into pcat, then the second half of hi*hi, which adds pcat in
+  //     its epilogue.  Each accumulation chain is then D / 32 steps of the
+  //     large products long instead of D / 16.
+  if ((st = split6(x, T, D, D, s.x6, false, sm, *dev)) != ETHOS_OK) return st;
+  if ((st = split6(w_cat, ncat, D, D, s.w6, true, sm, *dev)) != ETHOS_OK) return st;
   if (!bn_training) {
     count_launch();
     k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, 1, s.colp);
   }
   {
+    const int k0 = 5 * D + D / 2;  // d_model % 256 == 0: both slices 16-byte aligned, K % 64 == 0
+    EpiStoreF32 ep;
+    ep.out = s.pcat;
+    ep.ldo = ncat;
+    ep.M = T;
+    ep.scale = 1.0f;
+    ep.accumulate = 0;
+    if ((st = gemm(GemmOperand{s.x6, 6 * D, false}, GemmOperand{s.w6, 6 * D, false}, T, ncat, k0, 1, ep, dev_err,
+                   sm, *dev)) != ETHOS_OK)
+      return st;
     CUtensorMap tm_x, tm_w;
-    if ((st = make_tmap_bf16(&tm_x, s.x3, T, 3 * D, 128)) != ETHOS_OK) return st;
-    if ((st = make_tmap_bf16(&tm_w, s.w3, ncat, 3 * D, G2_BN / 2)) != ETHOS_OK) return st;
+    if ((st = make_tmap_bf16(&tm_x, s.x6 + k0, T, D / 2, 128, 6 * D)) != ETHOS_OK) return st;
+    if ((st = make_tmap_bf16(&tm_w, s.w6 + k0, ncat, D / 2, G2_BN / 2, 6 * D)) != ETHOS_OK) return st;
     EpiProj epi;
     epi.M = T;
     epi.HQ = HQ;
@@ -1654,7 +1674,9 @@ int ethos_layer_forward_f32(const ethos_dims* dims, const float* x, const float*
     epi.qs = nullptr;
     epi.qpre = qpre;
     epi.xp = xp;
-    if ((st = launch_gemm2sm(tm_x, tm_w, T, ncat, 3 * D, epi, dev_err, sm, *dev)) != ETHOS_OK) return st;
+    epi.part = s.pcat;
+    epi.ldp = ncat;
+    if ((st = launch_gemm2sm(tm_x, tm_w, T, ncat, D / 2, epi, dev_err, sm, *dev)) != ETHOS_OK) return st;
   }
   // (2) BatchNorm (model.py:216): batch statistics and running-stat update in
   //     training mode, running statistics in eval mode
@@ -1667,7 +1689,8 @@ int ethos_layer_forward_f32(const ethos_dims* dims, const float* x, const float*
                                                      bn + 3 * HQ, bn + 4 * HQ, bn_eps, bn_momentum, sbn, s.colp);
   }
   count_launch();
-  k_bn_apply_f32<<<rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(qpre, s.colp, T, H, dq, qhat);
+  k_bn_apply_f32<<<rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(qpre, s.colp, bn_training ? sbn : bn + 3 * HQ,
+                                                            bn + 2 * HQ, T, H, dq, qhat);
   if ((st = launch_status()) != ETHOS_OK) return st;
   // (3) sub-key scores of both halves (model.py:217-221), then top-k, grid
   //     top-k, softmax and id decode (model.py:224-245)
@@ -1675,10 +1698,9 @@ int ethos_layer_forward_f32(const ethos_dims* dims, const float* x, const float*
   if (cudaMemsetAsync(s.keys_s, 0, sizeof(__nv_bfloat16) * 2 * 2 * Kp * half, sm) != cudaSuccess)
     return ETHOS_ERR_CUDA;
   for (int p = 0; p < 2; ++p) {
-    if ((st = launch_split(keys + static_cast<int64_t>(p) * K * half, K, half, half,
-                           s.keys_s + static_cast<int64_t>(p) * Kp * half, half, 2 * Kp * half, 2, 2, sm, *dev)) !=
-        ETHOS_OK)
-      return st;
+    st = launch_split(keys + static_cast<int64_t>(p) * K * half, K, half, half,
+                      s.keys_s + static_cast<int64_t>(p) * Kp * half, half, 2 * Kp * half, 2, SPLIT_HI_LO, sm, *dev);
+    if (st != ETHOS_OK) return st;
   }
   const int64_t qlo = 2 * HT * half;
   for (int p = 0; p < 2; ++p) {

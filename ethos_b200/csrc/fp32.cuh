@@ -7,12 +7,22 @@
 // bits together), and a product is formed as hi*hi + lo*hi + hi*lo with fp32
 // accumulation, which leaves a relative error near 2^-16 per product.  The
 // three partial products run as three accumulating GEMMs on separate hi / lo
-// operand arrays, or, where an epilogue needs the whole sum at once (the query
-// projection), as one GEMM whose operands are the segments concatenated along
-// K ([hi | lo | hi] against [hi | hi | lo]).  Everything between the
-// contractions -- BatchNorm, scores, top-k, softmax, the expert table, GELU,
-// gathers and reductions -- stays in fp32 in the kernels below, which favour
-// plain, coalesced fp32 row access over the bf16 path's packed layouts.
+// operand arrays.  The query projection is the exception: training-mode
+// BatchNorm over a small batch amplifies an error in qpre by up to
+// 1 / (2 sqrt(eps)) (two tokens normalise to +-1, and for a column where they
+// nearly agree the result turns on their difference), so it carries a third
+// part r = bf16(v - hi - lo) (v = hi + lo + r exactly for normal fp32 values)
+// and forms the six products hi*r + r*hi + lo*lo + lo*hi + hi*lo + hi*hi
+// as one GEMM whose operands are the segments concatenated along K, so that
+// its epilogue sees the whole sum at once.  The order matters: the MMA's fp32
+// accumulator loses about half an ulp of the running sum per K step (measured
+// on the device: a relative error of 5.7e-6 over 192 steps of 16 with hi*hi
+// first), so the small products accumulate first, while the sum is small, and
+// hi*hi's D / 16 steps come last.
+// Everything between the contractions -- BatchNorm, scores, top-k, softmax,
+// the expert table, GELU, gathers and reductions -- stays in fp32 in the
+// kernels below, which favour plain, coalesced fp32 row access over the bf16
+// path's packed layouts.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -22,28 +32,43 @@
 namespace ethos {
 
 // ------------------------------------------------------------- split --
-// dst segment s (s < nseg) of row r, column c is at dst[r * ldd + c +
-// s * seg_off] and holds lo = bf16(v - bf16(v)) where bit s of lo_mask is set,
-// else hi = bf16(v).  K-concatenated operand: seg_off = cols, ldd = 3 * cols;
-// separate hi / lo arrays of the source's shape: nseg 2, lo_mask 2,
-// seg_off = rows * ldd.
+// Parts of an fp32 value v: hi = bf16(v), lo = bf16(v - hi), r = bf16(v - hi
+// - lo) (both differences exact in fp32).  dst segment s (s < nseg) of row r,
+// column c is at dst[r * ldd + c + s * seg_off] and holds the part that bits
+// 2s..2s+1 of `parts` select (0 hi, 1 lo, 2 r).  Separate hi / lo arrays of
+// the source's shape: nseg 2, parts SPLIT_HI_LO, seg_off = rows * ldd;
+// K-concatenated operand: seg_off = cols, ldd = nseg * cols.
+constexpr int SPLIT_HI_LO = 1 << 2;
+// The six-product projection operands, smallest products first:
+// A = [hi | r | lo | lo | hi | hi], B = [r | hi | lo | hi | lo | hi].
+constexpr int SPLIT6_A = (2 << 2) | (1 << 4) | (1 << 6);
+constexpr int SPLIT6_B = 2 | (1 << 4) | (1 << 8);
+
 __global__ void k_split_bf16(const float* __restrict__ src, int64_t rows, int cols, int64_t lds,
-                             __nv_bfloat16* __restrict__ dst, int64_t ldd, int64_t seg_off, int nseg, int lo_mask) {
+                             __nv_bfloat16* __restrict__ dst, int64_t ldd, int64_t seg_off, int nseg, int parts) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
     const float v = src[r * lds + c];
-    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+    __nv_bfloat16 part[3];
+    part[0] = __float2bfloat16_rn(v);
+    const float rem = v - __bfloat162float(part[0]);
+    part[1] = __float2bfloat16_rn(rem);
+    part[2] = __float2bfloat16_rn(rem - __bfloat162float(part[1]));
     __nv_bfloat16* d = dst + r * ldd + c;
-    for (int s = 0; s < nseg; ++s) d[s * seg_off] = ((lo_mask >> s) & 1) ? lo : hi;
+    for (int s = 0; s < nseg; ++s) d[s * seg_off] = part[(parts >> (2 * s)) & 3];
   }
 }
 
 // ------------------------------------------------------------ router --
-// Normalised queries q^ = qpre * scale + offset (per column, from
-// k_bn_finalize / k_bn_eval_colp) into qhat [2][H][T][dq/2] (half p, head h).
-__global__ void k_bn_apply_f32(const float* __restrict__ qpre, const float2* __restrict__ colp, int T, int H,
+// Normalised queries q^ = (qpre - center) * scale + beta per column into
+// qhat [2][H][T][dq/2] (half p, head h).  center is the batch mean (training)
+// or the running mean (eval), scale = gamma / sqrt(var + eps) (colp.x of
+// k_bn_finalize / k_bn_eval_colp); the centred form keeps the subtraction
+// exact where qpre and center agree to many bits (the folded qpre * scale +
+// offset form loses those bits to the rounding of the offset).
+__global__ void k_bn_apply_f32(const float* __restrict__ qpre, const float2* __restrict__ colp,
+                               const float* __restrict__ center, const float* __restrict__ beta, int T, int H,
                                int dq, float* __restrict__ qhat) {
   const int C = H * dq;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
@@ -53,10 +78,10 @@ __global__ void k_bn_apply_f32(const float* __restrict__ qpre, const float2* __r
   const int half = dq >> 1;
   const int p = e >= half ? 1 : 0;
   const int i = e - p * half;
-  const float2 cp = colp[col];
+  const float scale = colp[col].x, m = center[col], b = beta[col];
   float* base = qhat + static_cast<int64_t>(p * H + h) * T * half + i;
   for (int t = blockIdx.y; t < T; t += gridDim.y)
-    base[static_cast<int64_t>(t) * half] = fmaf(qpre[static_cast<int64_t>(t) * C + col], cp.x, cp.y);
+    base[static_cast<int64_t>(t) * half] = fmaf(qpre[static_cast<int64_t>(t) * C + col] - m, scale, b);
 }
 
 // Warp-wide arg-max of (value, index) pairs: the larger value wins, the
@@ -417,7 +442,7 @@ __global__ void __launch_bounds__(256) k_router_bwd_f32(const int32_t* __restric
 }
 
 // BatchNorm backward apply (k_bn_bwd_apply with an fp32 destination):
-// du[t][c] = A dq^ + B qpre + C per column.
+// du[t][c] = A dq^ + B (qpre - mean) + D per column, coef[c] = (A, B, D, mean).
 __global__ void k_bn_bwd_apply_f32(const float* __restrict__ dqh, const float* __restrict__ qpre,
                                    const float4* __restrict__ coef, int T, int C, float* __restrict__ du,
                                    int64_t ldu) {
@@ -426,7 +451,7 @@ __global__ void k_bn_bwd_apply_f32(const float* __restrict__ dqh, const float* _
   const float4 k = __ldg(coef + c);
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
     const int64_t o = static_cast<int64_t>(t) * C + c;
-    du[static_cast<int64_t>(t) * ldu + c] = fmaf(k.x, dqh[o], fmaf(k.y, qpre[o], k.z));
+    du[static_cast<int64_t>(t) * ldu + c] = fmaf(k.x, dqh[o], fmaf(k.y, qpre[o] - k.w, k.z));
   }
 }
 

@@ -184,7 +184,10 @@ struct EpiAtomicF32 : EpiNoColParams {
 //    qs[half][h][row][0..dq/2) = hi, [dq/2..dq) = lo.
 //  mode 1 (BatchNorm train): qpre[row][col] = v + bias (fp32) for the batch
 //    statistics pass.
-// x_proj is always written fp32 to xp[row][0..dh).
+// x_proj is always written fp32 to xp[row][0..dh).  With `part` set, the fp32
+// partial sum part[row][col] of an earlier launch over other K columns is
+// added to v first (a contraction split over launches, each accumulating from
+// zero in TMEM).
 struct EpiProj {
   static constexpr int kColParamBytes = 8;  // float2 (scale, offset) or (bias, -)
   static constexpr int kEpiWarps = 8;
@@ -198,6 +201,8 @@ struct EpiProj {
   __nv_bfloat16* qs;
   float* qpre;
   float* xp;
+  const float* part;  // [M][ldp] or nullptr
+  int64_t ldp;
   // epilogue thread `tid` (0..255) stages column n0 + tid
   __device__ __forceinline__ void load_col_params(int n0, uint8_t* dst, int tid) const {
     const int col = n0 + tid;
@@ -205,8 +210,19 @@ struct EpiProj {
     if (col < HQ) v = mode == 1 ? make_float2(__ldg(bias + col), 0.f) : __ldg(colp + col);
     reinterpret_cast<float2*>(dst)[tid] = v;
   }
-  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t* cp,
+  __device__ __forceinline__ void operator()(int row, int col, float (&v)[32], const uint8_t* cp,
                                              const EpiCtx& cx) const {
+    if (part != nullptr && row < M) {
+      const float4* src = reinterpret_cast<const float4*>(part + static_cast<int64_t>(row) * ldp + col);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 a = __ldg(src + j);
+        v[4 * j] += a.x;
+        v[4 * j + 1] += a.y;
+        v[4 * j + 2] += a.z;
+        v[4 * j + 3] += a.w;
+      }
+    }
     if (col >= HQ) {
       char* dst = reinterpret_cast<char*>(xp + static_cast<int64_t>(cx.row0) * dh + (col - HQ));
 #pragma unroll

@@ -170,10 +170,17 @@ def test_fp32_layer_matches_reference_golden_config1():
     assert compared >= 1, "both backward cases met a near-tie; nothing was compared"
 
 
-@pytest.mark.parametrize("T,training", [(1, False), (7, False), (131, False), (2, True), (131, True)])
+@pytest.mark.parametrize("T,training", [(1, False), (7, False), (131, False), (2, True), (3, True), (131, True)])
 def test_fp32_ragged_token_counts(T, training):
-    """Token counts that fill no tile (1, 7, 131) and the smallest batch
-    training-mode BatchNorm accepts (2): output and every gradient at 1e-4."""
+    """Token counts that fill no tile (1, 7, 131) and the smallest batches
+    training-mode BatchNorm accepts (2, 3): output and every gradient at 1e-4.
+
+    The small training batches are the ill-conditioned case: a column whose
+    tokens nearly agree normalises through their difference, which amplifies
+    an error in the projection by up to 1 / (2 sqrt(eps)).  A hi/lo split
+    projection (error near 2^-16) misses the bar there by 10x (dx 1.0e-3 at
+    T = 2, 1.2e-4 at T = 3); the six-product projection holds fp32's own
+    error (1.6e-5 and 7e-7 against an fp64 evaluation)."""
     cfg = CFG1
     sd = _stats_state(seeded_state_dict(EthosExpertLayer(EthosConfig(**cfg)), seed=6))
     dims = dims_of(cfg)
@@ -187,14 +194,8 @@ def test_fp32_ragged_token_counts(T, training):
     y_ref, _, _ = orc.layer_forward_given_ids(xr, p, ids, training)
     assert rel_err(y, y_ref.detach()) <= TOL
     (y_ref * gy).sum().backward()
-    assert rel_err(dx, xr.grad) <= TOL
+    assert rel_err(dx, xr.grad) <= TOL, rel_err(dx, xr.grad)
     for n, g_ref in oracle_grads(p, dims["num_heads"]).items():
         if training and "query_projs" in n and n.endswith(".bias"):
-            continue
-        if training and T == 2 and "query_projs" in n:
-            # two samples normalise to +-1 whatever their values: the query
-            # projections get no gradient through BatchNorm (both sides hold
-            # fp32 rounding noise)
-            assert grads[n].abs().max().item() <= 1e-5 and g_ref.abs().max().item() <= 1e-5, n
-            continue
+            continue  # zero up to rounding under batch statistics
         assert rel_err(grads[n], g_ref) <= TOL, (n, rel_err(grads[n], g_ref))
