@@ -65,6 +65,14 @@ EXPORTS = {
                                   _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P, _P]),
     "ethos_router_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _P, _P, _SZ,
                                   _P, _P]),
+    "ethos_expert_backward_workspace_size": (_SZ, [_DIMS]),
+    # dims, latents, w1, ids, weights, xp, dot, dhacc, htab, gtab, dxp, d_weights, d_latents,
+    # d_w1, workspace, workspace_bytes, dev_err, stream
+    "ethos_expert_backward": (_I, [_DIMS] + [_P] * 14 + [_SZ, _P, _P]),
+    "ethos_router_backward_workspace_size": (_SZ, [_DIMS]),
+    # dims, bn_training, eps, x, w_cat, bn, keys, ids, weights, d_weights, save_qpre, save_bn,
+    # dx, accumulate_dx, d_wq, d_bn, d_keys, workspace, workspace_bytes, dev_err, stream
+    "ethos_router_backward": (_I, [_DIMS, _I, _F] + [_P] * 10 + [_I] + [_P] * 4 + [_SZ, _P, _P]),
     "ethos_expert_forward": (_I, [_DIMS, _I, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "ethos_expert_table_build": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_router_forward_noalloc": (_I, [_DIMS, _P, _P, _P, _F, _P, _P, _P, _P, _P]),

@@ -31,7 +31,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[ETHOS_NOALLOC_S
 
 namespace {
 
-constexpr int kAbiVersion = 5;
+constexpr int kAbiVersion = 6;
 
 // The device GELU variants the kernels use, evaluated on x [n] (n even) into
 // out [5, n]: gelu_erf, gelu_erf2 (pairs), gelu_erf_and_grad2 (value, then
@@ -679,6 +679,245 @@ int launch_router_bwd(const ethos_dims& d, const int32_t* ids, const float* w, c
   return launch_status();
 }
 
+// Scratch of ethos_expert_backward: the expert half of BwdScratch plus a
+// [T, dh] bf16 operand row block for dxp (the kernel writes it as a GEMM
+// operand; only the fp32 dxp is returned).
+void carve_expert_backward(Carve& c, const ethos_dims& d, BwdScratch* s) {
+  const int64_t T = d.tokens, N = d.num_experts, R = d.num_heads * d.top_k;
+  *s = BwdScratch{};
+  s->htab = c.take<__half>(static_cast<size_t>(N * EX_DH));
+  s->gtab = c.take<__half>(static_cast<size_t>(N * EX_DH));
+  s->ca = c.take<float>(static_cast<size_t>(T * R));
+  s->cd = c.take<float>(static_cast<size_t>(T * R));
+  s->du = c.take<__nv_bfloat16>(static_cast<size_t>(T * EX_DH));
+  s->cnt = c.take<int>(static_cast<size_t>(N));
+  s->offs = c.take<int>(static_cast<size_t>(N));
+  s->cursor = c.take<int>(static_cast<size_t>(N));
+  s->bsums = c.take<int>(1024);
+  s->total = c.take<int>(4);
+  s->perm = c.take<int>(static_cast<size_t>(T * R));
+  s->dP = c.take<__nv_bfloat16>(static_cast<size_t>(N * EX_DH));
+  s->gx = c.take<__nv_bfloat16>(static_cast<size_t>(T * 2 * EX_DH));
+}
+
+// Scratch of ethos_router_backward: the router half of BwdScratch, the dq
+// operand [T, H*dq] bf16, and the recomputed normalised queries qs with
+// their per-column affine.
+struct RouterBwdExtra {
+  __nv_bfloat16* qs;  // [2][H][T][dq]
+  float2* colp;       // [H*dq]
+};
+
+void carve_router_backward(Carve& c, const ethos_dims& d, BwdScratch* s, RouterBwdExtra* x) {
+  const int64_t T = d.tokens, HQ = d.num_heads * d.d_query;
+  *s = BwdScratch{};
+  s->du = c.take<__nv_bfloat16>(static_cast<size_t>(T * HQ));
+  s->dqhat = c.take<float>(static_cast<size_t>(T * HQ));
+  s->dS = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.num_sub_keys));
+  s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
+  s->part = c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2);
+  s->coef = c.take<float>(static_cast<size_t>(4 * HQ));
+  s->stats = c.take<float>(static_cast<size_t>(2 * HQ));
+  x->qs = c.take<__nv_bfloat16>(static_cast<size_t>(2 * T * HQ));
+  x->colp = c.take<float2>(static_cast<size_t>(HQ));
+}
+
+// Inputs and outputs of the expert half of the backward.
+struct ExpertBwdIO {
+  const void* latents;
+  const void* w1;
+  const int32_t* ids;
+  const float* weights;
+  const float* xp;     // fp32 [T, dh]
+  const float* dot;    // fp32 [T, R]
+  const float* dhacc;  // fp32 [T, dh]
+  const void* htab;    // fp16 [N, dh] or NULL (then built here with gtab)
+  const void* gtab;
+  float* dxp;          // fp32 [T, dh] out
+  __nv_bfloat16* du;   // bf16 copy of dxp at du[t * ldu + du_off + j]
+  int64_t ldu;
+  int du_off;
+  float* dw;           // fp32 [T, R] out: dL/d(routing weight)
+  float* d_latents;
+  float* d_w1;
+};
+
+// Expert half of the backward (the gradients autograd takes through the
+// expert loop of model.py:306-336 given hacc's gradient): per-selection
+// weight gradients and dxp, then per-expert dP by a counting sort of the
+// selections, dE = dP W1 and dW1 = dP^T E.  Scratch from s: htab / gtab
+// (when io.htab is NULL), ca, cd, gx, the sort arrays and dP.
+int expert_bwd_core(const ethos_dims& d, const ExpertBwdIO& io, const BwdScratch& s, int* dev_err,
+                    cudaStream_t sm, const DeviceInfo& dev) {
+  const int T = static_cast<int>(d.tokens), N = static_cast<int>(d.num_experts);
+  const int R = static_cast<int>(d.num_heads * d.top_k);
+  const int cb = 256;
+  const int eblocks = dev.sm_count * 8;
+  int st;
+  if (cudaMemsetAsync(io.d_w1, 0, sizeof(float) * EX_DH * EX_DL, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(s.cnt, 0, sizeof(int) * N, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  // per-expert tables H = gelu(E W1^T), G = gelu'(E W1^T) (fp16), unless the
+  // forward kept them
+  const __half* htab_ = io.htab ? static_cast<const __half*>(io.htab) : s.htab;
+  const __half* gtab_ = io.gtab ? static_cast<const __half*>(io.gtab) : s.gtab;
+  if (io.htab == nullptr) {
+    EpiGeluBwdF16 e;
+    e.h_out = s.htab;
+    e.g_out = s.gtab;
+    e.ldo = EX_DH;
+    e.M = N;
+    if ((st = gemm(GemmOperand{io.latents, EX_DL, false}, GemmOperand{io.w1, EX_DL, false}, N, EX_DH, EX_DL, 1, e,
+                   dev_err, sm, dev)) != ETHOS_OK)
+      return st;
+  }
+  // per token: dw, a, ddot per selection; dxp (fp32 + bf16 operand)
+  {
+    if (BGATHER_STAGES - 1 < R / GATHER_ROWS) {  // one dhacc / xp buffer per warp
+      constexpr int bytes = bgather_smem_bytes(BGATHER_WARPS, BGATHER_STAGES, 1);
+      auto kern = k_expert_bwd_gather<BGATHER_WARPS, BGATHER_STAGES, 1>;
+      if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
+      int blocks = (T + BGATHER_WARPS - 1) / BGATHER_WARPS;
+      if (blocks > dev.sm_count) blocks = dev.sm_count;
+      count_launch();
+      kern<<<blocks, BGATHER_WARPS * 32, bytes, sm>>>(htab_, io.ids, io.weights, io.dot, io.dhacc, io.dw, s.ca, s.cd,
+                                                      io.dxp, io.du, io.ldu, io.du_off, io.xp, s.gx, T, R, N,
+                                                      dev_err);
+    } else {  // R = 4: double buffers, 2 stages
+      constexpr int W = BGATHER_SMALL_R_WARPS;
+      constexpr int bytes = bgather_smem_bytes(W, 2, 2);
+      auto kern = k_expert_bwd_gather<W, 2, 2>;
+      if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
+      int blocks = (T + W - 1) / W;
+      if (blocks > dev.sm_count) blocks = dev.sm_count;
+      count_launch();
+      kern<<<blocks, W * 32, bytes, sm>>>(htab_, io.ids, io.weights, io.dot, io.dhacc, io.dw, s.ca, s.cd, io.dxp,
+                                          io.du, io.ldu, io.du_off, io.xp, s.gx, T, R, N, dev_err);
+    }
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  // selections grouped by expert (counting sort)
+  {
+    const int64_t nsel = static_cast<int64_t>(T) * R;
+    count_launch();
+    k_count_experts<<<eblocks, cb, 0, sm>>>(io.ids, nsel, N, s.cnt, dev_err);
+    const int nblk = (N + 1023) / 1024;
+    if (nblk > 1024) return ETHOS_ERR_UNSUPPORTED_SHAPE;
+    count_launch();
+    k_scan_blocks<<<nblk, 1024, 0, sm>>>(s.cnt, N, s.offs, s.bsums);
+    count_launch();
+    k_scan_sums<<<1, 1024, 0, sm>>>(s.bsums, nblk, s.total);
+    count_launch();
+    k_scan_add<<<nblk, 1024, 0, sm>>>(s.offs, N, s.bsums, s.cursor);
+    count_launch();
+    k_scatter_experts<<<eblocks, cb, 0, sm>>>(io.ids, nsel, N, s.cursor, s.perm);
+    if ((st = launch_status()) != ETHOS_OK) return st;
+  }
+  // dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
+  count_launch();
+  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, s.total, s.ca, s.cd, s.gx, gtab_, s.dP, N, R);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  // dE = dP W1       (W1 read in place, MN-major)
+  {
+    EpiStoreF32 e;
+    e.out = io.d_latents;
+    e.ldo = EX_DL;
+    e.M = N;
+    e.scale = 1.0f;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{s.dP, EX_DH, false}, GemmOperand{io.w1, EX_DL, true}, N, EX_DL, EX_DH, 1, e, dev_err,
+                   sm, dev)) != ETHOS_OK)
+      return st;
+  }
+  // dW1 = dP^T E     (both read in place, MN-major; split-K over experts)
+  {
+    EpiAtomicF32 e;
+    e.out = io.d_w1;
+    e.ldo = EX_DL;
+    e.M = EX_DH;
+    e.scale = 1.0f;
+    if ((st = gemm(GemmOperand{s.dP, EX_DH, true}, GemmOperand{io.latents, EX_DL, true}, EX_DH, EX_DL, N,
+                   auto_ksplit(EX_DH, EX_DL, N, dev), e, dev_err, sm, dev)) != ETHOS_OK)
+      return st;
+  }
+  return ETHOS_OK;
+}
+
+// Inputs and outputs of the router half of the backward.
+struct RouterBwdIO {
+  int bn_training;
+  float bn_eps;
+  const float* bn;
+  const void* key_cat;
+  const int32_t* ids;
+  const float* weights;
+  const float* dw;        // fp32 [T, R]: dL/d(routing weight)
+  const float* qpre;      // fp32 [T, H*dq]
+  const float* save_bn;   // fp32 [2, H*dq] (training) or NULL
+  const void* qs;         // bf16 [2][H][T][dq] normalised queries (hi | lo)
+  __nv_bfloat16* du;      // dq (bf16) out at du[t * ldu + c], c < H*dq
+  int64_t ldu;
+  float* d_bn;
+  float* d_keys;
+};
+
+// Router half of the backward (model.py:208-254 under autograd): softmax
+// backward into the selected grid scores, the dense sub-key score gradient
+// dS and dq^, dK = dS^T q^, then BatchNorm's backward into dq and the
+// bias / gamma / beta gradients.  Scratch from s: dqhat, dS, part, coef,
+// stats.
+int router_bwd_core(const ethos_dims& d, const RouterBwdIO& io, const BwdScratch& s, int* dev_err,
+                    cudaStream_t sm, const DeviceInfo& dev) {
+  const int T = static_cast<int>(d.tokens), H = static_cast<int>(d.num_heads);
+  const int dq = static_cast<int>(d.d_query), HQ = H * dq, K = static_cast<int>(d.num_sub_keys), half = dq / 2;
+  const int cb = 256;
+  int st;
+  if (cudaMemsetAsync(io.d_keys, 0, sizeof(float) * 2 * K * half, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
+  if (cudaMemsetAsync(s.dS, 0, sizeof(__nv_bfloat16) * static_cast<size_t>(H) * 2 * T * K, sm) != cudaSuccess)
+    return ETHOS_ERR_CUDA;
+  // softmax backward, dq^ and the dense sub-key score gradient dS
+  const __nv_bfloat16* keys = static_cast<const __nv_bfloat16*>(io.key_cat);
+  switch (d.top_k) {
+    case 4: st = launch_router_bwd<4>(d, io.ids, io.weights, io.dw, keys, dq, s.dqhat, s.dS, sm, dev); break;
+    case 8: st = launch_router_bwd<8>(d, io.ids, io.weights, io.dw, keys, dq, s.dqhat, s.dS, sm, dev); break;
+    default: st = launch_router_bwd<16>(d, io.ids, io.weights, io.dw, keys, dq, s.dqhat, s.dS, sm, dev); break;
+  }
+  if (st != ETHOS_OK) return st;
+  // dK_p = dS_p^T q^_p over all heads and tokens (q^ = hi part of qs; both
+  // [2][H][T][.] so the (h, t) rows of a half are contiguous)
+  for (int p = 0; p < 2; ++p) {
+    EpiAtomicF32 e;
+    e.out = io.d_keys + static_cast<int64_t>(p) * K * half;
+    e.ldo = half;
+    e.M = K;
+    e.scale = 1.0f;
+    const __nv_bfloat16* dSp = s.dS + static_cast<int64_t>(p) * H * T * K;
+    const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(io.qs) + static_cast<int64_t>(p) * H * T * dq;
+    const int KK = H * T;
+    if ((st = gemm(GemmOperand{dSp, K, true}, GemmOperand{qh, dq, true}, K, half, KK, auto_ksplit(K, half, KK, dev),
+                   e, dev_err, sm, dev)) != ETHOS_OK)
+      return st;
+  }
+  // BatchNorm backward -> dq (bf16 into du[:, :HQ]), dbias, dgamma, dbeta
+  const float* mean = io.save_bn;
+  const float* invstd = io.save_bn ? io.save_bn + HQ : nullptr;
+  if (!io.bn_training) {
+    count_launch();
+    k_bn_eval_stats<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(io.bn, HQ, io.bn_eps, s.stats, s.stats + HQ);
+    mean = s.stats;
+    invstd = s.stats + HQ;
+  }
+  dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+  count_launch();
+  k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, io.qpre, mean, invstd, T, HQ, s.part);
+  count_launch();
+  k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, io.bn_training, io.bn + HQ, mean,
+                                                      invstd, io.d_bn + HQ, io.d_bn + 2 * HQ, io.d_bn, s.coef);
+  count_launch();
+  k_bn_bwd_apply<<<bn_rows_grid(HQ, T, cb, dev), cb, 0, sm>>>(s.dqhat, io.qpre, reinterpret_cast<const float4*>(s.coef),
+                                                              T, HQ, io.du, io.ldu);
+  return launch_status();
+}
+
 }  // namespace
 
 // =================================================================== ABI ==
@@ -830,8 +1069,10 @@ int ethos_router_forward(const ethos_dims* dims, const void* x, const void* w_ca
   carve_forward(c, *dims, bn_training, false, false, save_qpre == nullptr, save_bn == nullptr, false, &s);
   float* qpre = save_qpre ? save_qpre : s.qpre;
   float* sbn = save_bn ? save_bn : s.save_bn;
+  // with save_qpre the pre-BatchNorm queries are kept in eval mode too (the
+  // two-pass form), as ethos_router_backward needs them
   return router_core(*dims, x, w_cat, bn, bn_eps, bn_momentum, bn_training, key_cat, ids, weights, false, nullptr,
-                     s, s.qs, qpre, false, sbn, dev_err, static_cast<cudaStream_t>(stream), *dev);
+                     s, s.qs, qpre, save_qpre != nullptr, sbn, dev_err, static_cast<cudaStream_t>(stream), *dev);
 }
 
 int ethos_expert_forward(const ethos_dims* dims, int expert_path, const void* latents, const void* w1,
@@ -1068,21 +1309,15 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
   Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
   BwdScratch s;
   carve_backward(c, d, &s);
-  const int T = static_cast<int>(d.tokens), D = static_cast<int>(d.d_model), N = static_cast<int>(d.num_experts);
-  const int H = static_cast<int>(d.num_heads), R = static_cast<int>(d.num_heads * d.top_k);
-  const int dq = static_cast<int>(d.d_query), HQ = H * dq, K = static_cast<int>(d.num_sub_keys), half = dq / 2;
+  const int T = static_cast<int>(d.tokens), D = static_cast<int>(d.d_model);
+  const int H = static_cast<int>(d.num_heads), HQ = H * static_cast<int>(d.d_query);
   const int LDU = HQ + EX_DH;
   const float invH = 1.0f / static_cast<float>(H);
   const int cb = 256;
   const int eblocks = dev->sm_count * 8;
 
   // outputs that are accumulated
-  if (cudaMemsetAsync(d_w1, 0, sizeof(float) * EX_DH * EX_DL, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
   if (cudaMemsetAsync(d_w2, 0, sizeof(float) * 2 * D * EX_DH, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
-  if (cudaMemsetAsync(d_keys, 0, sizeof(float) * 2 * K * half, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
-  if (cudaMemsetAsync(s.cnt, 0, sizeof(int) * N, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
-  if (cudaMemsetAsync(s.dS, 0, sizeof(__nv_bfloat16) * static_cast<size_t>(H) * 2 * T * K, sm) != cudaSuccess)
-    return ETHOS_ERR_CUDA;
 
   const void* dy16 = dy;
   if (dy_fp32) {
@@ -1113,135 +1348,46 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                    auto_ksplit(D, EX_DH, T, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
       return st;
   }
-  // (3) per-expert tables H = gelu(E W1^T), G = gelu'(E W1^T)  (fp16), unless
-  // the forward kept them
-  const __half* htab_ = htab ? static_cast<const __half*>(htab) : s.htab;
-  const __half* gtab_ = gtab ? static_cast<const __half*>(gtab) : s.gtab;
-  if (htab == nullptr) {
-    EpiGeluBwdF16 e;
-    e.h_out = s.htab;
-    e.g_out = s.gtab;
-    e.ldo = EX_DH;
-    e.M = N;
-    if ((st = gemm(GemmOperand{latents, EX_DL, false}, GemmOperand{w1, EX_DL, false}, N, EX_DH, EX_DL, 1, e, dev_err,
-                   sm, *dev)) != ETHOS_OK)
-      return st;
-  }
-  // (4) per token: dw, a, ddot per selection; dxp (fp32 + bf16 into du)
+  // (3)-(8) experts: dw, dxp (bf16 into du[:, HQ:]), d_latents, d_w1
   {
-    if (BGATHER_STAGES - 1 < R / GATHER_ROWS) {  // one dhacc / xp buffer per warp
-      constexpr int bytes = bgather_smem_bytes(BGATHER_WARPS, BGATHER_STAGES, 1);
-      auto kern = k_expert_bwd_gather<BGATHER_WARPS, BGATHER_STAGES, 1>;
-      if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
-      int blocks = (T + BGATHER_WARPS - 1) / BGATHER_WARPS;
-      if (blocks > dev->sm_count) blocks = dev->sm_count;
-      count_launch();
-      kern<<<blocks, BGATHER_WARPS * 32, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd,
-                                                      s.dxp, s.du, LDU, HQ, save_xp, s.gx, T, R, N, dev_err);
-    } else {  // R = 4: double buffers, 2 stages
-      constexpr int W = BGATHER_SMALL_R_WARPS;
-      constexpr int bytes = bgather_smem_bytes(W, 2, 2);
-      auto kern = k_expert_bwd_gather<W, 2, 2>;
-      if ((st = smem_attr_once(reinterpret_cast<const void*>(kern), bytes)) != ETHOS_OK) return st;
-      int blocks = (T + W - 1) / W;
-      if (blocks > dev->sm_count) blocks = dev->sm_count;
-      count_launch();
-      kern<<<blocks, W * 32, bytes, sm>>>(htab_, ids, weights, save_dot, s.dhacc, s.dw, s.ca, s.cd, s.dxp, s.du,
-                                          LDU, HQ, save_xp, s.gx, T, R, N, dev_err);
-    }
-    if ((st = launch_status()) != ETHOS_OK) return st;
-  }
-  // (5) selections grouped by expert (counting sort)
-  {
-    const int64_t nsel = static_cast<int64_t>(T) * R;
-    count_launch();
-    k_count_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cnt, dev_err);
-    const int nblk = (N + 1023) / 1024;
-    if (nblk > 1024) return ETHOS_ERR_UNSUPPORTED_SHAPE;
-    count_launch();
-    k_scan_blocks<<<nblk, 1024, 0, sm>>>(s.cnt, N, s.offs, s.bsums);
-    count_launch();
-    k_scan_sums<<<1, 1024, 0, sm>>>(s.bsums, nblk, s.total);
-    count_launch();
-    k_scan_add<<<nblk, 1024, 0, sm>>>(s.offs, N, s.bsums, s.cursor);
-    count_launch();
-    k_scatter_experts<<<eblocks, cb, 0, sm>>>(ids, nsel, N, s.cursor, s.perm);
-    if ((st = launch_status()) != ETHOS_OK) return st;
-  }
-  // (6) dP[e] = G[e] * sum over e's selections of (a dhacc_t + ddot xp_t)
-  count_launch();
-  k_expert_dP<<<eblocks, 256, 0, sm>>>(s.offs, s.perm, s.total, s.ca, s.cd, s.gx, gtab_, s.dP, N, R);
-  if ((st = launch_status()) != ETHOS_OK) return st;
-  // (7) dE = dP W1       (W1 read in place, MN-major)
-  {
-    EpiStoreF32 e;
-    e.out = d_latents;
-    e.ldo = EX_DL;
-    e.M = N;
-    e.scale = 1.0f;
-    e.accumulate = 0;
-    if ((st = gemm(GemmOperand{s.dP, EX_DH, false}, GemmOperand{w1, EX_DL, true}, N, EX_DL, EX_DH, 1, e, dev_err, sm,
-                   *dev)) != ETHOS_OK)
-      return st;
-  }
-  // (8) dW1 = dP^T E     (both read in place, MN-major; split-K over experts)
-  {
-    EpiAtomicF32 e;
-    e.out = d_w1;
-    e.ldo = EX_DL;
-    e.M = EX_DH;
-    e.scale = 1.0f;
-    if ((st = gemm(GemmOperand{s.dP, EX_DH, true}, GemmOperand{latents, EX_DL, true}, EX_DH, EX_DL, N,
-                   auto_ksplit(EX_DH, EX_DL, N, *dev), e, dev_err, sm, *dev)) != ETHOS_OK)
-      return st;
+    ExpertBwdIO io;
+    io.latents = latents;
+    io.w1 = w1;
+    io.ids = ids;
+    io.weights = weights;
+    io.xp = save_xp;
+    io.dot = save_dot;
+    io.dhacc = s.dhacc;
+    io.htab = htab;
+    io.gtab = gtab;
+    io.dxp = s.dxp;
+    io.du = s.du;
+    io.ldu = LDU;
+    io.du_off = HQ;
+    io.dw = s.dw;
+    io.d_latents = d_latents;
+    io.d_w1 = d_w1;
+    if ((st = expert_bwd_core(d, io, s, dev_err, sm, *dev)) != ETHOS_OK) return st;
   }
   mark(stage_events, ETHOS_BWD_STAGE_EXPERTS, sm);  // d_latents, d_w1 final
-  // (9) router: softmax backward, dq^ and the dense sub-key score gradient dS
-  switch (d.top_k) {
-    case 4: st = launch_router_bwd<4>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq, s.dqhat,
-                                     s.dS, sm, *dev); break;
-    case 8: st = launch_router_bwd<8>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq, s.dqhat,
-                                     s.dS, sm, *dev); break;
-    default: st = launch_router_bwd<16>(d, ids, weights, s.dw, static_cast<const __nv_bfloat16*>(key_cat), dq,
-                                        s.dqhat, s.dS, sm, *dev); break;
-  }
-  if (st != ETHOS_OK) return st;
-  // (10) dK_p = dS_p^T q^_p over all heads and tokens (q^ = hi part of qs;
-  //      both [2][H][T][.] so the (h, t) rows of a half are contiguous)
-  for (int p = 0; p < 2; ++p) {
-    EpiAtomicF32 e;
-    e.out = d_keys + static_cast<int64_t>(p) * K * half;
-    e.ldo = half;
-    e.M = K;
-    e.scale = 1.0f;
-    const __nv_bfloat16* dSp = s.dS + static_cast<int64_t>(p) * H * T * K;
-    const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(save_qs) + static_cast<int64_t>(p) * H * T * dq;
-    const int KK = H * T;
-    if ((st = gemm(GemmOperand{dSp, K, true}, GemmOperand{qh, dq, true}, K, half, KK, auto_ksplit(K, half, KK, *dev),
-                   e, dev_err, sm, *dev)) != ETHOS_OK)
-      return st;
-  }
-  // (11) BatchNorm backward -> dq (bf16 into du[:, :HQ]), dbias, dgamma, dbeta
+  // (9)-(11) router: dq (bf16 into du[:, :HQ]), d_keys, d_bn
   {
-    const float* mean = save_bn;
-    const float* invstd = save_bn ? save_bn + HQ : nullptr;
-    if (!bn_training) {
-      count_launch();
-      k_bn_eval_stats<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, s.stats, s.stats + HQ);
-      mean = s.stats;
-      invstd = s.stats + HQ;
-    }
-    dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
-    count_launch();
-    k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, save_qpre, mean, invstd, T, HQ, s.part);
-    count_launch();
-    k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, bn_training, bn + HQ, mean,
-                                                        invstd, d_bn + HQ, d_bn + 2 * HQ, d_bn, s.coef);
-    count_launch();
-    k_bn_bwd_apply<<<bn_rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(s.dqhat, save_qpre,
-                                                                 reinterpret_cast<const float4*>(s.coef), T, HQ,
-                                                                 s.du, LDU);
-    if ((st = launch_status()) != ETHOS_OK) return st;
+    RouterBwdIO io;
+    io.bn_training = bn_training;
+    io.bn_eps = bn_eps;
+    io.bn = bn;
+    io.key_cat = key_cat;
+    io.ids = ids;
+    io.weights = weights;
+    io.dw = s.dw;
+    io.qpre = save_qpre;
+    io.save_bn = save_bn;
+    io.qs = save_qs;
+    io.du = s.du;
+    io.ldu = LDU;
+    io.d_bn = d_bn;
+    io.d_keys = d_keys;
+    if ((st = router_bwd_core(d, io, s, dev_err, sm, *dev)) != ETHOS_OK) return st;
   }
   // (12) dx = du @ W_cat          (W_cat read in place, MN-major)
   {
@@ -1280,6 +1426,141 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
       return st;
   }
   mark(stage_events, ETHOS_BWD_STAGE_END, sm);
+  return ETHOS_OK;
+}
+
+size_t ethos_expert_backward_workspace_size(const ethos_dims* dims) {
+  if (check_dims_impl(dims) != ETHOS_OK) return 0;
+  Carve c{nullptr, 0, 0};
+  BwdScratch s;
+  carve_expert_backward(c, *dims, &s);
+  return c.off + 256;
+}
+
+int ethos_expert_backward(const ethos_dims* dims, const void* latents, const void* w1, const int32_t* ids,
+                          const float* weights, const float* xp, const float* dot, const float* dhacc,
+                          const void* htab, const void* gtab, float* dxp, float* d_weights, float* d_latents,
+                          float* d_w1, void* workspace, size_t workspace_bytes, int* dev_err, void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!latents || !w1 || !ids || !weights || !xp || !dot || !dhacc || !dxp || !d_weights || !d_latents || !d_w1 ||
+      !workspace || !dev_err)
+    return ETHOS_ERR_INVALID_ARG;
+  if ((htab == nullptr) != (gtab == nullptr)) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(xp) || !aligned16(dhacc) || !aligned16(dxp) || !aligned16(latents) || !aligned16(w1))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  if (workspace_bytes < ethos_expert_backward_workspace_size(dims)) return ETHOS_ERR_WORKSPACE;
+  const ethos_dims& d = *dims;
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  BwdScratch s;
+  carve_expert_backward(c, d, &s);
+  ExpertBwdIO io;
+  io.latents = latents;
+  io.w1 = w1;
+  io.ids = ids;
+  io.weights = weights;
+  io.xp = xp;
+  io.dot = dot;
+  io.dhacc = dhacc;
+  io.htab = htab;
+  io.gtab = gtab;
+  io.dxp = dxp;
+  io.du = s.du;
+  io.ldu = EX_DH;
+  io.du_off = 0;
+  io.dw = d_weights;
+  io.d_latents = d_latents;
+  io.d_w1 = d_w1;
+  return expert_bwd_core(d, io, s, dev_err, static_cast<cudaStream_t>(stream), *dev);
+}
+
+size_t ethos_router_backward_workspace_size(const ethos_dims* dims) {
+  if (check_dims_impl(dims) != ETHOS_OK) return 0;
+  Carve c{nullptr, 0, 0};
+  BwdScratch s;
+  RouterBwdExtra x;
+  carve_router_backward(c, *dims, &s, &x);
+  return c.off + 256;
+}
+
+int ethos_router_backward(const ethos_dims* dims, int bn_training, float bn_eps, const void* x, const void* w_cat,
+                          const float* bn, const void* key_cat, const int32_t* ids, const float* weights,
+                          const float* d_weights, const float* save_qpre, const float* save_bn, float* dx,
+                          int accumulate_dx, float* d_wq, float* d_bn, float* d_keys, void* workspace,
+                          size_t workspace_bytes, int* dev_err, void* stream) {
+  int st = check_dims_impl(dims);
+  if (st != ETHOS_OK) return st;
+  if (!x || !w_cat || !bn || !key_cat || !ids || !weights || !d_weights || !save_qpre || !dx || !d_wq || !d_bn ||
+      !d_keys || !workspace || !dev_err)
+    return ETHOS_ERR_INVALID_ARG;
+  if (bn_training && !save_bn) return ETHOS_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w_cat) || !aligned16(save_qpre) || !aligned16(dx) || !aligned16(d_wq) ||
+      !aligned16(key_cat))
+    return ETHOS_ERR_ALIGNMENT;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  if (workspace_bytes < ethos_router_backward_workspace_size(dims)) return ETHOS_ERR_WORKSPACE;
+  const ethos_dims& d = *dims;
+  cudaStream_t sm = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<char*>(workspace), 0, workspace_bytes};
+  BwdScratch s;
+  RouterBwdExtra xs;
+  carve_router_backward(c, d, &s, &xs);
+  const int T = static_cast<int>(d.tokens), D = static_cast<int>(d.d_model);
+  const int H = static_cast<int>(d.num_heads), dq = static_cast<int>(d.d_query), HQ = H * dq;
+  const int cb = 256;
+  // the forward's normalised queries, recomputed from qpre with the affine
+  // the forward used (batch statistics or running statistics)
+  count_launch();
+  if (bn_training)
+    k_bn_colp_from_stats<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, save_bn, HQ, xs.colp);
+  else
+    k_bn_eval_colp<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(bn, HQ, bn_eps, 1, xs.colp);
+  count_launch();
+  k_bn_apply<<<bn_rows_grid(HQ, T, cb, *dev), cb, 0, sm>>>(save_qpre, xs.colp, T, H, dq, xs.qs);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  RouterBwdIO io;
+  io.bn_training = bn_training;
+  io.bn_eps = bn_eps;
+  io.bn = bn;
+  io.key_cat = key_cat;
+  io.ids = ids;
+  io.weights = weights;
+  io.dw = d_weights;
+  io.qpre = save_qpre;
+  io.save_bn = save_bn;
+  io.qs = xs.qs;
+  io.du = s.du;
+  io.ldu = HQ;
+  io.d_bn = d_bn;
+  io.d_keys = d_keys;
+  if ((st = router_bwd_core(d, io, s, dev_err, sm, *dev)) != ETHOS_OK) return st;
+  // dx (+)= dq @ W_q    (W_q = the first H*dq rows of w_cat, read in place)
+  {
+    EpiStoreF32 e;
+    e.out = dx;
+    e.ldo = D;
+    e.M = T;
+    e.scale = 1.0f;
+    e.accumulate = accumulate_dx ? 1 : 0;
+    if ((st = gemm(GemmOperand{s.du, HQ, false}, GemmOperand{w_cat, D, true}, T, D, HQ, 1, e, dev_err, sm,
+                   *dev)) != ETHOS_OK)
+      return st;
+  }
+  // dWq = dq^T x   [HQ, d]
+  {
+    EpiStoreF32 e;
+    e.out = d_wq;
+    e.ldo = D;
+    e.M = HQ;
+    e.scale = 1.0f;
+    e.accumulate = 0;
+    if ((st = gemm(GemmOperand{s.du, HQ, true}, GemmOperand{x, D, true}, HQ, D, T, 1, e, dev_err, sm, *dev)) !=
+        ETHOS_OK)
+      return st;
+  }
   return ETHOS_OK;
 }
 

@@ -862,6 +862,17 @@ __global__ void k_bn_eval_colp(const float* __restrict__ bn, int C, float eps, i
   colp[col] = make_float2(scale, beta - (rm - bias) * scale);
 }
 
+// Training-mode (scale, offset) from the batch statistics a forward saved
+// (mean, 1/sqrt(var + eps)), computed exactly as k_bn_finalize computes them,
+// so that a backward recomputing q^ from qpre gets the forward's values.
+__global__ void k_bn_colp_from_stats(const float* __restrict__ bn, const float* __restrict__ stats, int C,
+                                     float2* __restrict__ colp) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= C) return;
+  const float scale = stats[C + col] * bn[C + col];
+  colp[col] = make_float2(scale, bn[2 * C + col] - stats[col] * scale);
+}
+
 // Normalisation pass on qpre [T, C] -> split-bf16 scoring operand
 // qs[p][h][t][hi | lo].  One thread per 8 consecutive columns.
 // Grid: x covers the column groups of 8 (blockDim.x threads each), y walks the

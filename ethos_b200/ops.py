@@ -359,6 +359,73 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
 
 
 # ----------------------------------------------------------- fp32 path --
+def expert_backward(latents, w1, ids, weights, xp, dot, dhacc, dims, htab=None, gtab=None):
+    """Backward of ``expert_forward`` (ethos_expert_backward): the expert
+    half of the layer's backward, for a host that routes with its own router.
+    ``dot`` is ``expert_forward(..., save_dot=True)``'s second output and
+    ``dhacc`` fp32 ``[T, dh]`` the gradient of hacc.  Returns a dict of fp32
+    ``dxp [T, dh]``, ``d_weights [T, H, k]`` (the routing weights' gradient,
+    the router backward's input), ``d_latents [N, dl]`` and ``d_w1 [dh, dl]``."""
+    _require_cuda(ids, "ids")
+    if (htab is None) != (gtab is None):
+        raise ValueError("htab and gtab go together")
+    T = ids.shape[0]
+    dev = ids.device
+    ed = make_dims(T, dims)
+    L = lib()
+    ws_bytes = L.ethos_expert_backward_workspace_size(ctypes.byref(ed))
+    if ws_bytes == 0:
+        check(L.ethos_check_dims(ctypes.byref(ed)), "ethos_check_dims")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    f32 = dict(dtype=torch.float32, device=dev)
+    out = {"dxp": torch.empty((T, dims["d_hidden"]), **f32),
+           "d_weights": torch.empty((T, dims["num_heads"], dims["top_k"]), **f32),
+           "d_latents": torch.empty((dims["num_experts"], dims["d_latent"]), **f32),
+           "d_w1": torch.empty((dims["d_hidden"], dims["d_latent"]), **f32)}
+    err = device_error_word(dev)
+    check(L.ethos_expert_backward(ctypes.byref(ed), _vp(latents), _vp(w1), _vp(ids.contiguous()),
+                                  _vp(weights.contiguous()), _vp(xp.contiguous()), _vp(dot.contiguous()),
+                                  _vp(dhacc.contiguous().float()), _vp(htab), _vp(gtab), _vp(out["dxp"]),
+                                  _vp(out["d_weights"]), _vp(out["d_latents"]), _vp(out["d_w1"]), _vp(ws),
+                                  ws_bytes, _vp(err), _stream(dev)), "ethos_expert_backward")
+    return out
+
+
+def router_backward(d_weights, x2d, pw, ids, weights, save_qpre, bn_training, eps, save_bn=None, dx=None):
+    """Backward of ``router_forward`` (ethos_router_backward) given the routing
+    weights' gradient ``d_weights`` fp32 ``[T, H, k]``; ``save_qpre`` /
+    ``save_bn`` are the forward's save buffers.  With ``dx`` given (fp32
+    ``[T, d]``) the router's share of dL/dx is added to it, else a new ``dx``
+    is returned.  Returns a dict of fp32 ``dx``, ``d_wq [H*dq, d]``,
+    ``d_bn [3, H*dq]`` (bias, gamma, beta) and ``d_keys [2, K, dq/2]``."""
+    _require_cuda(x2d, "x")
+    d = pw.dims
+    T = x2d.shape[0]
+    dev = x2d.device
+    dims = make_dims(T, d)
+    L = lib()
+    ws_bytes = L.ethos_router_backward_workspace_size(ctypes.byref(dims))
+    if ws_bytes == 0:
+        check(L.ethos_check_dims(ctypes.byref(dims)), "ethos_check_dims")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    HQ = d["num_heads"] * d["d_query"]
+    f32 = dict(dtype=torch.float32, device=dev)
+    accumulate = dx is not None
+    if dx is None:
+        dx = torch.empty((T, d["d_model"]), **f32)
+    elif dx.dtype != torch.float32 or not dx.is_contiguous() or tuple(dx.shape) != (T, d["d_model"]):
+        raise ValueError("dx: a contiguous fp32 [T, d_model] tensor")
+    out = {"dx": dx, "d_wq": torch.empty((HQ, d["d_model"]), **f32), "d_bn": torch.empty((3, HQ), **f32),
+           "d_keys": torch.empty((2, d["num_sub_keys"], d["d_query"] // 2), **f32)}
+    err = device_error_word(dev)
+    check(L.ethos_router_backward(ctypes.byref(dims), 1 if bn_training else 0, float(eps), _vp(x2d), _vp(pw.w_cat),
+                                  _vp(pw.bn), _vp(pw.key_cat), _vp(ids.contiguous()), _vp(weights.contiguous()),
+                                  _vp(d_weights.contiguous().float()), _vp(save_qpre), _vp(save_bn), _vp(dx),
+                                  1 if accumulate else 0, _vp(out["d_wq"]), _vp(out["d_bn"]), _vp(out["d_keys"]),
+                                  _vp(ws), ws_bytes, _vp(err), _stream(dev)), "ethos_router_backward")
+    return out
+
+
 def _grad_layout(d):
     """Flat fp32 buffer for every parameter gradient (256-B aligned slices)."""
     HQ = d["num_heads"] * d["d_query"]

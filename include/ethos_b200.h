@@ -272,6 +272,53 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
 #define ETHOS_BWD_STAGE_END 1
 #define ETHOS_BWD_STAGE_COUNT 2
 
+/* The two halves of ethos_layer_backward as separate calls, for a host that
+ * routes with its own router (and so needs expert-only gradients and the
+ * gradient with respect to the routing weights) or that runs only the router
+ * from this library.  Composed, they give what ethos_layer_backward gives
+ * (which fuses the two dx GEMMs into one over [dq | dxp]).
+ *
+ * ethos_expert_backward: the backward of ethos_expert_forward -- the
+ * gradients autograd takes through the expert loop of model.py:306-336 given
+ * hacc's gradient.
+ *  latents, w1, ids, weights, xp  as passed to ethos_expert_forward
+ *  dot       fp32 [T, H*k]  ethos_expert_forward's `dot` output
+ *  dhacc     fp32 [T, dh]   dL/dhacc (for y = hacc W_v^T / H: dy W_v / H)
+ *  htab, gtab  fp16 [N, dh] tables from ethos_layer_forward's save_htab /
+ *            save_gtab, or both NULL (then built in the workspace)
+ * Outputs (fp32, overwritten):
+ *  dxp       [T, dh]        dL/dxp (the caller applies W_u: dx = dxp W_u^T)
+ *  d_weights [T, H*k]       dL/d(routing weight), the input of the router's
+ *                           backward (model.py:234's softmax output)
+ *  d_latents [N, dl], d_w1 [dh, dl]
+ * Ids outside [0, N) set ETHOS_ERR_ID_OUT_OF_RANGE in dev_err. */
+size_t ethos_expert_backward_workspace_size(const ethos_dims* dims);
+int ethos_expert_backward(const ethos_dims* dims, const void* latents, const void* w1, const int32_t* ids,
+                          const float* weights, const float* xp, const float* dot, const float* dhacc,
+                          const void* htab, const void* gtab, float* dxp, float* d_weights, float* d_latents,
+                          float* d_w1, void* workspace, size_t workspace_bytes, int* dev_err, void* stream);
+
+/* ethos_router_backward: the backward of ethos_router_forward
+ * (ProductKeyRouter.forward, model.py:208-254, under autograd): softmax
+ * backward into the selected grid scores, sub-key and query gradients, the
+ * BatchNorm backward (batch statistics when bn_training, else running
+ * statistics), and the query projection's gradients.
+ *  x, w_cat, bn, key_cat, ids, weights  as passed to / returned by the forward
+ *            (w_cat needs only its first H*dq rows)
+ *  d_weights fp32 [T, H*k]  dL/d(routing weight)
+ *  save_qpre, save_bn       the forward's save buffers (save_bn in training);
+ *            the normalised queries are recomputed from them
+ * Outputs (fp32):
+ *  dx        [T, d]         overwritten, or added to when accumulate_dx != 0
+ *                           (to sum the router's and the experts' shares)
+ *  d_wq [H*dq, d], d_bn [3, H*dq], d_keys [2, K, dq/2]  overwritten */
+size_t ethos_router_backward_workspace_size(const ethos_dims* dims);
+int ethos_router_backward(const ethos_dims* dims, int bn_training, float bn_eps, const void* x, const void* w_cat,
+                          const float* bn, const void* key_cat, const int32_t* ids, const float* weights,
+                          const float* d_weights, const float* save_qpre, const float* save_bn, float* dx,
+                          int accumulate_dx, float* d_wq, float* d_bn, float* d_keys, void* workspace,
+                          size_t workspace_bytes, int* dev_err, void* stream);
+
 /* Plain bf16 GEMM D[M, N] = A[M, K] B[N, K]^T * scale on the tcgen05 path
  * (fp32 accumulate), used by the layer and exposed for tests.  out_dtype 0 =
  * fp32, 1 = bf16.  M >= 1, N % 128 == 0, K % 8 == 0. */

@@ -130,6 +130,29 @@ def test_null_arguments_rejected_without_gpu(L):
     assert L.ethos_backward_workspace_size(ctypes.byref(d)) > 2 * 512 * 512 * 512 * 2
 
 
+def test_split_backward_host_checks(L):
+    """The expert-only and router-only backward calls reject missing
+    arguments and unpaired tables before any launch, and size their
+    workspaces below the whole layer's (each needs only its half)."""
+    d = _dims()
+    v = ctypes.c_void_p(256)
+    assert L.ethos_expert_backward(ctypes.byref(d), *([None] * 14), 0, None, None) == 1
+    # htab without gtab
+    args = [v] * 7 + [v, None] + [v] * 4
+    assert L.ethos_expert_backward(ctypes.byref(d), *args, v, 1 << 40, v, None) == 1
+    assert L.ethos_router_backward(ctypes.byref(d), 0, 1e-5, *([None] * 10), 0, *([None] * 4), 0, None, None) == 1
+    # training mode needs the forward's batch statistics
+    args = [v] * 8 + [None] + [v]
+    assert L.ethos_router_backward(ctypes.byref(d), 1, 1e-5, *args, 0, v, v, v, v, 1 << 40, v, None) == 1
+    whole = L.ethos_backward_workspace_size(ctypes.byref(d))
+    ex = L.ethos_expert_backward_workspace_size(ctypes.byref(d))
+    ro = L.ethos_router_backward_workspace_size(ctypes.byref(d))
+    assert 0 < ex < whole and 0 < ro < whole
+    bad = _dims(d_query=100)
+    assert L.ethos_expert_backward_workspace_size(ctypes.byref(bad)) == 0
+    assert L.ethos_router_backward_workspace_size(ctypes.byref(bad)) == 0
+
+
 def test_failure_test_hook_and_counter_host_checks(L):
     """Argument checks of the bounded-wait test entry point (no launch), and
     the launch counter is readable without a device."""
