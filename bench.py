@@ -491,6 +491,67 @@ def run_router(args, rank, world, local, dev):
         print(json.dumps(line), flush=True)
 
 
+def fp32_block(args, rank, world, local, dev, steps=None):
+    """The fp32 arithmetic path (fp32 parameters, the split-bf16 contractions):
+    config 2 with 16 384 tokens per GPU, the forward with BatchNorm on running
+    statistics and the forward + backward with batch statistics.  Returns the
+    report (every rank must call it)."""
+    import torch.distributed as dist
+    from ethos_b200 import ops
+    from ethos_b200.init import seeded_input, tensor_generator
+    steps = steps or args.steps
+    layer = build_layer(dev, dtype=torch.float32)
+    T = args.tokens
+    x = seeded_input(T, CFG2["d_model"], seed=rank).to(dev)
+    gy = (torch.randn((T, CFG2["d_model"]), generator=tensor_generator(rank, "bench.gy32")) * 1e-3).to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fwd():
+        with torch.no_grad():
+            layer(x.view(1, T, -1))
+
+    def fwd_bwd():
+        for q in layer.parameters():
+            q.grad = None
+        layer(x.view(1, T, -1)).backward(gy.view(1, T, -1))
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        ops.check_device_error(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for s_, e_ in ev:
+            flush.zero_()
+            s_.record(stream)
+            fn()
+            e_.record(stream)
+        torch.cuda.synchronize()
+        ops.check_device_error(dev)
+        ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    layer.eval()
+    fwd_ms = timed(fwd)
+    layer.train()
+    train_ms = timed(fwd_bwd)
+    del layer
+    return dict(workload="config 2 with fp32 parameters: fp32 arithmetic path (split-bf16 tcgen05 "
+                         "contractions, everything between them in fp32), 16384 tokens per GPU",
+                forward_ms=fwd_ms, forward_tokens_per_s=T * world / (fwd_ms / 1e3),
+                forward_backward_ms=train_ms, forward_backward_tokens_per_s=T * world / (train_ms / 1e3),
+                batchnorm="running statistics in the forward line, batch statistics in forward + backward",
+                l2="flushed between timed steps (256 MiB write)", steps=steps)
+
+
 def stack_block(args, rank, world, local, dev, steps=None, sampler=True):
     """Config 4, the expert layers of the decoder: 12 ETHOS expert layers
     (config-2 dimensions, each with its own seeded parameters) on one residual
@@ -818,6 +879,8 @@ def run_forward(args, rank, world, local, dev):
         torch.cuda.empty_cache()
         extra["router"] = router_block(args, rank, world, local, dev, steps=20, sampler=False)
         extra["stack"] = stack_block(args, rank, world, local, dev, steps=5, sampler=False)
+        torch.cuda.empty_cache()
+        extra["fp32"] = fp32_block(args, rank, world, local, dev, steps=5)
 
     peaks = load_peaks()
     total_tokens = T * world
