@@ -415,8 +415,9 @@ __global__ void __launch_bounds__(256, 3) k_expert_dP(const int* __restrict__ of
 // Router backward per (token, head) -- one warp each, lane l owns query
 // columns [8l, 8l+8) of each half (dq/2 = 256):
 //   dg_r  = w_r (dw_r - sum_r' w_r' dw_r')                    (softmax)
-//   dq^[t, h, :dq/2] = sum_r dg_r K1[i_r],  dq^[t, h, dq/2:] = sum_r dg_r K2[j_r]
 //   dS[p][h][t][i] = sum_{r: key_p(r) = i} dg_r              (dense, bf16)
+//   dq^[t, h, :dq/2] = sum_i dS[0][h][t][i] K1[i],  dq^[t, h, dq/2:] = sum_j dS[1][h][t][j] K2[j]
+//   (= sum_r dg_r K1[i_r] and sum_r dg_r K2[j_r]; dS in fp32 here)
 // with i_r = id_r / K, j_r = id_r % K.  dS feeds the dK GEMMs; its buffer is
 // zeroed beforehand and every (h, p, t, i) is written by one lane (duplicate
 // keys of a row are combined with __match_any_sync first).
@@ -447,7 +448,11 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
     const int i1 = id / K, i2 = id - i1 * K;
     // dS scatter: lanes with the same key combine (each lane walks the lanes
     // of its key group, the warp as long as the largest group), the lowest
-    // lane of a group stores
+    // lane of a group stores; the groups' keys, sums and leaders are kept for
+    // dq^ below
+    int key_p[2];
+    float tot_p[2];
+    unsigned lead_p[2];
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int key = act ? (p == 0 ? i1 : i2) : -1 - lane;
@@ -461,34 +466,36 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
         tot += m ? gu : 0.f;
         m &= m - 1u;
       }
-      if (act && leader == lane)
-        dS[((static_cast<int64_t>(p) * H + h) * T + t) * K + key] = __float2bfloat16_rn(tot);
+      const bool lead = act && leader == lane;
+      if (lead) dS[((static_cast<int64_t>(p) * H + h) * T + t) * K + key] = __float2bfloat16_rn(tot);
+      key_p[p] = key;
+      tot_p[p] = tot;
+      lead_p[p] = __ballot_sync(0xffffffffu, lead);
     }
-    // dq^ = sum_r dg_r * key rows: the selection's sub-key indices come from
-    // the lane that decoded them; bf16 pairs widen to fp32 pairs by shifts
-    unsigned long long acc0[4], acc1[4];
+    // dq^_p = sum over the half's distinct sub-keys of dS * key row (the grid
+    // top-k of a row draws on a few distinct sub-keys per half, ~5 of 16 at
+    // k = 16); bf16 pairs widen to fp32 pairs by shifts
+    unsigned long long acc[2][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      acc0[i] = 0ull;
-      acc1[i] = 0ull;
-    }
-#pragma unroll 4
-    for (int u = 0; u < TOPK; ++u) {
-      const float g = __shfl_sync(0xffffffffu, dg, u);
-      const int k1 = __shfl_sync(0xffffffffu, i1, u);
-      const int k2 = __shfl_sync(0xffffffffu, i2, u);
-      if (lane < nl) {
-        const uint4 a = *reinterpret_cast<const uint4*>(keys + static_cast<int64_t>(k1) * key_ld + 8 * lane);
-        const uint4 b = *reinterpret_cast<const uint4*>(keys + (static_cast<int64_t>(K) + k2) * key_ld + 8 * lane);
-        const unsigned long long g2 = pk2(g, g);
-        const uint32_t av[4] = {a.x, a.y, a.z, a.w};
-        const uint32_t bv[4] = {b.x, b.y, b.z, b.w};
+    for (int p = 0; p < 2; ++p) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const unsigned long long fa = pk2(__uint_as_float(av[i] << 16), __uint_as_float(av[i] & 0xffff0000u));
-          const unsigned long long fb = pk2(__uint_as_float(bv[i] << 16), __uint_as_float(bv[i] & 0xffff0000u));
-          acc0[i] = ffma2(g2, fa, acc0[i]);
-          acc1[i] = ffma2(g2, fb, acc1[i]);
+      for (int i = 0; i < 4; ++i) acc[p][i] = 0ull;
+      unsigned m = lead_p[p];
+      while (m != 0u) {  // warp-uniform
+        const int src = __ffs(m) - 1;
+        m &= m - 1u;
+        const float g = __shfl_sync(0xffffffffu, tot_p[p], src);
+        const int kk = __shfl_sync(0xffffffffu, key_p[p], src);
+        if (lane < nl) {
+          const uint4 a =
+              *reinterpret_cast<const uint4*>(keys + (static_cast<int64_t>(p) * K + kk) * key_ld + 8 * lane);
+          const unsigned long long g2 = pk2(g, g);
+          const uint32_t av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const unsigned long long fa = pk2(__uint_as_float(av[i] << 16), __uint_as_float(av[i] & 0xffff0000u));
+            acc[p][i] = ffma2(g2, fa, acc[p][i]);
+          }
         }
       }
     }
@@ -497,8 +504,8 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
       float c0[8], c1[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        upk2(acc0[i], c0[2 * i], c0[2 * i + 1]);
-        upk2(acc1[i], c1[2 * i], c1[2 * i + 1]);
+        upk2(acc[0][i], c0[2 * i], c0[2 * i + 1]);
+        upk2(acc[1][i], c1[2 * i], c1[2 * i + 1]);
       }
       *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(c0[0], c0[1], c0[2], c0[3]);
       *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(c0[4], c0[5], c0[6], c0[7]);

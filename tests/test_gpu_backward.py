@@ -52,7 +52,11 @@ def _grad_tol(name):
 
 @pytest.mark.parametrize("cfg,T,training", [(CFG1, 256, False), (CFG1, 256, True), (CFG2, 512, True),
                                             (CFG2, 1024, False), (CFG2, 2048, True), (CFG_R4, 300, True),
-                                            (CFG_R8, 300, False)])
+                                            (CFG_R8, 300, False),
+                                            # ragged token counts (fused path below N / (H k) tokens,
+                                            # the table path above) and the smallest training batches
+                                            (CFG1, 1, False), (CFG1, 7, False), (CFG1, 2, True),
+                                            (CFG1, 3, True), (CFG1, 131, True)])
 def test_layer_backward_matches_oracle(cfg, T, training):
     layer = EthosExpertLayer(EthosConfig(**cfg))
     sd = _stats_state(seeded_state_dict(layer, seed=3))
