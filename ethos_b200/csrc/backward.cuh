@@ -425,7 +425,7 @@ template <int TOPK>
 __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ ids, const float* __restrict__ w,
                                                      const float* __restrict__ dw,
                                                      const __nv_bfloat16* __restrict__ keys,  // [2][K] rows
-                                                     int64_t key_ld, float* __restrict__ dqhat,
+                                                     int64_t key_ld, __nv_bfloat16* __restrict__ dqhat,
                                                      __nv_bfloat16* __restrict__ dS, int T, int H, int K, int half) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -500,17 +500,21 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
       }
     }
     if (lane < nl) {
-      float* dst = dqhat + static_cast<int64_t>(t) * (H * 2 * half) + static_cast<int64_t>(h) * 2 * half;
-      float c0[8], c1[8];
+      // dq^ is stored in bf16: it only feeds BatchNorm's backward, whose
+      // output dq is the bf16 operand of the dx / dW_q GEMMs
+      __nv_bfloat16* dst = dqhat + static_cast<int64_t>(t) * (H * 2 * half) + static_cast<int64_t>(h) * 2 * half;
+      uint32_t o0[4], o1[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        upk2(acc[0][i], c0[2 * i], c0[2 * i + 1]);
-        upk2(acc[1][i], c1[2 * i], c1[2 * i + 1]);
+        float a0, a1, b0, b1;
+        upk2(acc[0][i], a0, a1);
+        upk2(acc[1][i], b0, b1);
+        const __nv_bfloat162 pa = __floats2bfloat162_rn(a0, a1), pb = __floats2bfloat162_rn(b0, b1);
+        o0[i] = *reinterpret_cast<const uint32_t*>(&pa);
+        o1[i] = *reinterpret_cast<const uint32_t*>(&pb);
       }
-      *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(c0[0], c0[1], c0[2], c0[3]);
-      *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(c0[4], c0[5], c0[6], c0[7]);
-      *reinterpret_cast<float4*>(dst + half + 8 * lane) = make_float4(c1[0], c1[1], c1[2], c1[3]);
-      *reinterpret_cast<float4*>(dst + half + 8 * lane + 4) = make_float4(c1[4], c1[5], c1[6], c1[7]);
+      *reinterpret_cast<uint4*>(dst + 8 * lane) = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+      *reinterpret_cast<uint4*>(dst + half + 8 * lane) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
     }
   }
 }
@@ -527,7 +531,11 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
 //   D = -A*m1
 // with coef[c] = (A, B, D, mean): centring qpre before the multiply keeps the
 // cancellation exact where qpre and the mean agree to many bits.
-__global__ void k_bn_bwd_partial(const float* __restrict__ dqh, const float* __restrict__ qpre,
+__device__ __forceinline__ float ld_f32(const float* p) { return *p; }
+__device__ __forceinline__ float ld_f32(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+template <class DQ>
+__global__ void k_bn_bwd_partial(const DQ* __restrict__ dqh, const float* __restrict__ qpre,
                                  const float* __restrict__ mean, const float* __restrict__ invstd, int T, int C,
                                  float* __restrict__ part) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
@@ -539,7 +547,7 @@ __global__ void k_bn_bwd_partial(const float* __restrict__ dqh, const float* __r
   float s = 0.f, sx = 0.f;
   for (int r = r0; r < r1; ++r) {
     const int64_t o = static_cast<int64_t>(r) * C + col;
-    const float g = dqh[o];
+    const float g = ld_f32(dqh + o);
     s += g;
     sx = fmaf(g, (qpre[o] - mu) * is, sx);
   }
@@ -573,7 +581,7 @@ __global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int
 // One thread per 8 consecutive columns (C % 8 == 0), grid x over the column
 // groups and y over the token rows (as k_bn_apply); coef[c] = (A, B, D, mean)
 // from k_bn_bwd_finalize.
-__global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __restrict__ qpre,
+__global__ void k_bn_bwd_apply(const __nv_bfloat16* __restrict__ dqh, const float* __restrict__ qpre,
                                const float4* __restrict__ coef, int T, int C, __nv_bfloat16* __restrict__ du,
                                int64_t ldu) {
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -583,9 +591,9 @@ __global__ void k_bn_bwd_apply(const float* __restrict__ dqh, const float* __res
   for (int u = 0; u < 8; ++u) k[u] = __ldg(coef + c0 + u);
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
     const int64_t o = static_cast<int64_t>(t) * C + c0;
-    const float4 g0 = *reinterpret_cast<const float4*>(dqh + o), g1 = *reinterpret_cast<const float4*>(dqh + o + 4);
+    float gv[8];
+    unpack_b8(*reinterpret_cast<const uint4*>(dqh + o), gv);
     const float4 q0 = *reinterpret_cast<const float4*>(qpre + o), q1 = *reinterpret_cast<const float4*>(qpre + o + 4);
-    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
     const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     uint32_t out[4];
 #pragma unroll

@@ -622,7 +622,7 @@ struct BwdScratch {
   int* total;
   int* perm;
   __nv_bfloat16* dP;
-  float* dqhat;
+  __nv_bfloat16* dqhat;  // [T][HQ] dq^ (bf16: feeds BatchNorm's backward only)
   __nv_bfloat16* dS;
   __nv_bfloat16* gx;
   float* part;
@@ -649,7 +649,7 @@ void carve_backward(Carve& c, const ethos_dims& d, BwdScratch* s) {
   s->total = c.take<int>(4);
   s->perm = c.take<int>(static_cast<size_t>(T * R));
   s->dP = c.take<__nv_bfloat16>(static_cast<size_t>(N * EX_DH));
-  s->dqhat = c.take<float>(static_cast<size_t>(T * HQ));
+  s->dqhat = c.take<__nv_bfloat16>(static_cast<size_t>(T * HQ));
   s->dS = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.num_sub_keys));
   s->gx = c.take<__nv_bfloat16>(static_cast<size_t>(T * 2 * EX_DH));
   s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
@@ -667,7 +667,8 @@ __global__ void k_f32_to_bf16(const float* __restrict__ in, int64_t n, __nv_bflo
 
 template <int TOPK>
 int launch_router_bwd(const ethos_dims& d, const int32_t* ids, const float* w, const float* dw,
-                      const __nv_bfloat16* keys, int64_t key_ld, float* dqhat, __nv_bfloat16* dS, cudaStream_t stream,
+                      const __nv_bfloat16* keys, int64_t key_ld, __nv_bfloat16* dqhat, __nv_bfloat16* dS,
+                      cudaStream_t stream,
                       const DeviceInfo& dev) {
   const int TH = static_cast<int>(d.tokens * d.num_heads);
   int blocks = (TH + 7) / 8;
@@ -712,7 +713,7 @@ void carve_router_backward(Carve& c, const ethos_dims& d, BwdScratch* s, RouterB
   const int64_t T = d.tokens, HQ = d.num_heads * d.d_query;
   *s = BwdScratch{};
   s->du = c.take<__nv_bfloat16>(static_cast<size_t>(T * HQ));
-  s->dqhat = c.take<float>(static_cast<size_t>(T * HQ));
+  s->dqhat = c.take<__nv_bfloat16>(static_cast<size_t>(T * HQ));
   s->dS = c.take<__nv_bfloat16>(static_cast<size_t>(d.num_heads * 2 * T * d.num_sub_keys));
   s->slabs = static_cast<int>((T + BN_ROWS_PER_SLAB - 1) / BN_ROWS_PER_SLAB);
   s->part = c.take<float>(static_cast<size_t>(s->slabs) * HQ * 2);
