@@ -472,14 +472,17 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
     for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++it) {
       const int h = item / num_mt;
       const int t = (item - h * num_mt) * 128 + row;
-      float lv[2][TOPK];
-      int li[2][TOPK];
-#pragma unroll
+      // The half loop stays rolled (one copy of its body in the instruction
+      // stream): the current half's list is (cv, ci), half 0's is copied to
+      // (lv0, li0) at the end of its iteration and half 1's stays in (cv, ci).
+      float lv0[TOPK], cv[TOPK];
+      int li0[TOPK], ci[TOPK];
+#pragma unroll 1
       for (int p = 0; p < 2; ++p) {
 #pragma unroll
         for (int j = 0; j < TOPK; ++j) {
-          lv[p][j] = -INFINITY;
-          li[p][j] = 0;
+          cv[j] = -INFINITY;
+          ci[j] = 0;
         }
         // The half's units stay in TMEM until its candidates are compacted:
         // 1. per unit, the maxima of this group's 8-key groups, sorted and
@@ -663,8 +666,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
             for (int j = 0; j < TOPK; ++j) {
               const int slot = static_cast<int>(__float_as_uint(key[j]) & 31u);
               const float2 e = cand[32 * slot];
-              lv[p][j] = slot < n ? e.x : -INFINITY;
-              li[p][j] = slot < n ? __float_as_int(e.y) : 0;
+              cv[j] = slot < n ? e.x : -INFINITY;
+              ci[j] = slot < n ? __float_as_int(e.y) : 0;
             }
           } else {
             // Rare: some row of the warp has more than CAND_CAP candidates.
@@ -676,7 +679,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
 #pragma unroll 1
             for (int s2 = 0; s2 < nmax; ++s2) {
               const float2 e = cand[32 * s2];
-              topk_insert<TOPK>(lv[p], li[p], s2 < n ? e.x : -INFINITY, s2 < n ? __float_as_int(e.y) : 0);
+              topk_insert<TOPK>(cv, ci, s2 < n ? e.x : -INFINITY, s2 < n ? __float_as_int(e.y) : 0);
             }
             __syncwarp();
 #pragma unroll 1
@@ -691,7 +694,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
                 if (c * 32 >= vg) break;
                 float sc[32];
                 tmem_ld32(cbase + c * 32, sc);
-                topk_fold_chunk<TOPK, false>(lv[p], li[p], sc, nullptr, key0 + c * 32, tau, stage, nullptr, lane);
+                topk_fold_chunk<TOPK, false>(cv, ci, sc, nullptr, key0 + c * 32, tau, stage, nullptr, lane);
               }
               tc_fence_before();
               mbar_arrive(&ctl->acc_empty[buf]);
@@ -706,8 +709,8 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
         named_bar_sync(1, 256);
 #pragma unroll
         for (int j = 0; j < TOPK; ++j) {
-          pub_v[j * 128 + row] = lv[p][j];
-          pub_i[j * 128 + row] = li[p][j];
+          pub_v[j * 128 + row] = cv[j];
+          pub_i[j * 128 + row] = ci[j];
         }
         named_bar_sync(1, 256);
         {
@@ -719,14 +722,21 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
             oi[j] = oth_i[j * 128 + row];
           }
           if (grp == 0) {
-            top_merge_kv<TOPK>(lv[p], li[p], ov, oi);
+            top_merge_kv<TOPK>(cv, ci, ov, oi);
           } else {
-            top_merge_kv<TOPK>(ov, oi, lv[p], li[p]);
+            top_merge_kv<TOPK>(ov, oi, cv, ci);
 #pragma unroll
             for (int j = 0; j < TOPK; ++j) {
-              lv[p][j] = ov[j];
-              li[p][j] = oi[j];
+              cv[j] = ov[j];
+              ci[j] = oi[j];
             }
+          }
+        }
+        if (p == 0) {
+#pragma unroll
+          for (int j = 0; j < TOPK; ++j) {
+            lv0[j] = cv[j];
+            li0[j] = ci[j];
           }
         }
       }
@@ -739,9 +749,9 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
       int fid[TOPK];
       if constexpr (TOPK == 16) {
         if (grp == fin) {
-          grid_rows01<16>(lv[0], li[0], lv[1], li[1], g.K, fv, fid);
+          grid_rows01<16>(lv0, li0, cv, ci, g.K, fv, fid);
         } else {
-          grid_rows27<16>(lv[0], li[0], lv[1], li[1], g.K, fv, fid);
+          grid_rows27<16>(lv0, li0, cv, ci, g.K, fv, fid);
         }
         named_bar_sync(1, 256);
         if (grp != fin) {
@@ -763,7 +773,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS, 1)
           top_merge_kv<16>(fv, fid, ov, oi);
         }
       } else {
-        if (grp == fin) grid_topk<TOPK>(lv[0], li[0], lv[1], li[1], g.K, fv, fid);
+        if (grp == fin) grid_topk<TOPK>(lv0, li0, cv, ci, g.K, fv, fid);
       }
       if (grp == fin && ok && t < g.T) {
         // fp32 softmax over the selected scores (model.py:234)
