@@ -531,11 +531,7 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
 //   D = -A*m1
 // with coef[c] = (A, B, D, mean): centring qpre before the multiply keeps the
 // cancellation exact where qpre and the mean agree to many bits.
-__device__ __forceinline__ float ld_f32(const float* p) { return *p; }
-__device__ __forceinline__ float ld_f32(const __nv_bfloat16* p) { return __bfloat162float(*p); }
-
-template <class DQ>
-__global__ void k_bn_bwd_partial(const DQ* __restrict__ dqh, const float* __restrict__ qpre,
+__global__ void k_bn_bwd_partial(const float* __restrict__ dqh, const float* __restrict__ qpre,
                                  const float* __restrict__ mean, const float* __restrict__ invstd, int T, int C,
                                  float* __restrict__ part) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
@@ -545,14 +541,41 @@ __global__ void k_bn_bwd_partial(const DQ* __restrict__ dqh, const float* __rest
   const int r0 = slab * BN_ROWS_PER_SLAB;
   const int r1 = min(T, r0 + BN_ROWS_PER_SLAB);
   float s = 0.f, sx = 0.f;
+#pragma unroll 8
   for (int r = r0; r < r1; ++r) {
     const int64_t o = static_cast<int64_t>(r) * C + col;
-    const float g = ld_f32(dqh + o);
+    const float g = dqh[o];
     s += g;
     sx = fmaf(g, (qpre[o] - mu) * is, sx);
   }
   part[(static_cast<int64_t>(slab) * C + col) * 2 + 0] = s;
   part[(static_cast<int64_t>(slab) * C + col) * 2 + 1] = sx;
+}
+
+// The same partial sums over a bf16 dq^ (the bf16 path), two adjacent
+// columns per thread (C even) so a warp reads 128 contiguous bytes of dq^ and
+// 256 of qpre per row.  Grid x covers the column pairs.
+__global__ void k_bn_bwd_partial_bf16(const __nv_bfloat16* __restrict__ dqh, const float* __restrict__ qpre,
+                                      const float* __restrict__ mean, const float* __restrict__ invstd, int T, int C,
+                                      float* __restrict__ part) {
+  const int col = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  const int slab = blockIdx.y;
+  if (col >= C) return;
+  const float mu0 = mean[col], mu1 = mean[col + 1], is0 = invstd[col], is1 = invstd[col + 1];
+  const int r0 = slab * BN_ROWS_PER_SLAB;
+  const int r1 = min(T, r0 + BN_ROWS_PER_SLAB);
+  float s0 = 0.f, s1 = 0.f, sx0 = 0.f, sx1 = 0.f;
+#pragma unroll 8
+  for (int r = r0; r < r1; ++r) {
+    const int64_t o = static_cast<int64_t>(r) * C + col;
+    const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dqh + o));
+    const float2 q = *reinterpret_cast<const float2*>(qpre + o);
+    s0 += g.x;
+    s1 += g.y;
+    sx0 = fmaf(g.x, (q.x - mu0) * is0, sx0);
+    sx1 = fmaf(g.y, (q.y - mu1) * is1, sx1);
+  }
+  *reinterpret_cast<float4*>(part + (static_cast<int64_t>(slab) * C + col) * 2) = make_float4(s0, sx0, s1, sx1);
 }
 
 __global__ void k_bn_bwd_finalize(const float* __restrict__ part, int slabs, int C, int T, int training,

@@ -907,9 +907,9 @@ int router_bwd_core(const ethos_dims& d, const RouterBwdIO& io, const BwdScratch
     mean = s.stats;
     invstd = s.stats + HQ;
   }
-  dim3 grid_p((HQ + cb - 1) / cb, s.slabs);
+  dim3 grid_p((HQ / 2 + cb - 1) / cb, s.slabs);
   count_launch();
-  k_bn_bwd_partial<<<grid_p, cb, 0, sm>>>(s.dqhat, io.qpre, mean, invstd, T, HQ, s.part);
+  k_bn_bwd_partial_bf16<<<grid_p, cb, 0, sm>>>(s.dqhat, io.qpre, mean, invstd, T, HQ, s.part);
   count_launch();
   k_bn_bwd_finalize<<<(HQ + cb - 1) / cb, cb, 0, sm>>>(s.part, s.slabs, HQ, T, io.bn_training, io.bn + HQ, mean,
                                                       invstd, io.d_bn + HQ, io.d_bn + 2 * HQ, io.d_bn, s.coef);
