@@ -656,6 +656,9 @@ def main():
                     help="leave the config-3 router and config-4 stack blocks out of the forward line")
     ap.add_argument("--ref-seconds", type=float, default=3.0,
                     help="CPU seconds per reference-arm step (a bounded sample of the workload)")
+    ap.add_argument("--no-numa-bind", action="store_true",
+                    help="with several ranks, leave each rank's CPU affinity alone instead of binding it to its "
+                         "GPU's NUMA node (pinned staging buffers then land wherever the process first runs)")
     ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "stack"],
                     help="forward: config 2 (headline, with the config-5 train block); train: config 5 alone; "
                          "router: config 3 routing microbenchmark; stack: config 4's 12 expert layers")
@@ -673,6 +676,14 @@ def main():
     from datetime import timedelta
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    args.host_cpus = None
+    if world > 1 and not args.no_numa_bind:
+        # each rank's pinned host buffers on its GPU's NUMA node (one rank per
+        # GPU shares the host links; the single-rank run keeps every core for
+        # its CPU baseline)
+        from ethos_b200.dist import bind_to_device_numa
+        cpus = bind_to_device_numa(dev)
+        args.host_cpus = len(cpus) if cpus else None
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
@@ -943,7 +954,10 @@ def run_forward(args, rank, world, local, dev):
                  pipeline="upload / layer / download on three streams, L2 flush per step inside the span",
                  serial_ms_per_step=serial_ms, copy_only_ms_per_step=copy_ms,
                  copy_only_note="the same uploads and downloads without the layer, concurrently on every rank "
-                                "(max over ranks)"),
+                                "(max over ranks)",
+                 host_binding=(f"each rank bound to the {args.host_cpus} CPUs of its GPU's NUMA node before its "
+                               "pinned buffers were allocated" if args.host_cpus else "process CPU affinity as "
+                               "started")),
         gpu_launches=n_launch,
         clocks=clocks,
     )

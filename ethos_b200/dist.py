@@ -13,13 +13,18 @@ i.e. data parallelism with the gradients reduced across ranks.  Here:
   tests);
 * BatchNorm uses each rank's batch statistics, as the reference does (no
   SyncBN); ``average_running_stats`` optionally averages the running
-  statistics so that ranks evaluate identically.
+  statistics so that ranks evaluate identically;
+* ``bind_to_device_numa`` keeps each rank's host work and pinned staging
+  buffers on its GPU's NUMA node.
 """
+
+import os
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_range", "shard_tokens", "GradAllReducer", "average_running_stats", "overlap_grad_allreduce"]
+__all__ = ["shard_range", "shard_tokens", "GradAllReducer", "average_running_stats", "overlap_grad_allreduce",
+           "bind_to_device_numa"]
 
 
 def shard_range(total, rank, world):
@@ -113,3 +118,50 @@ def average_running_stats(module, group=None):
                 t = buf.float().clone()
                 dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
                 buf.copy_((t / world).to(buf.dtype))
+
+
+def _affinity_cpus(words):
+    """CPU ids set in an NVML CPU-affinity mask (64-bit words, CPU 64 i + b is
+    bit b of word i)."""
+    return {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+
+
+def bind_to_device_numa(device=None, nvml=None, uuid=None):
+    """Restricts this process to the CPUs that NVML reports as close to the
+    GPU (its NUMA node), so that host memory the process touches first after
+    the call -- the pinned buffers of host <-> device copies in particular --
+    is placed in that node's memory and its copies do not cross the socket
+    interconnect.  Call it once per rank, before allocating pinned buffers.
+
+    Only the process's own CPU affinity changes (within the CPUs it may
+    already use); no GPU setting is read-modify-written.  Returns the CPU set
+    in effect afterwards, or None when NVML is missing or reports nothing
+    usable (the affinity is then left as it was).  ``nvml`` and ``uuid``
+    (the device UUID without its "GPU-" prefix) are for tests."""
+    if nvml is None:
+        try:
+            import pynvml as nvml
+        except ImportError:
+            return None
+    if uuid is None:
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    try:
+        nvml.nvmlInit()
+    except Exception:
+        return None
+    try:
+        handle = nvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
+        words = nvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+    except Exception:
+        return None
+    finally:
+        try:
+            nvml.nvmlShutdown()
+        except Exception:
+            pass
+    cpus = _affinity_cpus(words) & os.sched_getaffinity(0)
+    if not cpus:
+        return None
+    os.sched_setaffinity(0, cpus)
+    return cpus

@@ -128,3 +128,50 @@ def test_shard_range_covers_tokens():
             spans = [shard_range(total, r, world) for r in range(world)]
             assert spans[0][0] == 0 and spans[-1][1] == total
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+class _FakeNvml:
+    """Stands in for pynvml: one device whose CPU-affinity mask is `words`."""
+
+    def __init__(self, words, fail_handle=False):
+        self.words, self.fail_handle, self.calls = words, fail_handle, []
+
+    def nvmlInit(self):
+        self.calls.append("init")
+
+    def nvmlShutdown(self):
+        self.calls.append("shutdown")
+
+    def nvmlDeviceGetHandleByUUID(self, uuid):
+        self.calls.append(uuid)
+        if self.fail_handle:
+            raise RuntimeError("no such device")
+        return 7
+
+    def nvmlDeviceGetCpuAffinity(self, handle, n):
+        assert handle == 7 and n >= 1
+        return self.words
+
+
+def test_bind_to_device_numa_with_fake_nvml():
+    """The process is restricted to the CPUs of the GPU's affinity mask that
+    it may already use; a failing NVML leaves the affinity alone."""
+    import os
+    from ethos_b200.dist import _affinity_cpus, bind_to_device_numa
+    assert _affinity_cpus([0b1011, 1]) == {0, 1, 3, 64}
+    before = os.sched_getaffinity(0)
+    try:
+        first = min(before)
+        words = [0] * (first // 64 + 1)
+        words[first // 64] = 1 << (first % 64)
+        fake = _FakeNvml(words)
+        got = bind_to_device_numa(nvml=fake, uuid="abc")
+        assert got == {first} and os.sched_getaffinity(0) == {first}
+        assert fake.calls[:2] == ["init", "GPU-abc"] and fake.calls[-1] == "shutdown"
+        os.sched_setaffinity(0, before)
+        # a mask outside the allowed CPUs, or an NVML error: nothing changes
+        assert bind_to_device_numa(nvml=_FakeNvml([0]), uuid="abc") is None
+        assert bind_to_device_numa(nvml=_FakeNvml([1], fail_handle=True), uuid="abc") is None
+        assert os.sched_getaffinity(0) == before
+    finally:
+        os.sched_setaffinity(0, before)
