@@ -136,7 +136,7 @@ EncodeTiledFn encode_fn() {
 // box_cols 64, 32 or 16 (rows of 128, 64 or 32 bytes, with the swizzle of
 // that width); the UMMA descriptor of the consuming kernel must match it.
 int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int box_rows, int64_t ld = 0,
-                   int box_cols = 64) {
+                   int box_cols = 64, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return ETHOS_ERR_TENSOR_MAP;
   if (ld == 0) ld = cols;
@@ -146,7 +146,7 @@ int make_tmap_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, 
   if (box_cols != 64 && box_cols != 32 && box_cols != 16) return ETHOS_ERR_TENSOR_MAP;
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  CUresult r = fn(m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
                   box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : (box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B),
@@ -204,9 +204,13 @@ int operand_tmap(CUtensorMap* m, const GemmOperand& o, int64_t mn, int64_t k, in
 
 // Launches D = A B^T on the generic kernel.  ksplit > 1 requires an epilogue
 // that accumulates (EpiAtomicF32).  BN = 256 when N allows, else 128.
+// tc: the output's tensor map, for an epilogue that stores through TMA
+// (Epi::kTmaStore); other epilogues ignore the argument.
 template <class Epi, bool AMN, bool BMN, int BN>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit, const Epi& epi,
-                  int* err, cudaStream_t stream, const DeviceInfo& dev, int hold_unit = -1) {
+                  int* err, cudaStream_t stream, const DeviceInfo& dev, int hold_unit = -1,
+                  const CUtensorMap* tc = nullptr) {
+  if (Epi::kTmaStore && tc == nullptr) return ETHOS_ERR_INVALID_ARG;
   auto kern = k_gemm<Epi, AMN, BMN, BN>;
   int st = smem_attr_once(reinterpret_cast<const void*>(kern), GemmCfg<Epi>::kSmem);
   if (st != ETHOS_OK) return st;
@@ -214,8 +218,8 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   const int units = tiles * ksplit;
   const int grid = units < dev.sm_count ? units : dev.sm_count;
   if (grid <= 0) return ETHOS_OK;
-  return launch_pdl(kern, dim3(grid), dim3(GemmCfg<Epi>::kThreads), GemmCfg<Epi>::kSmem, stream, ta, tb, M, N, K,
-                    ksplit, epi, err, hold_unit);
+  return launch_pdl(kern, dim3(grid), dim3(GemmCfg<Epi>::kThreads), GemmCfg<Epi>::kSmem, stream, ta, tb,
+                    tc != nullptr ? *tc : ta, M, N, K, ksplit, epi, err, hold_unit);
 }
 
 template <class Epi, bool AMN = false, bool BMN = false>
@@ -342,8 +346,8 @@ int launch_gemm2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
 // Forward-path GEMM: both operands K-major (tensor maps built by the caller).
 template <class Epi>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int* err,
-                cudaStream_t stream, const DeviceInfo& dev) {
-  return launch_gemm_t<Epi, false, false, 256>(ta, tb, M, N, K, 1, epi, err, stream, dev);
+                cudaStream_t stream, const DeviceInfo& dev, const CUtensorMap* tc = nullptr) {
+  return launch_gemm_t<Epi, false, false, 256>(ta, tb, M, N, K, 1, epi, err, stream, dev, -1, tc);
 }
 
 // ------------------------------------------------------- workspace layout --
@@ -456,11 +460,11 @@ int build_table(const ethos_dims& d, const void* latents, const void* w1, __half
     eg.M = N;
     return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev);
   }
-  EpiGeluF16 eg;
-  eg.out = table;
-  eg.ldo = EX_DH;
-  eg.M = N;
-  return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev);
+  // the table leaves through TMA stores of 32-row x 64-column boxes (128-byte
+  // swizzle), the layout the epilogue stages
+  CUtensorMap tm_h;
+  if ((st = make_tmap_bf16(&tm_h, table, N, EX_DH, 32, 0, 64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16)) != ETHOS_OK) return st;
+  return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, EpiGeluF16{}, err, stream, dev, &tm_h);
 }
 
 // phase B: per-token gather, dot, activation, weighted sum

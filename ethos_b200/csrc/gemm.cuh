@@ -55,8 +55,10 @@ struct GemmCfg {
   static constexpr int kEpiThreads = 32 * kEpiWarps;
   static constexpr int kThreads = 64 + kEpiThreads;
   static constexpr int kStages = kEpiWarps == 16 ? 3 : GEMM_STAGES;
-  static constexpr int kSmem = kStages * GEMM_STAGE_BYTES + GEMM_COLP_BYTES + kEpiWarps * GEMM_STG_WARP_BYTES +
-                               1024 + static_cast<int>(sizeof(GemmCtl));
+  // a TMA-store epilogue stages its warp's whole 32-row x 128-byte block
+  static constexpr int kStgWarpBytes = Epi::kTmaStore ? 32 * 128 : GEMM_STG_WARP_BYTES;
+  static constexpr int kSmem = kStages * GEMM_STAGE_BYTES + GEMM_COLP_BYTES + kEpiWarps * kStgWarpBytes + 1024 +
+                               static_cast<int>(sizeof(GemmCtl));
   static_assert(kSmem <= 227 * 1024, "GEMM shared memory");
 };
 
@@ -73,6 +75,7 @@ struct EpiCtx {
   int row0;
   int nrows;
   int lane;
+  int chunk;  // index of the 32-column chunk among this warp's chunks of the tile
 };
 
 // Warp-cooperative store of 32 rows x 64 bytes.  Lane l holds the 64 bytes
@@ -107,6 +110,10 @@ __device__ __forceinline__ void warp_store_rows64(const EpiCtx& cx, const uint4 
 struct EpiNoColParams {
   static constexpr int kColParamBytes = 0;
   static constexpr int kEpiWarps = 8;
+  // true: the functor writes its fp16/bf16 row pieces into the warp's staging
+  // block (EpiCtx::stg, 32 rows x 128 B, 128-byte swizzle) and the kernel
+  // stores the block with one TMA store per warp and tile (tensor map tmC)
+  static constexpr bool kTmaStore = false;
   __device__ __forceinline__ void load_col_params(int, uint8_t*, int) const {}
 };
 
@@ -191,6 +198,7 @@ struct EpiAtomicF32 : EpiNoColParams {
 struct EpiProj {
   static constexpr int kColParamBytes = 8;  // float2 (scale, offset) or (bias, -)
   static constexpr int kEpiWarps = 8;
+  static constexpr bool kTmaStore = false;
   int M;   // tokens
   int HQ;  // H * d_query
   int dq;
@@ -287,11 +295,13 @@ struct EpiProj {
 // evaluated once per expert instead of once per selection).
 struct EpiGeluF16 : EpiNoColParams {
   static constexpr int kEpiWarps = 16;  // 0.117 ms vs 0.126 ms with 8 (262144 x 512 table)
-  __half* out;
-  int64_t ldo;
-  int M;
-  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
-    uint4 w4[4];
+  // The table rows leave through TMA stores of each warp's staged 32 x 64
+  // block: written directly, every warp store instruction touched 32 rows
+  // with 16-byte pieces and the LSU path bound the kernel (l1tex 79 % busy,
+  // 16.8 M L2 write requests per launch).
+  static constexpr bool kTmaStore = true;
+  __device__ __forceinline__ void operator()(int, int, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
+    const int r = cx.lane;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint32_t w[4];
@@ -302,14 +312,10 @@ struct EpiGeluF16 : EpiNoColParams {
         const __half2 hh = __floats2half2_rn(g0, g1);
         w[u] = *reinterpret_cast<const uint32_t*>(&hh);
       }
-      w4[j] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    // direct per-row stores: with one output the staged transpose costs more
-    // than it saves here (0.127 vs 0.117 ms, measured)
-    if (cx.lane < cx.nrows) {
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(cx.row0 + cx.lane) * ldo + col);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) dst[j] = w4[j];
+      // 16-byte piece p of row r at r * 128 + ((p ^ (r & 7)) << 4): the
+      // 128-byte swizzle of the store's tensor map, free of bank conflicts
+      const int p = cx.chunk * 4 + j;
+      *reinterpret_cast<uint4*>(cx.stg + r * 128 + ((p ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 };
@@ -368,8 +374,9 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32_major(int M, int N, b
 
 template <class Epi, bool kAMN, bool kBMN, int BN>
 __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-           int ksplit, Epi epi, int* err, int hold_unit) {
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+           const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int ksplit, Epi epi, int* err,
+           int hold_unit) {
   static_assert(BN == 128 || BN == 256, "N tile is 128 or 256");
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
@@ -380,7 +387,8 @@ __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* colp_s = smem + STAGES * GEMM_STAGE_BYTES;
   uint8_t* stg_s = colp_s + GEMM_COLP_BYTES;
-  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(stg_s + Cfg::kEpiWarps * GEMM_STG_WARP_BYTES);
+  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(stg_s + Cfg::kEpiWarps * Cfg::kStgWarpBytes);
+  static_assert(!Epi::kTmaStore || CHUNKS == 2, "a TMA-store epilogue stages two 32-column chunks per warp");
   const int warp = warp_id();
   const int lane = lane_id();
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
@@ -532,15 +540,34 @@ __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
       if (!ok) continue;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
-      const EpiCtx cx{stg_s + (warp - 2) * GEMM_STG_WARP_BYTES, m0 + q * 32, min(32, M - (m0 + q * 32)), lane};
+      EpiCtx cx{stg_s + (warp - 2) * Cfg::kStgWarpBytes, m0 + q * 32, min(32, M - (m0 + q * 32)), lane, 0};
+      if constexpr (Epi::kTmaStore) {
+        // the previous tile's store must be done reading the staging block
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int c = ch * CHUNKS; c < (ch + 1) * CHUNKS; ++c) {
         float v[32];
         tmem_ld32(tmem_addr(tmem, q * 32, buf * BN + c * 32), v);
+        cx.chunk = c - ch * CHUNKS;
         epi(row, n0 + c * 32, v, cps, cx);
       }
       tc_fence_before();
       mbar_arrive(&ctl->acc_empty[buf]);
+      if constexpr (Epi::kTmaStore) {
+        fence_proxy_async_smem();  // the lanes' staging writes, visible to the TMA unit
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, cx.stg, n0 + ch * CHUNKS * 32, m0 + q * 32);
+          bulk_commit();
+        }
+      }
+    }
+    // the CTA's shared memory must outlive the stores' reads, and the table
+    // is complete when the kernel ends
+    if constexpr (Epi::kTmaStore) {
+      if (lane == 0) bulk_wait<0>();
     }
   }
 

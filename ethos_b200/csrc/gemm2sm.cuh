@@ -55,6 +55,7 @@ struct Gemm2Cfg {
   static constexpr int kSmem = G2_STAGES * G2_STAGE_BYTES + GEMM_COLP_BYTES + kEpiWarps * GEMM_STG_WARP_BYTES + 1024 +
                                static_cast<int>(sizeof(Gemm2Ctl));
   static_assert(kSmem <= 227 * 1024, "2-SM GEMM shared memory");
+  static_assert(!Epi::kTmaStore, "TMA-store epilogues run on the single-SM kernel");
 };
 
 // ------------------------------------------------------ cluster helpers --
@@ -299,11 +300,12 @@ __global__ void __launch_bounds__(Gemm2Cfg<Epi>::kThreads, 1)
       if (ok) {
         tc_fence_after();
         const int row = m0 + q * 32 + lane;
-        const EpiCtx cx{stg_s + (warp - 2) * GEMM_STG_WARP_BYTES, m0 + q * 32, min(32, M - (m0 + q * 32)), lane};
+        EpiCtx cx{stg_s + (warp - 2) * GEMM_STG_WARP_BYTES, m0 + q * 32, min(32, M - (m0 + q * 32)), lane, 0};
 #pragma unroll 1
         for (int c = ch * CHUNKS; c < (ch + 1) * CHUNKS; ++c) {
           float v[32];
           tmem_ld32(tmem_addr(tmem, q * 32, buf * G2_BN + c * 32), v);
+          cx.chunk = c - ch * CHUNKS;
           epi(row, n0 + c * 32, v, cps, cx);
         }
       }

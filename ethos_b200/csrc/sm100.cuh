@@ -148,9 +148,30 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* t
 }
 
 // Make generic-proxy writes to shared memory visible to the async proxy
-// (tcgen05.mma operand reads).
+// (tcgen05.mma operand reads, TMA stores).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2-D tiled bulk tensor store shared -> global (this GPU's memory), tracked
+// by the issuing thread's bulk groups.  The box's rows outside the tensor are
+// not written.  x (the contiguous coordinate) must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N of this thread's bulk groups are incomplete (writes done)
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ------------------------------------------------------------ cp.async 16B --
@@ -366,108 +387,86 @@ __device__ __forceinline__ float ex2_approx(float t) {
 // approximate='none'), with the normal CDF written through its tail mass
 //   h = 1 - Phi(|x|) = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt(2)):
 //   Phi(x) = 1 - h (x >= 0),  Phi(x) = h (x < 0),  GELU(x) = max(x, 0) - |x| h.
-// erfcx is evaluated in the rational form of Hastings' erfc approximation
-// (Abramowitz & Stegun 7.1.26), erfcx(z) ~ t (C0 + C1 t + ... + C4 t^4) with
-// t = 1 / (1 + P z), P and C_k refit by csrc/fit_gelu.py (fp32 evaluation:
-// |Phi error| <= 3e-7, |GELU error| <= 1.2e-7); t takes one rcp.approx and
-// the exponential one ex2.approx.  d GELU / dx = Phi(x) + x phi(x) reuses the
-// same exponential: phi(x) = exp(-x^2 / 2) / sqrt(2 pi).
+// h is one power of two, h = 2^(kE x^2 + Q(u)), kE = -1 / (2 ln 2), where
+// Q(a) = log2(0.5 erfcx(a / sqrt 2)) is a degree-7 polynomial in
+// u = min(|x|, kA) * (2 / kA) - 1 fitted by weighted minimax (Lawson's
+// algorithm; csrc/fit_gelu.py): fp32 evaluation within 1.9e-7 of Phi and
+// 7.1e-8 + 2^-23 |GELU| of the erf GELU.  Clamping |x| at kA = 5.5 keeps the
+// Gaussian factor exact, so the tail stays below the true mass times
+// |x| / 5.5 there.  One ex2.approx per value and no reciprocal; the
+// derivative d GELU / dx = Phi(x) + x phi(x) takes the density from a second
+// one, phi(x) = 2^(kE x^2 + log2(1 / sqrt(2 pi))).
 namespace gelu_detail {
-constexpr float kP = 3.327062726e-01f;  // P / sqrt(2): t = 1 / (1 + kP |x|)
-constexpr float kE = -0.72134752f;      // -log2(e) / 2
-constexpr float kPdf = 0.39894228f;     // 1 / sqrt(2 pi)
-constexpr float C0 = 2.474880069e-01f, C1 = 3.996735513e-01f, C2 = -1.586927176e-01f, C3 = 7.302848697e-01f,
-                C4 = -2.187540382e-01f;
+constexpr float kA = 5.500000000e+00f;    // clamp of |x| for the polynomial
+constexpr float kU = 3.636363745e-01f;    // 2 / kA: u = min(|x|, kA) kU - 1
+constexpr float kE = -7.213475108e-01f;   // -1 / (2 ln 2): exp(-x^2 / 2) = 2^(kE x^2)
+constexpr float kPdf2 = -1.325748086e+00f;  // log2(1 / sqrt(2 pi))
+constexpr float Q0 = -2.935396671e+00f, Q1 = -1.197389245e+00f, Q2 = 4.303870797e-01f, Q3 = -1.840556413e-01f,
+                Q4 = 8.516710997e-02f, Q5 = -8.533163927e-03f, Q6 = 3.714597598e-02f, Q7 = 7.281220052e-03f;
 }  // namespace gelu_detail
 
-__device__ __forceinline__ float rcp_approx(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
+// exponent of h = 2^(kE x^2 + Q(u)) for one value
+__device__ __forceinline__ float gelu_tail_exponent(float x) {
+  using namespace gelu_detail;
+  const float u = fmaf(fminf(fabsf(x), kA), kU, -1.0f);
+  float q = Q7;
+  q = fmaf(q, u, Q6);
+  q = fmaf(q, u, Q5);
+  q = fmaf(q, u, Q4);
+  q = fmaf(q, u, Q3);
+  q = fmaf(q, u, Q2);
+  q = fmaf(q, u, Q1);
+  q = fmaf(q, u, Q0);
+  return fmaf(x * x, kE, q);
 }
 
-// 1 / d for two values d >= 1 on the FMA pipe (no MUFU operation): the
-// integer seed 0x7EF311C7 - bits(d) is within 12 % of 1 / d, and three
-// Newton steps t <- t (2 - d t) square the relative error each time
-// (0.12 -> 1.4e-2 -> 2e-4 -> 4e-8).
-__device__ __forceinline__ unsigned long long rcp2_newton(unsigned long long d, float d0, float d1) {
-  unsigned long long t = pk2(__int_as_float(0x7EF311C7 - __float_as_int(d0)),
-                             __int_as_float(0x7EF311C7 - __float_as_int(d1)));
-  const unsigned long long nd = pk2(-d0, -d1), two = pk2(2.0f, 2.0f);
-#pragma unroll
-  for (int i = 0; i < 3; ++i) t = fmul2(t, ffma2(nd, t, two));
-  (void)d;
-  return t;
-}
-
-// h = 0.5 exp(-x^2 / 2) erfcx(|x| / sqrt 2) -- the tail mass 1 - Phi(|x|) --
-// for two values, the polynomial on packed pairs; the 0.5 rides in the ex2
-// argument (log2 0.5 = -1) and the half-exponential e = 0.5 exp(-x^2 / 2) is
-// returned too.  With ETHOS_GELU_RCP_NR (the default) the reciprocal runs
-// on the FMA pipe (rcp2_newton), leaving one MUFU operation (ex2) per value:
-// the expert-table epilogue measured 0.1106 against 0.1152 ms with two MUFU
-// operations (config 2, B200).
-#ifndef ETHOS_GELU_RCP_NR
-#define ETHOS_GELU_RCP_NR 1
-#endif
-__device__ __forceinline__ void gelu_tail2(float x0, float x1, float& h0, float& h1, float& e0, float& e1) {
+// h = 1 - Phi(|x|) for two values, the polynomial and the exponent on packed
+// pairs (the same fp32 operations as the scalar form, so the same results)
+__device__ __forceinline__ void gelu_tail2(float x0, float x1, float& h0, float& h1) {
   using namespace gelu_detail;
-  const unsigned long long d = ffma2(pk2(fabsf(x0), fabsf(x1)), pk2(kP, kP), pk2(1.0f, 1.0f));
-  float d0, d1;
-  upk2(d, d0, d1);
-#if ETHOS_GELU_RCP_NR
-  const unsigned long long t = rcp2_newton(d, d0, d1);
-#else
-  const unsigned long long t = pk2(rcp_approx(d0), rcp_approx(d1));
-#endif
-  unsigned long long q = pk2(C4, C4);
-  q = ffma2(q, t, pk2(C3, C3));
-  q = ffma2(q, t, pk2(C2, C2));
-  q = ffma2(q, t, pk2(C1, C1));
-  q = ffma2(q, t, pk2(C0, C0));
-  e0 = ex2_approx(fmaf(x0 * kE, x0, -1.0f));  // 0.5 exp(-x^2 / 2)
-  e1 = ex2_approx(fmaf(x1 * kE, x1, -1.0f));
-  const unsigned long long h = fmul2(fmul2(q, t), pk2(e0, e1));
-  upk2(h, h0, h1);
+  const unsigned long long u = ffma2(pk2(fminf(fabsf(x0), kA), fminf(fabsf(x1), kA)), pk2(kU, kU), pk2(-1.0f, -1.0f));
+  unsigned long long q = pk2(Q7, Q7);
+  q = ffma2(q, u, pk2(Q6, Q6));
+  q = ffma2(q, u, pk2(Q5, Q5));
+  q = ffma2(q, u, pk2(Q4, Q4));
+  q = ffma2(q, u, pk2(Q3, Q3));
+  q = ffma2(q, u, pk2(Q2, Q2));
+  q = ffma2(q, u, pk2(Q1, Q1));
+  q = ffma2(q, u, pk2(Q0, Q0));
+  const unsigned long long xv = pk2(x0, x1);
+  const unsigned long long s = ffma2(fmul2(xv, xv), pk2(kE, kE), q);
+  float s0, s1;
+  upk2(s, s0, s1);
+  h0 = ex2_approx(s0);
+  h1 = ex2_approx(s1);
 }
-__device__ __forceinline__ float gelu_tail(float x, float& e) {
-  using namespace gelu_detail;
-  const float t = rcp_approx(fmaf(fabsf(x), kP, 1.0f));
-  float q = C4;
-  q = fmaf(q, t, C3);
-  q = fmaf(q, t, C2);
-  q = fmaf(q, t, C1);
-  q = fmaf(q, t, C0);
-  e = ex2_approx(fmaf(x * kE, x, -1.0f));  // 0.5 exp(-x^2 / 2)
-  return e * (q * t);
+__device__ __forceinline__ float gelu_tail(float x) { return ex2_approx(gelu_tail_exponent(x)); }
+__device__ __forceinline__ float gelu_erf(float x) { return fmaf(-fabsf(x), gelu_tail(x), fmaxf(x, 0.0f)); }
+// normal density phi(x) = 2^(kE x^2 + log2(1 / sqrt(2 pi)))
+__device__ __forceinline__ float gelu_pdf(float x) {
+  return ex2_approx(fmaf(x * x, gelu_detail::kE, gelu_detail::kPdf2));
 }
-__device__ __forceinline__ float gelu_erf(float x) {
-  float e;
-  return fmaf(-fabsf(x), gelu_tail(x, e), fmaxf(x, 0.0f));
-}
-// d GELU / dx = Phi(x) + x phi(x), phi(x) = exp(-x^2/2) / sqrt(2 pi) =
-// 2 e / sqrt(2 pi) with e the half-exponential of the tail
+// d GELU / dx = Phi(x) + x phi(x)
 __device__ __forceinline__ float gelu_erf_grad(float x) {
-  float e;
-  const float h = gelu_tail(x, e);
+  const float h = gelu_tail(x);
   const float phi = x >= 0.0f ? 1.0f - h : h;
-  return fmaf(x * (2.0f * gelu_detail::kPdf), e, phi);
+  return fmaf(x, gelu_pdf(x), phi);
 }
 __device__ __forceinline__ void gelu_erf2(float x0, float x1, float& g0, float& g1) {
-  float h0, h1, e0, e1;
-  gelu_tail2(x0, x1, h0, h1, e0, e1);
+  float h0, h1;
+  gelu_tail2(x0, x1, h0, h1);
   g0 = fmaf(-fabsf(x0), h0, fmaxf(x0, 0.0f));
   g1 = fmaf(-fabsf(x1), h1, fmaxf(x1, 0.0f));
 }
-// GELU and its derivative of two values from one evaluation
+// GELU and its derivative of two values from one tail evaluation
 __device__ __forceinline__ void gelu_erf_and_grad2(float x0, float x1, float& g0, float& g1, float& d0, float& d1) {
-  float h0, h1, e0, e1;
-  gelu_tail2(x0, x1, h0, h1, e0, e1);
+  float h0, h1;
+  gelu_tail2(x0, x1, h0, h1);
   g0 = fmaf(-fabsf(x0), h0, fmaxf(x0, 0.0f));
   g1 = fmaf(-fabsf(x1), h1, fmaxf(x1, 0.0f));
   const float p0 = x0 >= 0.0f ? 1.0f - h0 : h0, p1 = x1 >= 0.0f ? 1.0f - h1 : h1;
-  d0 = fmaf(x0 * (2.0f * gelu_detail::kPdf), e0, p0);
-  d1 = fmaf(x1 * (2.0f * gelu_detail::kPdf), e1, p1);
+  d0 = fmaf(x0, gelu_pdf(x0), p0);
+  d1 = fmaf(x1, gelu_pdf(x1), p1);
 }
 
 // Warp transpose-reduce: on entry lane l holds v[0..31] (32 columns of one
