@@ -209,8 +209,9 @@ int operand_tmap(CUtensorMap* m, const GemmOperand& o, int64_t mn, int64_t k, in
 template <class Epi, bool AMN, bool BMN, int BN>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int ksplit, const Epi& epi,
                   int* err, cudaStream_t stream, const DeviceInfo& dev, int hold_unit = -1,
-                  const CUtensorMap* tc = nullptr) {
+                  const CUtensorMap* tc = nullptr, const CUtensorMap* td = nullptr) {
   if (Epi::kTmaStore && tc == nullptr) return ETHOS_ERR_INVALID_ARG;
+  if (GemmCfg<Epi>::kTmaOutputs == 2 && td == nullptr) return ETHOS_ERR_INVALID_ARG;
   auto kern = k_gemm<Epi, AMN, BMN, BN>;
   int st = smem_attr_once(reinterpret_cast<const void*>(kern), GemmCfg<Epi>::kSmem);
   if (st != ETHOS_OK) return st;
@@ -219,7 +220,7 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   const int grid = units < dev.sm_count ? units : dev.sm_count;
   if (grid <= 0) return ETHOS_OK;
   return launch_pdl(kern, dim3(grid), dim3(GemmCfg<Epi>::kThreads), GemmCfg<Epi>::kSmem, stream, ta, tb,
-                    tc != nullptr ? *tc : ta, M, N, K, ksplit, epi, err, hold_unit);
+                    tc != nullptr ? *tc : ta, td != nullptr ? *td : ta, M, N, K, ksplit, epi, err, hold_unit);
 }
 
 template <class Epi, bool AMN = false, bool BMN = false>
@@ -346,8 +347,9 @@ int launch_gemm2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
 // Forward-path GEMM: both operands K-major (tensor maps built by the caller).
 template <class Epi>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const Epi& epi, int* err,
-                cudaStream_t stream, const DeviceInfo& dev, const CUtensorMap* tc = nullptr) {
-  return launch_gemm_t<Epi, false, false, 256>(ta, tb, M, N, K, 1, epi, err, stream, dev, -1, tc);
+                cudaStream_t stream, const DeviceInfo& dev, const CUtensorMap* tc = nullptr,
+                const CUtensorMap* td = nullptr) {
+  return launch_gemm_t<Epi, false, false, 256>(ta, tb, M, N, K, 1, epi, err, stream, dev, -1, tc, td);
 }
 
 // ------------------------------------------------------- workspace layout --
@@ -452,18 +454,16 @@ int build_table(const ethos_dims& d, const void* latents, const void* w1, __half
   CUtensorMap tm_e, tm_w1;
   if ((st = make_tmap_bf16(&tm_e, latents, N, EX_DL, 128)) != ETHOS_OK) return st;
   if ((st = make_tmap_bf16(&tm_w1, w1, EX_DH, EX_DL, 256)) != ETHOS_OK) return st;
-  if (gtab != nullptr) {  // training: G = gelu'(E W1^T) alongside, for the backward
-    EpiGeluBwdF16 eg;
-    eg.h_out = table;
-    eg.g_out = gtab;
-    eg.ldo = EX_DH;
-    eg.M = N;
-    return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, eg, err, stream, dev);
-  }
-  // the table leaves through TMA stores of 32-row x 64-column boxes (128-byte
+  // the tables leave through TMA stores of 32-row x 64-column boxes (128-byte
   // swizzle), the layout the epilogue stages
   CUtensorMap tm_h;
   if ((st = make_tmap_bf16(&tm_h, table, N, EX_DH, 32, 0, 64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16)) != ETHOS_OK) return st;
+  if (gtab != nullptr) {  // training: G = gelu'(E W1^T) alongside, for the backward
+    CUtensorMap tm_g;
+    if ((st = make_tmap_bf16(&tm_g, gtab, N, EX_DH, 32, 0, 64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16)) != ETHOS_OK)
+      return st;
+    return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, EpiGeluBwdF16{}, err, stream, dev, &tm_h, &tm_g);
+  }
   return launch_gemm(tm_e, tm_w1, N, EX_DH, EX_DL, EpiGeluF16{}, err, stream, dev, &tm_h);
 }
 
@@ -766,14 +766,7 @@ int expert_bwd_core(const ethos_dims& d, const ExpertBwdIO& io, const BwdScratch
   const __half* htab_ = io.htab ? static_cast<const __half*>(io.htab) : s.htab;
   const __half* gtab_ = io.gtab ? static_cast<const __half*>(io.gtab) : s.gtab;
   if (io.htab == nullptr) {
-    EpiGeluBwdF16 e;
-    e.h_out = s.htab;
-    e.g_out = s.gtab;
-    e.ldo = EX_DH;
-    e.M = N;
-    if ((st = gemm(GemmOperand{io.latents, EX_DL, false}, GemmOperand{io.w1, EX_DL, false}, N, EX_DH, EX_DL, 1, e,
-                   dev_err, sm, dev)) != ETHOS_OK)
-      return st;
+    if ((st = build_table(d, io.latents, io.w1, s.htab, s.gtab, dev_err, sm, dev)) != ETHOS_OK) return st;
   }
   // per token: dw, a, ddot per selection; dxp (fp32 + bf16 operand)
   {

@@ -54,10 +54,14 @@ struct GemmCfg {
   static_assert(kEpiWarps == 8 || kEpiWarps == 16, "8 or 16 epilogue warps");
   static constexpr int kEpiThreads = 32 * kEpiWarps;
   static constexpr int kThreads = 64 + kEpiThreads;
-  static constexpr int kStages = kEpiWarps == 16 ? 3 : GEMM_STAGES;
-  // a TMA-store epilogue stages its warp's whole 32-row x 128-byte block
-  static constexpr int kStgWarpBytes = Epi::kTmaStore ? 32 * 128 : GEMM_STG_WARP_BYTES;
-  static constexpr int kSmem = kStages * GEMM_STAGE_BYTES + GEMM_COLP_BYTES + kEpiWarps * kStgWarpBytes + 1024 +
+  // a TMA-store epilogue stages its warp's whole 32-row x 128-byte block of
+  // each output (one or two outputs, tensor maps tmC and tmD); with two, the
+  // ring keeps two stages (one tile's K = 128 here) to make room for them
+  static constexpr int kTmaOutputs = Epi::kTmaStore ? Epi::kTmaOutputs : 0;
+  static constexpr int kStages = kEpiWarps == 16 ? (kTmaOutputs == 2 ? 2 : 3) : GEMM_STAGES;
+  static constexpr int kStgWarpBytes = Epi::kTmaStore ? 32 * 128 * kTmaOutputs : GEMM_STG_WARP_BYTES;
+  static constexpr int kColpBytes = Epi::kColParamBytes > 0 ? GEMM_COLP_BYTES : 0;
+  static constexpr int kSmem = kStages * GEMM_STAGE_BYTES + kColpBytes + kEpiWarps * kStgWarpBytes + 1024 +
                                static_cast<int>(sizeof(GemmCtl));
   static_assert(kSmem <= 227 * 1024, "GEMM shared memory");
 };
@@ -114,6 +118,7 @@ struct EpiNoColParams {
   // block (EpiCtx::stg, 32 rows x 128 B, 128-byte swizzle) and the kernel
   // stores the block with one TMA store per warp and tile (tensor map tmC)
   static constexpr bool kTmaStore = false;
+  static constexpr int kTmaOutputs = 1;
   __device__ __forceinline__ void load_col_params(int, uint8_t*, int) const {}
 };
 
@@ -199,6 +204,7 @@ struct EpiProj {
   static constexpr int kColParamBytes = 8;  // float2 (scale, offset) or (bias, -)
   static constexpr int kEpiWarps = 8;
   static constexpr bool kTmaStore = false;
+  static constexpr int kTmaOutputs = 1;
   int M;   // tokens
   int HQ;  // H * d_query
   int dq;
@@ -290,9 +296,21 @@ struct EpiProj {
   }
 };
 
+// Lane r's 64 bytes w[0..3] of chunk `chunk` into its row of a staged 32 x 64
+// fp16 block: 16-byte piece p of row r at r * 128 + ((p ^ (r & 7)) << 4), the
+// 128-byte swizzle of the store's tensor map, free of bank conflicts.
+__device__ __forceinline__ void stage_row_sw128(uint8_t* block, int r, int chunk, const uint4 (&w)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int p = chunk * 4 + j;
+    *reinterpret_cast<uint4*>(block + r * 128 + ((p ^ (r & 7)) << 4)) = w[j];
+  }
+}
+
 // Expert hidden table: out[row][col] = fp16(gelu_erf(v)) for the expert-
 // expansion GEMM E @ W1^T (row = expert id, col = hidden unit; model.py:323
-// evaluated once per expert instead of once per selection).
+// evaluated once per expert instead of once per selection), stored through
+// the tensor map tmC.
 struct EpiGeluF16 : EpiNoColParams {
   static constexpr int kEpiWarps = 16;  // 0.117 ms vs 0.126 ms with 8 (262144 x 512 table)
   // The table rows leave through TMA stores of each warp's staged 32 x 64
@@ -301,7 +319,7 @@ struct EpiGeluF16 : EpiNoColParams {
   // 16.8 M L2 write requests per launch).
   static constexpr bool kTmaStore = true;
   __device__ __forceinline__ void operator()(int, int, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
-    const int r = cx.lane;
+    uint4 w4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint32_t w[4];
@@ -312,23 +330,20 @@ struct EpiGeluF16 : EpiNoColParams {
         const __half2 hh = __floats2half2_rn(g0, g1);
         w[u] = *reinterpret_cast<const uint32_t*>(&hh);
       }
-      // 16-byte piece p of row r at r * 128 + ((p ^ (r & 7)) << 4): the
-      // 128-byte swizzle of the store's tensor map, free of bank conflicts
-      const int p = cx.chunk * 4 + j;
-      *reinterpret_cast<uint4*>(cx.stg + r * 128 + ((p ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      w4[j] = make_uint4(w[0], w[1], w[2], w[3]);
     }
+    stage_row_sw128(cx.stg, cx.lane, cx.chunk, w4);
   }
 };
 
-// Backward tables: H = fp16(gelu_erf(v)) and G = fp16(gelu_erf'(v)) for the
-// pre-activations v = E @ W1^T of every expert.
+// Backward tables: H = fp16(gelu_erf(v)) (tmC) and G = fp16(gelu_erf'(v))
+// (tmD) for the pre-activations v = E @ W1^T of every expert, each through
+// TMA stores of the warp's staged blocks (H block, then G block 4 KB later).
 struct EpiGeluBwdF16 : EpiNoColParams {
   static constexpr int kEpiWarps = 16;
-  __half* h_out;
-  __half* g_out;
-  int64_t ldo;
-  int M;
-  __device__ __forceinline__ void operator()(int, int col, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
+  static constexpr bool kTmaStore = true;
+  static constexpr int kTmaOutputs = 2;
+  __device__ __forceinline__ void operator()(int, int, float (&v)[32], const uint8_t*, const EpiCtx& cx) const {
     uint4 h4[4], g4[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -345,11 +360,8 @@ struct EpiGeluBwdF16 : EpiNoColParams {
       h4[j] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
       g4[j] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
     }
-    // two outputs: the staged transpose pays here (whole backward 2.50 ->
-    // 2.38 ms at config 5), unlike in the one-output forward table
-    const int64_t off = static_cast<int64_t>(cx.row0) * ldo + col;
-    warp_store_rows64(cx, h4, reinterpret_cast<char*>(h_out + off), ldo * 2);
-    warp_store_rows64(cx, g4, reinterpret_cast<char*>(g_out + off), ldo * 2);
+    stage_row_sw128(cx.stg, cx.lane, cx.chunk, h4);
+    stage_row_sw128(cx.stg + 32 * 128, cx.lane, cx.chunk, g4);
   }
 };
 
@@ -375,8 +387,8 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32_major(int M, int N, b
 template <class Epi, bool kAMN, bool kBMN, int BN>
 __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-           const __grid_constant__ CUtensorMap tmC, int M, int N, int K, int ksplit, Epi epi, int* err,
-           int hold_unit) {
+           const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD, int M, int N, int K,
+           int ksplit, Epi epi, int* err, int hold_unit) {
   static_assert(BN == 128 || BN == 256, "N tile is 128 or 256");
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = GEMM_A_BYTES + B_BYTES;
@@ -386,7 +398,7 @@ __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* colp_s = smem + STAGES * GEMM_STAGE_BYTES;
-  uint8_t* stg_s = colp_s + GEMM_COLP_BYTES;
+  uint8_t* stg_s = colp_s + Cfg::kColpBytes;
   GemmCtl* ctl = reinterpret_cast<GemmCtl*>(stg_s + Cfg::kEpiWarps * Cfg::kStgWarpBytes);
   static_assert(!Epi::kTmaStore || CHUNKS == 2, "a TMA-store epilogue stages two 32-column chunks per warp");
   const int warp = warp_id();
@@ -560,6 +572,7 @@ __global__ void __launch_bounds__(GemmCfg<Epi>::kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           tma_store_2d(&tmC, cx.stg, n0 + ch * CHUNKS * 32, m0 + q * 32);
+          if constexpr (Cfg::kTmaOutputs == 2) tma_store_2d(&tmD, cx.stg + 32 * 128, n0 + ch * CHUNKS * 32, m0 + q * 32);
           bulk_commit();
         }
       }
