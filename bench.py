@@ -311,9 +311,11 @@ def train_block(args, rank, world, local, dev, layer=None, steps=None, sampler=T
     x = seeded_input(T, CFG2["d_model"], seed=rank).to(device=dev, dtype=torch.bfloat16)
     gy = (torch.randn((T, CFG2["d_model"]), generator=tensor_generator(rank, "bench.gy")) * 1e-3).to(
         device=dev, dtype=torch.bfloat16)
-    # AdamW as the reference's DeepSpeed config (train.py:74-79), fused over all
-    # of the layer's parameters in one launch, fp32 master weights for bf16
-    opt = FusedAdamW(layer.parameters(), lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    # AdamW as the reference's DeepSpeed config (train.py:74-79, with its
+    # gradient clipping at global norm 1.0, train.py:100), fused over all of
+    # the layer's parameters in one launch, fp32 master weights for bf16
+    opt = FusedAdamW(layer.parameters(), lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                     max_grad_norm=1.0)
     comm = None
     if world > 1:
         overlap_grad_allreduce(layer)  # all-reduce inside the backward, overlapped
@@ -379,7 +381,7 @@ def train_block(args, rank, world, local, dev, layer=None, steps=None, sampler=T
                global_batch=T * world, parallelism=f"dp{world}", dtype="bf16 (fp32 gradients and master weights)",
                workload="config 5: forward (BN on batch statistics), backward through all 37 parameters, "
                         "NCCL AVG all-reduce of the fp32 gradients overlapped with the backward (N > 1), "
-                        "fused AdamW with fp32 master weights",
+                        "global-norm gradient clipping at 1.0 and fused AdamW with fp32 master weights",
                l2="flushed between timed steps (256 MiB write)", gpu_launches=n_launch,
                allreduce=dict(bytes_per_step=grad_bytes if world > 1 else 0,
                               span_ms=ar[0] if ar else 0.0, exposed_ms=ar[1] if ar else 0.0,

@@ -79,7 +79,9 @@ EXPORTS = {
     "ethos_product_key_topk": (_I, [_DIMS, _P, _P, _P, _P, _P, _P]),
     "ethos_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _F, _I, _P, _P]),
     "ethos_gemm_bf16_ex": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _F, _I, _P, _P]),
-    "ethos_adamw_step": (_I, [_P, _I, _I64, _F, _F, _F, _F, _F, _I64, _P, _P]),
+    "ethos_adamw_step": (_I, [_P, _I, _I64, _F, _F, _F, _F, _F, _I64, _P, _P, _P]),
+    "ethos_grad_clip_workspace_size": (_SZ, []),
+    "ethos_grad_clip_coef": (_I, [_P, _I, _F, _P, _SZ, _P, _P, _P]),
     "ethos_set_wait_limit_ns": (_I, [ctypes.c_uint64]),
     "ethos_test_gelu": (_I, [_P, _P, _I64, _P]),
     "ethos_forward_workspace_size_f32": (_SZ, [_DIMS, _I]),

@@ -1563,7 +1563,8 @@ int ethos_router_backward(const ethos_dims* dims, int bn_training, float bn_eps,
 }
 
 int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t max_n, float lr, float beta1,
-                     float beta2, float eps, float weight_decay, int64_t step, int* dev_err, void* stream) {
+                     float beta2, float eps, float weight_decay, int64_t step, const float* grad_scale, int* dev_err,
+                     void* stream) {
   (void)dev_err;
   if (num_tensors == 0 || max_n == 0) return ETHOS_OK;
   if (tensors == nullptr || num_tensors < 0 || num_tensors > 65535 || max_n < 0 || step < 1)
@@ -1587,7 +1588,29 @@ int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t 
   if (bx < 1) bx = 1;
   count_launch();
   k_adamw<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(num_tensors)), threads, 0,
-            static_cast<cudaStream_t>(stream)>>>(tensors, s);
+            static_cast<cudaStream_t>(stream)>>>(tensors, s, grad_scale);
+  return launch_status();
+}
+
+size_t ethos_grad_clip_workspace_size(void) { return sizeof(double) * GRAD_CLIP_BLOCKS; }
+
+int ethos_grad_clip_coef(const ethos_adam_tensor* tensors, int num_tensors, float max_norm, void* workspace,
+                         size_t workspace_bytes, float* out, int* dev_err, void* stream) {
+  (void)dev_err;
+  if (tensors == nullptr || out == nullptr || num_tensors <= 0 || !(max_norm > 0.f)) return ETHOS_ERR_INVALID_ARG;
+  if (workspace == nullptr || workspace_bytes < ethos_grad_clip_workspace_size() ||
+      (reinterpret_cast<uintptr_t>(workspace) & 7u) != 0)
+    return ETHOS_ERR_WORKSPACE;
+  int st;
+  DeviceInfo* dev = nullptr;
+  if ((st = device_info(&dev)) != ETHOS_OK) return st;
+  const cudaStream_t sm = static_cast<cudaStream_t>(stream);
+  double* partial = static_cast<double*>(workspace);
+  count_launch();
+  k_grad_sqnorm<<<GRAD_CLIP_BLOCKS, GRAD_CLIP_THREADS, 0, sm>>>(tensors, num_tensors, partial);
+  if ((st = launch_status()) != ETHOS_OK) return st;
+  count_launch();
+  k_grad_clip_coef<<<1, GRAD_CLIP_THREADS, 0, sm>>>(partial, GRAD_CLIP_BLOCKS, max_norm, out);
   return launch_status();
 }
 

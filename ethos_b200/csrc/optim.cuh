@@ -26,8 +26,12 @@ __device__ __forceinline__ float adam_elem(float p, float g, float& m, float& v,
   return p - s.step_size * (m / denom);
 }
 
-__global__ void k_adamw(const ethos_adam_tensor* __restrict__ tensors, AdamScalars s) {
+// grad_scale (device, may be null): every gradient is multiplied by
+// grad_scale[0] before the update (the clip coefficient of k_grad_clip_coef)
+__global__ void k_adamw(const ethos_adam_tensor* __restrict__ tensors, AdamScalars s,
+                        const float* __restrict__ grad_scale) {
   const ethos_adam_tensor td = tensors[blockIdx.y];
+  const float gs = grad_scale != nullptr ? *grad_scale : 1.0f;
   const int64_t n = td.n;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
   const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(td.param) | reinterpret_cast<uintptr_t>(td.grad) |
@@ -65,7 +69,7 @@ __global__ void k_adamw(const ethos_adam_tensor* __restrict__ tensors, AdamScala
         p[0] = pa.x; p[1] = pa.y; p[2] = pa.z; p[3] = pa.w;
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) p[u] = adam_elem(p[u], g[u], m[u], v[u], s);
+      for (int u = 0; u < 4; ++u) p[u] = adam_elem(p[u], g[u] * gs, m[u], v[u], s);
       *reinterpret_cast<float4*>(td.exp_avg + i) = make_float4(m[0], m[1], m[2], m[3]);
       *reinterpret_cast<float4*>(td.exp_avg_sq + i) = make_float4(v[0], v[1], v[2], v[3]);
       if (td.master != nullptr) *reinterpret_cast<float4*>(td.master + i) = make_float4(p[0], p[1], p[2], p[3]);
@@ -81,8 +85,9 @@ __global__ void k_adamw(const ethos_adam_tensor* __restrict__ tensors, AdamScala
     } else {
       for (int u = 0; u < cnt; ++u) {
         const int64_t j = i + u;
-        const float gg = td.grad_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(td.grad)[j])
-                                      : static_cast<const float*>(td.grad)[j];
+        const float gg = (td.grad_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(td.grad)[j])
+                                       : static_cast<const float*>(td.grad)[j]) *
+                         gs;
         float mm = td.exp_avg[j], vv = td.exp_avg_sq[j];
         const float pp = td.master != nullptr ? td.master[j]
                          : td.param_bf16      ? __bfloat162float(static_cast<const __nv_bfloat16*>(td.param)[j])
@@ -97,6 +102,79 @@ __global__ void k_adamw(const ethos_adam_tensor* __restrict__ tensors, AdamScala
           static_cast<float*>(td.param)[j] = np;
       }
     }
+  }
+}
+
+// ---------------------------------------------------- gradient clipping --
+// Global-norm clipping as torch.nn.utils.clip_grad_norm_ (and DeepSpeed's
+// gradient_clipping, train.py:100) defines it: norm = sqrt(sum of every
+// gradient element squared), coef = min(1, max_norm / (norm + 1e-6)).  The sum
+// does not depend on scheduling, so data-parallel ranks holding the same
+// all-reduced gradients get bit-identical coefficients: a fixed grid of
+// GRAD_CLIP_BLOCKS blocks walks every tensor in table order, each thread
+// taking fixed elements of each and accumulating in fp64; block b writes its
+// sum to partial[b], and one block adds the partials in a fixed order.
+constexpr int GRAD_CLIP_BLOCKS = 592;
+constexpr int GRAD_CLIP_THREADS = 256;
+
+__global__ void __launch_bounds__(GRAD_CLIP_THREADS) k_grad_sqnorm(const ethos_adam_tensor* __restrict__ tensors,
+                                                                   int num_tensors, double* __restrict__ partial) {
+  __shared__ double red[GRAD_CLIP_THREADS];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
+  const int64_t first = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  double acc = 0.0;
+  for (int y = 0; y < num_tensors; ++y) {
+    const ethos_adam_tensor td = tensors[y];
+    const int64_t n = td.n;
+    const bool vec = (n % 4 == 0) && (reinterpret_cast<uintptr_t>(td.grad) & (td.grad_bf16 ? 7u : 15u)) == 0;
+    for (int64_t i = first; i < n; i += stride) {
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      if (vec) {
+        if (td.grad_bf16) {
+          const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(td.grad) + i);
+          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+          g[0] = a.x; g[1] = a.y; g[2] = b.x; g[3] = b.y;
+        } else {
+          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(td.grad) + i);
+          g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
+        }
+      } else {
+        const int cnt = static_cast<int>(n - i < 4 ? n - i : 4);
+        for (int u = 0; u < cnt; ++u)
+          g[u] = td.grad_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(td.grad)[i + u])
+                              : static_cast<const float*>(td.grad)[i + u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc = fma(static_cast<double>(g[u]), static_cast<double>(g[u]), acc);
+    }
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = GRAD_CLIP_THREADS / 2; w > 0; w >>= 1) {
+    if (static_cast<int>(threadIdx.x) < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partial[blockIdx.x] = red[0];
+}
+
+// out[0] = norm, out[1] = min(1, max_norm / (norm + 1e-6)); one block
+__global__ void __launch_bounds__(GRAD_CLIP_THREADS) k_grad_clip_coef(const double* __restrict__ partial, int count,
+                                                                      float max_norm, float* __restrict__ out) {
+  __shared__ double red[GRAD_CLIP_THREADS];
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) acc += partial[i];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = GRAD_CLIP_THREADS / 2; w > 0; w >>= 1) {
+    if (static_cast<int>(threadIdx.x) < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float norm = static_cast<float>(sqrt(red[0]));
+    const float coef = max_norm / (norm + 1e-6f);
+    out[0] = norm;
+    out[1] = coef > 1.0f ? 1.0f : coef;  // a NaN norm stays NaN, as torch.clamp leaves it
   }
 }
 

@@ -415,7 +415,9 @@ int ethos_test_gelu(const float* x, float* out, int64_t n, void* stream);
  * `p` is `master` (fp32) when given, whose new value is then also written to
  * `param` rounded to its dtype; otherwise `param` itself (fp32 or bf16).
  * `tensors` is a DEVICE array of `num_tensors` descriptors; `max_n` is the
- * largest `n` among them (sizes the launch).  Grad dtype: fp32 or bf16. */
+ * largest `n` among them (sizes the launch).  Grad dtype: fp32 or bf16.
+ * `grad_scale` (device fp32 [1], or NULL for 1): every gradient is multiplied
+ * by grad_scale[0] before the update (the clip coefficient below). */
 typedef struct ethos_adam_tensor {
   void* param;        /* fp32 or bf16 [n]                                     */
   const void* grad;   /* fp32 or bf16 [n]                                     */
@@ -428,7 +430,23 @@ typedef struct ethos_adam_tensor {
 } ethos_adam_tensor;
 
 int ethos_adamw_step(const ethos_adam_tensor* tensors, int num_tensors, int64_t max_n, float lr, float beta1,
-                     float beta2, float eps, float weight_decay, int64_t step, int* dev_err, void* stream);
+                     float beta2, float eps, float weight_decay, int64_t step, const float* grad_scale, int* dev_err,
+                     void* stream);
+
+/* Global-norm gradient clipping, the reference's `gradient_clipping: 1.0`
+ * (train.py:100, applied by DeepSpeed before its AdamW step) with the rule of
+ * torch.nn.utils.clip_grad_norm_: over every `grad` of `tensors` (the same
+ * DEVICE descriptor array as ethos_adamw_step),
+ *   norm = sqrt(sum of g^2),  coef = min(1, max_norm / (norm + 1e-6)),
+ * written to out fp32 [2] (device) = {norm, coef}; pass &out[1] as
+ * ethos_adamw_step's `grad_scale` to clip inside the update (the gradients
+ * themselves are not modified).  The sum is taken in a fixed order (fp64
+ * partials per block of a fixed grid in `workspace`), so equal gradients give
+ * bit-identical results on every GPU.  `workspace`: 8-byte aligned device
+ * memory of at least ethos_grad_clip_workspace_size() bytes. */
+size_t ethos_grad_clip_workspace_size(void);
+int ethos_grad_clip_coef(const ethos_adam_tensor* tensors, int num_tensors, float max_norm, void* workspace,
+                         size_t workspace_bytes, float* out, int* dev_err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -18,7 +18,7 @@ HEADER = os.path.join(ROOT, "include", "ethos_b200.h")
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|uint64_t|const char\s*\*)\s*(ethos_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|size_t|uint64_t|const char\s*\*)\s*(ethos_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -43,7 +43,7 @@ def test_every_declared_symbol_is_exported(L):
 def test_ctypes_argument_counts_match_header():
     """Every ctypes prototype has as many arguments as the header declares."""
     text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
-    for m in re.finditer(r"^\s*(?:int|size_t|uint64_t|const char\s*\*)\s*(ethos_\w+)\s*\(([^)]*)\)\s*;", text,
+    for m in re.finditer(r"^\s*(?:int|int64_t|size_t|uint64_t|const char\s*\*)\s*(ethos_\w+)\s*\(([^)]*)\)\s*;", text,
                          flags=re.M):
         name, args = m.group(1), m.group(2).strip()
         n = 0 if args in ("", "void") else len(args.split(","))
