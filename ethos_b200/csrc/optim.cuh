@@ -112,41 +112,62 @@ __global__ void k_adamw(const ethos_adam_tensor* __restrict__ tensors, AdamScala
 // does not depend on scheduling, so data-parallel ranks holding the same
 // all-reduced gradients get bit-identical coefficients: a fixed grid of
 // GRAD_CLIP_BLOCKS blocks walks every tensor in table order, each thread
-// taking fixed elements of each and accumulating in fp64; block b writes its
+// taking fixed chunks of each and accumulating in fp64; block b writes its
 // sum to partial[b], and one block adds the partials in a fixed order.
-constexpr int GRAD_CLIP_BLOCKS = 592;
+constexpr int GRAD_CLIP_BLOCKS = 1184;  // 8 per SM of a B200; fixed, so the sum's order is too
 constexpr int GRAD_CLIP_THREADS = 256;
 
+// sum of squares of 8 gradient elements (16 bytes of bf16 or 32 of fp32)
+__device__ __forceinline__ double sq8(const ethos_adam_tensor& td, int64_t c) {
+  float g[8];
+  if (td.grad_bf16) {
+    const uint4 u = *(reinterpret_cast<const uint4*>(td.grad) + c);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      g[2 * k] = f.x;
+      g[2 * k + 1] = f.y;
+    }
+  } else {
+    const float4 a = *(reinterpret_cast<const float4*>(td.grad) + 2 * c);
+    const float4 b = *(reinterpret_cast<const float4*>(td.grad) + 2 * c + 1);
+    g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w; g[4] = b.x; g[5] = b.y; g[6] = b.z; g[7] = b.w;
+  }
+  double s = 0.0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s = fma(static_cast<double>(g[k]), static_cast<double>(g[k]), s);
+  return s;
+}
+
+// Thread t takes the 8-element chunks t, t + T, t + 2T, ... (T = threads of
+// the grid) of every tensor, two chunks' loads in flight at a time; a tensor
+// whose size or address does not allow 16-byte chunks is walked element by
+// element instead.  The assignment depends only on the sizes.
 __global__ void __launch_bounds__(GRAD_CLIP_THREADS) k_grad_sqnorm(const ethos_adam_tensor* __restrict__ tensors,
                                                                    int num_tensors, double* __restrict__ partial) {
   __shared__ double red[GRAD_CLIP_THREADS];
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
-  const int64_t first = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   double acc = 0.0;
   for (int y = 0; y < num_tensors; ++y) {
     const ethos_adam_tensor td = tensors[y];
     const int64_t n = td.n;
-    const bool vec = (n % 4 == 0) && (reinterpret_cast<uintptr_t>(td.grad) & (td.grad_bf16 ? 7u : 15u)) == 0;
-    for (int64_t i = first; i < n; i += stride) {
-      float g[4] = {0.f, 0.f, 0.f, 0.f};
-      if (vec) {
-        if (td.grad_bf16) {
-          const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(td.grad) + i);
-          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-          g[0] = a.x; g[1] = a.y; g[2] = b.x; g[3] = b.y;
-        } else {
-          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(td.grad) + i);
-          g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
-        }
-      } else {
-        const int cnt = static_cast<int>(n - i < 4 ? n - i : 4);
-        for (int u = 0; u < cnt; ++u)
-          g[u] = td.grad_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(td.grad)[i + u])
-                              : static_cast<const float*>(td.grad)[i + u];
+    if (n % 8 == 0 && (reinterpret_cast<uintptr_t>(td.grad) & 15u) == 0) {
+      const int64_t nc = n / 8;
+      int64_t c = tid;
+      for (; c + nt < nc; c += 2 * nt) {
+        const double a = sq8(td, c), b = sq8(td, c + nt);
+        acc += a;
+        acc += b;
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) acc = fma(static_cast<double>(g[u]), static_cast<double>(g[u]), acc);
+      if (c < nc) acc += sq8(td, c);
+    } else {
+      for (int64_t j = tid; j < n; j += nt) {
+        const float g = td.grad_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(td.grad)[j])
+                                     : static_cast<const float*>(td.grad)[j];
+        acc = fma(static_cast<double>(g), static_cast<double>(g), acc);
+      }
     }
   }
   red[threadIdx.x] = acc;
