@@ -62,7 +62,7 @@ EXPORTS = {
                                  _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P, _P]),
     "ethos_backward_workspace_size": (_SZ, [_DIMS]),
     "ethos_layer_backward": (_I, [_DIMS, _I, _F, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                  _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P, _P]),
+                                  _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P, _P]),
     "ethos_router_forward": (_I, [_DIMS, _P, _P, _P, _F, _F, _I, _P, _P, _P, _P, _P, _P, _SZ,
                                   _P, _P]),
     "ethos_expert_backward_workspace_size": (_SZ, [_DIMS]),

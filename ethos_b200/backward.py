@@ -61,8 +61,14 @@ def layer_backward(ctx, gy):
         dist.get_world_size(comm["group"]) > 1
     timing = overlap and comm.get("log") is not None
     events = [torch.cuda.Event(enable_timing=timing), torch.cuda.Event(enable_timing=timing)] if overlap else None
-    bwd = ops.layer_backward_f32 if pw.fp32 else ops.layer_backward
-    g = bwd(gy.reshape(-1, gy.shape[-1]), sv["xin"], pw, sv, ctx.training_bn, eps, stage_events=events)
+    if pw.fp32:
+        g = ops.layer_backward_f32(gy.reshape(-1, gy.shape[-1]), sv["xin"], pw, sv, ctx.training_bn, eps,
+                                   stage_events=events)
+    else:
+        # a bf16 input gets its gradient from the dx GEMM directly in bf16
+        dx_dtype = torch.bfloat16 if ctx.x_dtype == torch.bfloat16 else torch.float32
+        g = ops.layer_backward(gy.reshape(-1, gy.shape[-1]), sv["xin"], pw, sv, ctx.training_bn, eps,
+                               stage_events=events, dx_dtype=dx_dtype)
     if overlap:
         _overlapped_allreduce(layer, g, events)
     params = ctx.params

@@ -418,9 +418,11 @@ __global__ void __launch_bounds__(256, 3) k_expert_dP(const int* __restrict__ of
 //   dS[p][h][t][i] = sum_{r: key_p(r) = i} dg_r              (dense, bf16)
 //   dq^[t, h, :dq/2] = sum_i dS[0][h][t][i] K1[i],  dq^[t, h, dq/2:] = sum_j dS[1][h][t][j] K2[j]
 //   (= sum_r dg_r K1[i_r] and sum_r dg_r K2[j_r]; dS in fp32 here)
-// with i_r = id_r / K, j_r = id_r % K.  dS feeds the dK GEMMs; its buffer is
-// zeroed beforehand and every (h, p, t, i) is written by one lane (duplicate
-// keys of a row are combined with __match_any_sync first).
+// with i_r = id_r / K, j_r = id_r % K.  dS feeds the dK GEMMs; each warp
+// writes its two dS rows whole -- zeros by coalesced 16-byte stores, then,
+// after __syncwarp orders the lanes' stores, each nonzero (h, p, t, i) by one
+// lane (duplicate keys of a row are combined with __match_any_sync first) --
+// so no separate pass zeroes the 268 MB buffer (config 2).  K % 8 == 0.
 template <int TOPK>
 __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ ids, const float* __restrict__ w,
                                                      const float* __restrict__ dw,
@@ -434,6 +436,12 @@ __global__ void __launch_bounds__(256) k_router_bwd(const int32_t* __restrict__ 
   for (int th = gw; th < T * H; th += nw) {
     const int t = th / H, h = th - t * H;
     const int64_t o = static_cast<int64_t>(th) * TOPK;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint4* row = reinterpret_cast<uint4*>(dS + ((static_cast<int64_t>(p) * H + h) * T + t) * K);
+      for (int c = lane; c < K / 8; c += 32) row[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    __syncwarp();
     // a selection whose id lies outside [0, K*K) (k_count_experts reports
     // it) contributes nothing and reads key row 0
     const int id_in = lane < TOPK ? ids[o + lane] : 0;

@@ -870,9 +870,8 @@ int router_bwd_core(const ethos_dims& d, const RouterBwdIO& io, const BwdScratch
   const int cb = 256;
   int st;
   if (cudaMemsetAsync(io.d_keys, 0, sizeof(float) * 2 * K * half, sm) != cudaSuccess) return ETHOS_ERR_CUDA;
-  if (cudaMemsetAsync(s.dS, 0, sizeof(__nv_bfloat16) * static_cast<size_t>(H) * 2 * T * K, sm) != cudaSuccess)
-    return ETHOS_ERR_CUDA;
-  // softmax backward, dq^ and the dense sub-key score gradient dS
+  // softmax backward, dq^ and the dense sub-key score gradient dS (k_router_bwd
+  // writes every row of dS, zeros included)
   const __nv_bfloat16* keys = static_cast<const __nv_bfloat16*>(io.key_cat);
   switch (d.top_k) {
     case 4: st = launch_router_bwd<4>(d, io.ids, io.weights, io.dw, keys, dq, s.dqhat, s.dS, sm, dev); break;
@@ -1288,8 +1287,8 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          const void* w1, const void* wv, const int32_t* ids, const float* weights,
                          const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
                          const float* save_bn, const void* save_qs, const void* htab, const void* gtab,
-                         float* dx, float* d_latents, float* d_w1, float* d_w2, float* d_wq, float* d_bn,
-                         float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
+                         void* dx, int dx_bf16, float* d_latents, float* d_w1, float* d_w2, float* d_wq,
+                         float* d_bn, float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
                          void* const* stage_events, void* stream) {
   int st = check_dims_impl(dims);
   if (st != ETHOS_OK) return st;
@@ -1387,10 +1386,20 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
     io.d_keys = d_keys;
     if ((st = router_bwd_core(d, io, s, dev_err, sm, *dev)) != ETHOS_OK) return st;
   }
-  // (12) dx = du @ W_cat          (W_cat read in place, MN-major)
-  {
+  // (12) dx = du @ W_cat          (W_cat read in place, MN-major), in fp32 or
+  // straight into bf16
+  if (dx_bf16) {
+    EpiStoreBF16 e;
+    e.out = static_cast<__nv_bfloat16*>(dx);
+    e.ldo = D;
+    e.M = T;
+    e.scale = 1.0f;
+    if ((st = gemm(GemmOperand{s.du, LDU, false}, GemmOperand{w_cat, D, true}, T, D, LDU, 1, e, dev_err, sm,
+                   *dev)) != ETHOS_OK)
+      return st;
+  } else {
     EpiStoreF32 e;
-    e.out = dx;
+    e.out = static_cast<float*>(dx);
     e.ldo = D;
     e.M = T;
     e.scale = 1.0f;

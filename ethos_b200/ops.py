@@ -303,10 +303,11 @@ def _numel(shape):
 BWD_STAGE_EXPERTS, BWD_STAGE_END = 0, 1  # ETHOS_BWD_STAGE_* (include/ethos_b200.h)
 
 
-def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
+def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None, dx_dtype=torch.float32):
     """Gradients of the layer (see ethos_layer_backward).  ``dy`` [T, d] bf16
     or fp32; ``saved`` is the dict returned by ``layer_forward(save=True)``.
-    Returns a dict of fp32 tensors: dx, d_latents, d_w1, d_w2, d_wq [H*dq, d],
+    Returns a dict of fp32 tensors (dx in ``dx_dtype``, fp32 or bf16): dx,
+    d_latents, d_w1, d_w2, d_wq [H*dq, d],
     d_bn [3, H*dq] (bias, gamma, beta), d_keys [2, K, dq/2], and the flat fp32
     buffer holding all parameter gradients (``flat``, ``layout``).
     ``stage_events``: optional [experts_done, end] ``torch.cuda.Event`` (or
@@ -338,7 +339,9 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
         off += (n + 63) // 64 * 64
     flat = torch.empty(off, dtype=torch.float32, device=dev)
     g = {name: flat[o:o + _numel(shp)].view(shp) for name, o, shp in layout}
-    g["dx"] = torch.empty((T, d["d_model"]), dtype=torch.float32, device=dev)
+    if dx_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("dx_dtype: torch.float32 or torch.bfloat16")
+    g["dx"] = torch.empty((T, d["d_model"]), dtype=dx_dtype, device=dev)
     g["flat"] = flat
     g["layout"] = layout
     dy = dy.contiguous()
@@ -351,6 +354,7 @@ def layer_backward(dy, x16, pw, saved, bn_training, eps, stage_events=None):
                                  _vp(saved["weights"]), _vp(saved["xp"]), _vp(saved["hacc"]), _vp(saved["dot"]),
                                  _vp(saved["qpre"]), _vp(saved.get("bn_stats")), _vp(saved["qs"]),
                                  _vp(saved.get("htab")), _vp(saved.get("gtab")), _vp(g["dx"]),
+                                 1 if dx_dtype == torch.bfloat16 else 0,
                                  _vp(g["d_latents"]), _vp(g["d_w1"]), _vp(g["d_w2"]), _vp(g["d_wq"]),
                                  _vp(g["d_bn"]), _vp(g["d_keys"]), _vp(ws), ws_bytes, _vp(err),
                                  _events(stage_events), _stream(dev)),

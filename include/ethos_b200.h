@@ -245,8 +245,10 @@ size_t ethos_backward_workspace_size(const ethos_dims* dims);
  *  save_*     the forward's save buffers (all required; save_bn in training)
  *  htab, gtab the forward's save_htab / save_gtab when it filled them (table
  *             path), else NULL: the backward then builds both itself
- * Outputs (fp32, overwritten):
- *  dx        [T, d]
+ * Outputs (fp32 unless stated, overwritten):
+ *  dx        [T, d]         fp32, or bf16 when dx_bf16 != 0 (the dx GEMM
+ *                           then stores bf16 directly; for a bf16 layer
+ *                           input, no separate conversion pass)
  *  d_latents [N, dl]        expert_latents.weight
  *  d_w1      [dh, dl]       generation_network.net.0.weight
  *  d_w2      [2d, dh]       generation_network.net.2.weight
@@ -258,8 +260,8 @@ int ethos_layer_backward(const ethos_dims* dims, int bn_training, float bn_eps, 
                          const void* w1, const void* wv, const int32_t* ids, const float* weights,
                          const float* save_xp, const void* save_hacc, const float* save_dot, const float* save_qpre,
                          const float* save_bn, const void* save_qs, const void* htab, const void* gtab,
-                         float* dx, float* d_latents, float* d_w1, float* d_w2, float* d_wq, float* d_bn,
-                         float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
+                         void* dx, int dx_bf16, float* d_latents, float* d_w1, float* d_w2, float* d_wq,
+                         float* d_bn, float* d_keys, void* workspace, size_t workspace_bytes, int* dev_err,
                          void* const* stage_events, void* stream);
 
 /* Backward stage events: with a non-NULL `stage_events` (ETHOS_BWD_STAGE_COUNT

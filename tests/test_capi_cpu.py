@@ -124,8 +124,8 @@ def test_null_arguments_rejected_without_gpu(L):
     st = L.ethos_layer_forward(ctypes.byref(d), None, None, None, 1e-5, 0.1, 0, None, None, None, None, 0, None, None,
                                None, None, None, None, None, None, None, None, None, None, 0, None, None, None)
     assert st == 1  # ETHOS_ERR_INVALID_ARG
-    st = L.ethos_layer_backward(ctypes.byref(d), 0, 1e-5, None, 0, *([None] * 17), *([None] * 7), None, 0,
-                                None, None, None)
+    st = L.ethos_layer_backward(ctypes.byref(d), 0, 1e-5, None, 0, *([None] * 17), None, 0, *([None] * 6), None,
+                                0, None, None, None)
     assert st == 1
     assert L.ethos_backward_workspace_size(ctypes.byref(d)) > 2 * 512 * 512 * 512 * 2
 

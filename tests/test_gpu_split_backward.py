@@ -159,3 +159,23 @@ def test_router_backward_matches_oracle(cfg, T, training):
             assert g.abs().max().item() <= 1e-6, n  # the batch mean absorbs the bias
             continue
         assert rel_err(g.cpu(), g_ref) <= TOL, (n, rel_err(g.cpu(), g_ref))
+
+
+@pytest.mark.parametrize("cfg,T,training", [(CFG1, 256, True), (CFG2, 1024, False)])
+def test_layer_backward_bf16_dx_is_rounded_fp32_dx(cfg, T, training):
+    """dx straight from the dx GEMM in bf16 (what the module uses for a bf16
+    input) equals the fp32 dx rounded to bf16, bit for bit: the same GEMM and
+    accumulation order, only the epilogue's store differs; the parameter
+    gradients do not depend on dx's dtype (equal to fp32 rounding: the
+    split-K weight-gradient GEMMs add their partials with fp32 atomics, whose
+    order varies from run to run)."""
+    _, _, pw, eps, mom, x, gy = _setup(cfg, T, training)
+    x16, gy16 = x.to("cuda", torch.bfloat16), gy.to("cuda", torch.bfloat16)
+    sv = ops.layer_forward(x16, pw, training, eps, mom, save=True)
+    g32 = ops.layer_backward(gy16, x16, pw, sv, training, eps)
+    g16 = ops.layer_backward(gy16, x16, pw, sv, training, eps, dx_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    ops.check_device_error("cuda")
+    assert g16["dx"].dtype == torch.bfloat16
+    assert torch.equal(g16["dx"], g32["dx"].to(torch.bfloat16))
+    assert rel_err(g16["flat"], g32["flat"]) <= 1e-5
