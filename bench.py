@@ -19,8 +19,8 @@ the NCCL all-reduce of every gradient overlapped with the backward (N > 1) and
 a fused AdamW update -- timed at the same N, with the all-reduce time left
 exposed and a cross-rank checksum of the reduced gradients and updated
 parameters (the run exits non-zero if the ranks disagree) -- and short
-``router`` (config 3, the routing microbenchmark) and ``stack`` (config 4's
-12 expert layers) blocks.
+``router`` (config 3, the routing microbenchmark) and ``decoder`` (config 4:
+the whole 12-layer decoder forward with the ETHOS expert layers) blocks.
 
 ``--impl reference`` times the reference path's CPU implementation on the
 host cores (the vectorised fp32 restatement in oracle/ethos_oracle.py of
@@ -554,46 +554,50 @@ def fp32_block(args, rank, world, local, dev, steps=None):
                 l2="flushed between timed steps (256 MiB write)", steps=steps)
 
 
-def stack_block(args, rank, world, local, dev, steps=None, sampler=True):
-    """Config 4, the expert layers of the decoder: 12 ETHOS expert layers
-    (config-2 dimensions, each with its own seeded parameters) on one residual
-    stream, h = h + layer(rms_norm(h)), over the embeddings of 16 384 token ids
-    drawn Zipf(1.1) over a 100 277-entry vocabulary.  The decoder's attention,
-    embedding and output head are the reference's own model code, which is not
-    part of this repository, so they are not timed; the report gives the
-    expert layers' share of the forward.  Every rank must call it."""
+def decoder_block(args, rank, world, local, dev, steps=None, sampler=True):
+    """Config 4: the whole ETHOS decoder forward (ethos_b200.decoder.EthosDecoder,
+    the reference CompressedMoEModel's architecture, model.py:345-395): 12
+    layers of RMSNorm + multi-head latent attention (16 heads, latent KV 256,
+    rotary) + RMSNorm + ETHOS expert layer (config-2 dimensions), the final
+    RMSNorm and the tied output head over a 100 277-entry vocabulary, on
+    batch 8 x sequence 2048 token ids drawn Zipf(1.1), every parameter seeded
+    by name, bf16.  Only the expert layers run on this repository's kernels;
+    attention is torch's scaled_dot_product_attention (cuDNN's sm100 kernel on
+    a B200; the reference calls flash_attn, whose sm80 kernel is slower here).
+    A second,
+    untimed pass records CUDA events around every expert layer for their share
+    of the forward.  Every rank must call it."""
     import numpy as np
     import torch.distributed as dist
-    import torch.nn.functional as F
-    from ethos_b200 import EthosConfig, EthosExpertLayer, ops
-    from ethos_b200.init import seeded_init_
+    from ethos_b200 import ops
+    from ethos_b200.decoder import DecoderConfig, EthosDecoder
+    from ethos_b200.init import seeded_state_dict
     steps = steps or args.steps
-    n_layers, vocab, T = 12, 100277, args.tokens
+    seq = 2048
+    T = args.tokens
+    if T % seq != 0:
+        raise SystemExit("--tokens must be a multiple of the sequence length 2048 for the decoder")
+    cfg = DecoderConfig(num_layers=12, num_dense_layers=0, vocab_size=100277, **CFG2)
+    model = EthosDecoder(cfg)
+    sd = seeded_state_dict(model, seed=0)
+    sd["tok_embeddings.weight"] = sd["output.weight"]
+    model.load_state_dict(sd)
+    del sd
+    model = model.to(device=dev, dtype=torch.bfloat16).eval()
     rng = np.random.default_rng(1000 + rank)
     ids = rng.zipf(1.1, size=4 * T)
-    ids = torch.from_numpy(ids[ids <= vocab][:T] - 1).to(dev)
+    ids = torch.from_numpy(ids[ids <= cfg.vocab_size][:T] - 1).to(dev).view(T // seq, seq)
     assert ids.numel() == T
-    g = torch.Generator().manual_seed(7)
-    emb = (torch.randn((vocab, CFG2["d_model"]), generator=g) / CFG2["d_model"] ** 0.5).to(dev, torch.bfloat16)
-    layers = []
-    for i in range(n_layers):
-        layer = EthosExpertLayer(EthosConfig(**CFG2))
-        seeded_init_(layer, seed=100 + i)
-        layers.append(layer.to(device=dev, dtype=torch.bfloat16).eval())
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def forward():
-        h = emb[ids].view(1, T, -1)
-        for layer in layers:
-            h = h + layer(F.rms_norm(h, (h.shape[-1],)))
-        return h
-
     with torch.no_grad():
         for _ in range(max(args.warmup, 3)):
-            forward()
+            model(ids)
         torch.cuda.synchronize()
         ops.check_device_error(dev)
+        attn_impl = "flash_attn" if model.layers[0].self_attn.use_flash_attn else \
+            "torch scaled_dot_product_attention"
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         n_launch = launches()
         clk = ClockSampler(local) if sampler else None
@@ -605,7 +609,7 @@ def stack_block(args, rank, world, local, dev, steps=None, sampler=True):
         for s_, e_ in ev:
             flush.zero_()
             s_.record(stream)
-            forward()
+            model(ids)
             e_.record(stream)
         torch.cuda.synchronize()
         n_launch = launches() - n_launch
@@ -613,36 +617,62 @@ def stack_block(args, rank, world, local, dev, steps=None, sampler=True):
             dist.barrier()
         clocks = clk.stop() if clk else None
         ops.check_device_error(dev)
+        # untimed: events around every expert layer
+        marks = []
+        hooks = []
+        for layer in model.expert_layers():
+            hooks.append(layer.register_forward_pre_hook(
+                lambda m, a: marks.append(torch.cuda.Event(enable_timing=True)) or marks[-1].record(stream)))
+            hooks.append(layer.register_forward_hook(
+                lambda m, a, o: marks.append(torch.cuda.Event(enable_timing=True)) or marks[-1].record(stream)))
+        totals = []
+        for _ in range(3):
+            marks.clear()
+            flush.zero_()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            model(ids)
+            e0.record(stream)
+            torch.cuda.synchronize()
+            expert = sum(marks[2 * i].elapsed_time(marks[2 * i + 1]) for i in range(len(marks) // 2))
+            totals.append((expert, s0.elapsed_time(e0)))
+        for h in hooks:
+            h.remove()
     ms = sum(s_.elapsed_time(e_) for s_, e_ in ev) / len(ev)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
-    out = dict(metric="decoder expert-layer stack tokens/s (12 x ETHOS expert layer, 262K experts, k=16x8)",
-               value=T * world / (ms / 1e3), unit="tokens/s", ms_per_step=ms, ms_per_layer=ms / n_layers,
-               steps=steps, data="synthetic (Zipf(1.1) token ids)",
-               workload="config 4, expert layers only: embedding lookup, then 12 x (RMSNorm, ETHOS expert layer, "
-                        "residual add); MLA attention and the output head are not included",
-               tokens_per_gpu=T, layers=n_layers, vocab=vocab, parallelism=f"dp{world}",
-               l2="flushed between timed steps (256 MiB write)", gpu_launches=n_launch)
+    expert_ms = sum(a for a, _ in totals) / len(totals)
+    whole_ms = sum(b for _, b in totals) / len(totals)
+    out = dict(metric="ETHOS decoder forward tokens/s (12 layers: MLA attention + ETHOS expert layer, "
+                      "262K experts, k=16x8; vocab 100277)",
+               value=T * world / (ms / 1e3), unit="tokens/s", ms_per_step=ms, steps=steps,
+               data="synthetic (Zipf(1.1) token ids), random init",
+               workload="config 4: embedding, 12 x (RMSNorm, MLA attention 16 heads / latent KV 256 / rotary, "
+                        "RMSNorm, ETHOS expert layer), RMSNorm, tied output head; batch 8 x seq 2048",
+               attention=attn_impl, expert_layers_ms=expert_ms, expert_share=expert_ms / whole_ms,
+               tokens_per_gpu=T, batch=T // seq, seq_len=seq, layers=cfg.num_layers, vocab=cfg.vocab_size,
+               parallelism=f"dp{world}", l2="flushed between timed steps (256 MiB write)", gpu_launches=n_launch)
     if clocks is not None:
         out["clocks"] = clocks
-    del layers
+    del model
     return out
 
 
-def run_stack(args, rank, world, local, dev):
-    """--mode stack: config 4's expert layers alone, as their own JSON line."""
-    r = stack_block(args, rank, world, local, dev)
+def run_decoder(args, rank, world, local, dev):
+    """--mode decoder: config 4, the whole decoder forward, as its own JSON line."""
+    r = decoder_block(args, rank, world, local, dev)
     if rank == 0:
         line = dict(metric=r["metric"], value=r["value"], unit=r["unit"], n_gpus=world, steps=args.steps,
-                    warmup=args.warmup, ms_per_step=r["ms_per_step"], ms_per_layer=r["ms_per_layer"],
-                    higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16", data=r["data"],
-                    config=dict(workload=r["workload"], tokens_per_gpu=r["tokens_per_gpu"], layers=r["layers"],
-                                vocab=r["vocab"], parallelism=r["parallelism"], l2=r["l2"]),
+                    warmup=args.warmup, ms_per_step=r["ms_per_step"], higher_is_better=True, scaling="weak",
+                    vs_baseline=None, dtype="bf16", data=r["data"],
+                    config=dict(workload=r["workload"], tokens_per_gpu=r["tokens_per_gpu"], batch=r["batch"],
+                                seq_len=r["seq_len"], layers=r["layers"], vocab=r["vocab"],
+                                parallelism=r["parallelism"], l2=r["l2"], attention=r["attention"]),
+                    expert_layers_ms=r["expert_layers_ms"], expert_share=r["expert_share"],
                     gpu_launches=r["gpu_launches"], clocks=r.get("clocks"))
         print(json.dumps(line), flush=True)
-
 
 def main():
     ap = argparse.ArgumentParser()
@@ -655,15 +685,16 @@ def main():
     ap.add_argument("--no-train", action="store_true", help="leave the training block out of the forward line")
     ap.add_argument("--train-steps", type=int, default=20, help="timed training steps in the train block")
     ap.add_argument("--no-extra", action="store_true",
-                    help="leave the config-3 router and config-4 stack blocks out of the forward line")
+                    help="leave the config-3 router and config-4 decoder blocks out of the forward line")
     ap.add_argument("--ref-seconds", type=float, default=3.0,
                     help="CPU seconds per reference-arm step (a bounded sample of the workload)")
     ap.add_argument("--no-numa-bind", action="store_true",
                     help="with several ranks, leave each rank's CPU affinity alone instead of binding it to its "
                          "GPU's NUMA node (pinned staging buffers then land wherever the process first runs)")
-    ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "stack"],
+    ap.add_argument("--mode", default="forward", choices=["forward", "train", "router", "decoder", "stack"],
                     help="forward: config 2 (headline, with the config-5 train block); train: config 5 alone; "
-                         "router: config 3 routing microbenchmark; stack: config 4's 12 expert layers")
+                         "router: config 3 routing microbenchmark; decoder (or stack): config 4, the whole "
+                         "decoder forward")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -692,8 +723,9 @@ def main():
 
     ok = True
     try:
-        if args.mode in ("train", "router", "stack"):
-            {"train": run_train, "router": run_router, "stack": run_stack}[args.mode](args, rank, world, local, dev)
+        if args.mode in ("train", "router", "decoder", "stack"):
+            {"train": run_train, "router": run_router, "decoder": run_decoder,
+             "stack": run_decoder}[args.mode](args, rank, world, local, dev)
         else:
             ok = run_forward(args, rank, world, local, dev)
     finally:
@@ -891,7 +923,7 @@ def run_forward(args, rank, world, local, dev):
     if not args.no_extra and args.tokens == TOKENS:
         torch.cuda.empty_cache()
         extra["router"] = router_block(args, rank, world, local, dev, steps=20, sampler=False)
-        extra["stack"] = stack_block(args, rank, world, local, dev, steps=5, sampler=False)
+        extra["decoder"] = decoder_block(args, rank, world, local, dev, steps=5, sampler=False)
         torch.cuda.empty_cache()
         extra["fp32"] = fp32_block(args, rank, world, local, dev, steps=5)
 

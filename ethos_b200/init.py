@@ -6,7 +6,8 @@ Convention (the benchmark configs say "N(0, 1/sqrt(fan_in))"):
   well as the embedding tables (latent codes, sub-keys) ``[rows, dim]`` -- is
   drawn N(0, 1) and scaled by ``1/sqrt(cols)``;
 * biases are 0; BatchNorm gamma = 1, beta = 0, running mean 0, running var 1,
-  ``num_batches_tracked`` 0;
+  ``num_batches_tracked`` 0; other 1-D weights (the decoder's RMSNorm gains)
+  are 1;
 * inputs ``x`` are N(0, 1).
 
 Each tensor draws from its own ``torch.Generator`` seeded from ``seed`` and the
@@ -37,6 +38,8 @@ def _value_for(name, like, seed):
         return torch.zeros(shape)
     if name.endswith(".bias"):
         return torch.zeros(shape)
+    if len(shape) == 1 and name.endswith("weight"):
+        return torch.ones(shape)
     if len(shape) != 2:
         raise ValueError(f"unexpected parameter {name} with shape {shape}")
     g = tensor_generator(seed, name)

@@ -16,7 +16,9 @@ The "model" case builds the reference's whole decoder (``CompressedMoEModel``,
 ``model.py:368-395``: 1 dense and 2 expert layers at a small size), runs its
 forward on CPU and records what each expert layer received and returned,
 with its routing; ``tests/test_reference_model.py`` replays those inputs
-through the oracle and through the GPU layers.
+through the oracle and through the GPU layers.  The "decoder" case records
+the same decoder's final logits with every parameter seeded by name, for
+``tests/test_decoder.py``.
 
 Small cases store every tensor.  The config-1 case (d_model 512, 4096
 experts, 256 tokens) stores the forward outputs in full and, for a 32-token
@@ -70,6 +72,14 @@ MODEL_CASE = dict(vocab_size=1024, d_model=512, num_layers=3, num_heads=4, num_d
                   num_routing_heads=8, d_query=512, d_ffn_intermediate=512, max_seq_len=64, rms_norm_eps=1e-6,
                   rope_theta=10000.0, use_triton=False)
 MODEL_BATCH, MODEL_SEQ = 2, 32
+
+# The reference's whole decoder again, for an end-to-end check of
+# ethos_b200.decoder.EthosDecoder: every parameter seeded by name (seed 21;
+# the tied tok_embeddings / output weight takes output.weight's values), fp32
+# throughout (no bf16 rounding: the GPU side runs the fp32 path), and the
+# final logits recorded.
+DECODER_CASE = dict(MODEL_CASE, vocab_size=512, num_layers=2, num_dense_layers=1, num_moe_layers=1)
+DECODER_BATCH, DECODER_SEQ, DECODER_SEED = 2, 48, 21
 
 
 def checksum(sd):
@@ -193,11 +203,30 @@ def run_model_case(model_mod):
     return dict(model_cfg=dict(MODEL_CASE), batch=MODEL_BATCH, seq=MODEL_SEQ, input_ids=input_ids, layers=layers)
 
 
+def run_decoder_case(model_mod):
+    """Logits of the reference decoder (eval mode, CPU, fp32) with every
+    parameter seeded by name."""
+    from ethos_b200.init import seeded_state_dict
+    cfg = _Cfg(**DECODER_CASE)
+    model = model_mod.CompressedMoEModel(cfg).eval()
+    sd = seeded_state_dict(model, seed=DECODER_SEED)
+    sd["tok_embeddings.weight"] = sd["output.weight"]
+    model.load_state_dict(sd)
+    g = torch.Generator().manual_seed(9)
+    input_ids = torch.randint(0, cfg.vocab_size, (DECODER_BATCH, DECODER_SEQ), generator=g)
+    t0 = time.time()
+    with torch.no_grad():
+        logits = model(input_ids)
+    print(f"[decoder] forward {time.time() - t0:.1f}s, logits {tuple(logits.shape)}")
+    keys = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    return dict(model_cfg=dict(DECODER_CASE), seed=DECODER_SEED, input_ids=input_ids, logits=logits, keys=keys)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ETHOS_REFERENCE"),
                     help="reference checkout holding model.py (default: $ETHOS_REFERENCE)")
-    ap.add_argument("--cases", default=",".join(list(CASES) + ["model"]))
+    ap.add_argument("--cases", default=",".join(list(CASES) + ["model", "decoder"]))
     args = ap.parse_args()
     if not args.reference:
         ap.error("name the reference checkout with --reference or ETHOS_REFERENCE")
@@ -209,7 +238,12 @@ def main():
     import model as model_mod  # the reference's model.py
     torch.set_num_threads(os.cpu_count() or 1)
     for name in args.cases.split(","):
-        rec = run_model_case(model_mod) if name == "model" else run_case(model_mod, name, CASES[name])
+        if name == "model":
+            rec = run_model_case(model_mod)
+        elif name == "decoder":
+            rec = run_decoder_case(model_mod)
+        else:
+            rec = run_case(model_mod, name, CASES[name])
         path = os.path.join(HERE, f"golden_{name}.pt")
         torch.save(rec, path)
         print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")
