@@ -146,3 +146,31 @@ def test_clipping_bf16_master_weights_and_determinism():
     assert [m for m, _ in norms] == [m for m, _ in norms2]
     for a, b in zip(ours, again):
         assert torch.equal(a.detach(), b.detach())
+
+
+@pytest.mark.gpu
+def test_clipping_across_param_groups():
+    """Two parameter groups with their own lr and weight decay: one clip norm
+    over both (as clip_grad_norm_ over every parameter), each group updated
+    with its own hyper-parameters from its slice of the descriptor table."""
+    from ethos_b200.optim import FusedAdamW
+    base = _params(11, torch.float32)
+    ours = [torch.nn.Parameter(t.clone().cuda()) for t in base]
+    ref = [torch.nn.Parameter(t.clone().cuda()) for t in base]
+    groups = lambda ps: [dict(params=ps[:2], lr=3e-3, weight_decay=0.0), dict(params=ps[2:], lr=1e-2,
+                                                                            weight_decay=0.1)]
+    o1 = FusedAdamW(groups(ours), max_grad_norm=0.5)
+    o2 = torch.optim.AdamW(groups(ref), foreach=False)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    for _ in range(3):
+        for a, b in zip(ours, ref):
+            gr = torch.randn(a.shape, device="cuda", generator=g)
+            a.grad = gr.clone()
+            b.grad = gr.clone()
+        o1.step()
+        theirs = torch.nn.utils.clip_grad_norm_(ref, 0.5).item()
+        o2.step()
+        assert abs(o1.last_grad_norm.item() - theirs) <= 2e-6 * theirs
+    torch.cuda.synchronize()
+    for a, b in zip(ours, ref):
+        torch.testing.assert_close(a.detach(), b.detach(), rtol=2e-6, atol=2e-7)
