@@ -16,6 +16,9 @@
 // TMEM accumulators, so the epilogue of tile i overlaps the main loop of tile
 // i+1.  Split-K: work unit u covers tile u % tiles and K blocks of slice
 // u / tiles; split-K epilogues reduce into fp32 with vector atomics.
+// Epilogues store through the LSU (per-row or warp-transposed rows), or, with
+// Epi::kTmaStore (the expert-table GELU epilogues), stage each warp's 32-row
+// block in shared memory and write it with TMA stores (tensor maps tmC, tmD).
 #pragma once
 
 #include <cuda_fp16.h>
@@ -72,8 +75,9 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 
 // ------------------------------------------------------------- epilogues --
 // Per-warp context of an epilogue call: the warp's 32 output rows start at
-// row0 (nrows of them are inside the matrix) and `stg` is its 2 KB staging
-// buffer.  All 32 lanes call the functor together.
+// row0 (nrows of them are inside the matrix) and `stg` is its staging buffer
+// (2 KB, or the 4 KB block of each output of a TMA-store epilogue).  All 32
+// lanes call the functor together.
 struct EpiCtx {
   uint8_t* stg;
   int row0;
