@@ -69,12 +69,6 @@ class RMSNorm(nn.Module):
         return self.weight * F.rms_norm(x, (x.shape[-1],), None, self.eps)
 
 
-def _rotate(t):
-    """[a, b] -> [-b, a] over the last dimension's halves."""
-    a, b = t.chunk(2, dim=-1)
-    return torch.cat((-b, a), dim=-1)
-
-
 class LatentAttention(nn.Module):
     """Multi-head latent attention with the reference's projections and
     rotary embedding (see the module docstring)."""
@@ -100,14 +94,32 @@ class LatentAttention(nn.Module):
         inv = 1.0 / (config.rope_theta ** (torch.arange(0, self.rope, 2, dtype=torch.float32) / self.rope))
         self.register_buffer("inv_freq", inv, persistent=False)
         self.use_flash_attn = False  # True: flash_attn's kernel (when it runs here) instead of torch's
+        self._tables = {}
 
     def _cos_sin(self, S, dtype, device):
-        # angles in fp32 from fp32 positions, then rounded to the activations'
-        # dtype, as the reference's cached tables are
-        pos = torch.arange(S, device=device, dtype=torch.float32)
-        ang = torch.outer(pos, self.inv_freq.to(device))
-        ang = torch.cat((ang, ang), dim=-1)
-        return ang.cos().to(dtype), ang.sin().to(dtype)
+        """cos and sin of the first half of the rotary angles, [S, 1, rope/2]
+        (the second half repeats them), kept per (length, dtype, device)."""
+        key = (S, dtype, str(device))
+        hit = self._tables.get(key)
+        if hit is None:
+            # angles in fp32 from fp32 positions, then rounded to the
+            # activations' dtype, as the reference's cached tables are
+            pos = torch.arange(S, device=device, dtype=torch.float32)
+            ang = torch.outer(pos, self.inv_freq.to(device))
+            hit = (ang.cos().to(dtype).view(S, 1, -1), ang.sin().to(dtype).view(S, 1, -1))
+            self._tables = {key: hit}
+        return hit
+
+    def _rotary_into(self, out, t, cos, sin):
+        """out <- t cos + rotate(t) sin, for t = [a, b] halves:
+        out = [a cos - b sin, b cos + a sin], written into the view `out`."""
+        r2 = self.rope // 2
+        a, b = t[..., :r2], t[..., r2:]
+        lo, hi = out[..., :r2], out[..., r2:]
+        torch.mul(a, cos, out=lo)
+        lo.addcmul_(b, sin, value=-1.0)
+        torch.mul(b, cos, out=hi)
+        hi.addcmul_(a, sin)
 
     def _core(self, q, k, v):
         """Causal attention on [B, S, H, dim] tensors -> [B, S, H*v_dim]."""
@@ -133,14 +145,25 @@ class LatentAttention(nn.Module):
         latent, k_rot = ckv.split([self.kv_rank, self.rope], dim=-1)
         kv = self.kv_b_proj(self.kv_a_layernorm(latent)).view(B, S, H, self.nope + self.v_dim)
         k_nope, v = kv.split([self.nope, self.v_dim], dim=-1)
-        cos, sin = self._cos_sin(S, v.dtype, x.device)
-        cos, sin = cos.view(S, 1, -1), sin.view(S, 1, -1)  # over [.., S, H, rope]
-        q_rot = q_rot * cos + _rotate(q_rot) * sin
-        k_rot = k_rot.unsqueeze(2)  # one rotary key per token, shared by the heads
-        k_rot = k_rot * cos + _rotate(k_rot) * sin
-        q = torch.cat((q_nope, q_rot), dim=-1)
-        k = torch.cat((k_nope, k_rot.expand(B, S, H, self.rope)), dim=-1)
-        return self.o_proj(self._core(q, k, v))
+        cos, sin = self._cos_sin(S, v.dtype, x.device)  # [S, 1, rope/2], over [.., S, H, rope/2]
+        if torch.is_grad_enabled():
+            # the same values by differentiable ops (out= writes record no graph)
+            def rot(t):
+                a, b = t[..., :self.rope // 2], t[..., self.rope // 2:]
+                return torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
+            qf = torch.cat((q_nope, rot(q_rot)), dim=-1)
+            kf = torch.cat((k_nope, rot(k_rot.unsqueeze(2)).expand(B, S, H, self.rope)), dim=-1)
+            return self.o_proj(self._core(qf, kf, v))
+        # inference: queries and keys assembled in place, [B, S, H, nope | rope]
+        qf = torch.empty((B, S, H, self.q_dim), dtype=q.dtype, device=q.device)
+        qf[..., :self.nope].copy_(q_nope)
+        self._rotary_into(qf[..., self.nope:], q_rot, cos, sin)
+        kr = torch.empty((B, S, 1, self.rope), dtype=k_rot.dtype, device=k_rot.device)
+        self._rotary_into(kr, k_rot.unsqueeze(2), cos, sin)  # one rotary key per token, shared by the heads
+        kf = torch.empty((B, S, H, self.q_dim), dtype=kv.dtype, device=kv.device)
+        kf[..., :self.nope].copy_(k_nope)
+        kf[..., self.nope:].copy_(kr.expand(B, S, H, self.rope))
+        return self.o_proj(self._core(qf, kf, v))
 
 
 class SwiGLU(nn.Module):

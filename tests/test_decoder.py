@@ -112,3 +112,21 @@ def test_decoder_matches_reference_logits(dtype, bound):
     err = rel_err(logits.float().cpu(), rec["logits"])
     print(f"decoder logits, {dtype}: relative error {err:.2e}")
     assert err <= bound
+
+
+def test_attention_same_with_and_without_autograd():
+    """The latent attention's in-place inference path and its differentiable
+    path compute the same values, and the latter back-propagates."""
+    from ethos_b200.decoder import LatentAttention
+    rec = load_golden("decoder")
+    cfg = DecoderConfig(**{k: v for k, v in rec["model_cfg"].items() if k not in ("num_moe_layers", "use_triton")})
+    att = LatentAttention(cfg)
+    att.load_state_dict(seeded_state_dict(att, seed=4))
+    x = torch.randn(2, 24, cfg.d_model, generator=torch.Generator().manual_seed(6))
+    with torch.no_grad():
+        inf = att(x)
+    xg = x.clone().requires_grad_(True)
+    trn = att(xg)
+    trn.square().sum().backward()
+    assert torch.allclose(inf, trn.detach(), rtol=1e-6, atol=1e-6)
+    assert xg.grad is not None and torch.isfinite(xg.grad).all()
